@@ -1,0 +1,499 @@
+"""Benchmark of the sm_100a attention / KV-cache path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (`value`): decode-attention HBM GB/s on config 3 -- 64 sequences,
+32 query / 8 kv heads, head_dim 128, page 16, context U[1024, 8192] (seed 2),
+one fused append + paged GQA decode per step, inputs resident in HBM (the
+1.27 GB cache is larger than L2, so no flush is needed).  Algorithmic bytes
+per step are counted from the drawn lengths (doe_b200/workloads.py).
+Secondary numbers in the same line: config 4 (int8 KV, 32 long sequences),
+its 512-token chunk quantise-append, and config 1 (f32 decode).
+
+N > 1 (torchrun, one rank per GPU): every rank runs its own copy of the
+workload (sequence-sharded decode needs no collective); NCCL carries only the
+barrier and the max-over-ranks of the device times.  `scaling` is "weak".
+
+`e2e` is the same metric through the backend C ABI (doe_cuda_dispatch) with
+host buffers: each step writes Q / new K,V / lengths from pinned host memory
+and reads the f32 output back.  `cpu_baseline` and `--impl reference` time
+the C restatement of the reference's CPU path (oracle/, OpenMP, all host
+cores) on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "source": "measured"}
+    return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS,
+            "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def profiled_traffic() -> dict:
+    p = ROOT / "profiles" / "traffic.json"
+    return json.loads(p.read_text()) if p.exists() else {}
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = Path(f"/tmp/doe_bench_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        self.path.unlink(missing_ok=True)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+def dist_setup():
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    import torch
+
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(world, vals: list[float]) -> list[float]:
+    import torch
+
+    if world == 1:
+        return vals
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def time_steps(step, steps: int, warmup: int, world: int):
+    """Device time of `steps` calls: total (ms) and per-call event times (ms)."""
+    import torch
+
+    for _ in range(warmup):
+        step()
+    barrier(world)
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    per = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    ev0.record(stream)
+    for a, b in per:
+        a.record(stream)
+        step()
+        b.record(stream)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    total = ev0.elapsed_time(ev1)
+    each = [a.elapsed_time(b) for a, b in per]
+    barrier(world)
+    return total, each
+
+
+# ---------------------------------------------------------------------------
+def build_paged(w, fill_seed):
+    import torch
+
+    from doe_b200 import workloads
+    from doe_b200.kv import PagedKVCache
+
+    cache = PagedKVCache(num_pages=w.num_pages, page_size=w.page_size, num_kv_heads=w.num_kv_heads,
+                         head_dim=w.head_dim, block_table=w.block_table, kv_dtype=w.kv_dtype)
+    workloads.fill_pools(cache, fill_seed)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    dev = dict(q=t(w.q), lens=t(w.seq_lens), nk=t(w.new_k), nv=t(w.new_v))
+    dev["out"] = torch.empty((w.num_seqs, w.num_heads, w.head_dim), dtype=torch.float32, device="cuda")
+    dev["status"] = torch.zeros(1, dtype=torch.int32, device="cuda")
+    return cache, dev
+
+
+def paged_step_fn(w, cache, dev):
+    from doe_b200 import ops
+
+    def step():
+        ops.paged_decode(cache, dev["q"], dev["lens"], w.scale, new_k=dev["nk"], new_v=dev["nv"],
+                         out=dev["out"], status=dev["status"])
+    return step
+
+
+def measure_paged(w, fill_seed, steps, warmup, world, pk):
+    cache, dev = build_paged(w, fill_seed)
+    step = paged_step_fn(w, cache, dev)
+    total, each = time_steps(step, steps, warmup, world)
+    total, kern = max_over_ranks(world, [total, float(np.mean(each))])
+    assert int(dev["status"].item()) == 0, f"device status {int(dev['status'].item()):#x}"
+    sb = w.step_bytes()
+    res = {
+        "ms_per_step": total / steps,
+        "gbs": world * sb["total"] * steps / (total / 1e3) / 1e9,
+        "tokens_per_s": world * w.tokens_per_step() * steps / (total / 1e3),
+        "kernel_ms": kern,
+        "kernel_gbs": sb["total"] / (kern / 1e3) / 1e9,
+        "bytes_per_step": sb,
+    }
+    res["frac"] = res["kernel_gbs"] / pk["hbm_gbs"]
+    return res, cache, dev
+
+
+def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512):
+    import torch
+
+    from doe_b200 import ops
+
+    g = np.random.default_rng(w.seed + 100)
+    nk = g.standard_normal((w.num_seqs, chunk, w.num_kv_heads, w.head_dim), dtype=np.float32).astype(np.float16)
+    nv = g.standard_normal((w.num_seqs, chunk, w.num_kv_heads, w.head_dim), dtype=np.float32).astype(np.float16)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    nk, nv = t(nk), t(nv)
+    pos = t((w.ctx + 1).astype(np.int32))  # after the decode token
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def step():
+        ops.paged_append(cache, nk, nv, pos, status=status)
+    total, each = time_steps(step, steps, warmup, world)
+    total, = max_over_ranks(world, [total])
+    assert int(status.item()) == 0
+    rows = w.num_seqs * chunk * w.num_kv_heads
+    rd = 2 * rows * w.head_dim * 2 + w.num_seqs * 4
+    wr = 2 * rows * (w.head_dim + 2)
+    gbs = world * (rd + wr) * steps / (total / 1e3) / 1e9
+    return {"ms_per_step": total / steps, "gbs": gbs, "bytes_per_step": rd + wr,
+            "frac": gbs / world / pk["hbm_gbs"]}
+
+
+def measure_f32(steps, warmup, world, pk):
+    import torch
+
+    from doe_b200 import ops, workloads
+
+    d = workloads.decode_f32()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    q, k, v = t(d.q), t(d.k), t(d.v)
+    out = torch.empty_like(q)
+    # flush L2 between iterations: the 2 MB problem would otherwise sit in L2
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    times = []
+    for i in range(warmup + steps):
+        flush.fill_(i & 0xff)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.attention_decode_f32(q, k, v, d.scale, out=out)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= warmup:
+            times.append(a.elapsed_time(b))
+    ms, = max_over_ranks(world, [float(np.mean(times))])
+    return {"us_per_step": ms * 1e3, "gbs": world * d.bytes_per_step / (ms / 1e3) / 1e9,
+            "bytes_per_step": d.bytes_per_step, "l2": "flushed (256 MB write) between steps"}
+
+
+def measure_e2e(w, cache, steps, warmup, world):
+    """Same decode step through doe_cuda_dispatch with host buffers."""
+    import ctypes as C
+
+    import torch
+
+    from doe_b200.backend import Bind, CudaBackend
+
+    be = CudaBackend(torch.cuda.current_device())
+    # cache state lives on the device: upload the pools once (not timed)
+    chunk = 64 << 20
+    for h, pool in ((2, cache.k_pool), (3, cache.v_pool)):
+        host = pool.cpu().numpy().view(np.uint8).reshape(-1)
+        be.ensure_buffer(h, host.nbytes)
+        for o in range(0, host.nbytes, chunk):
+            be.execute_buffer_write_bytes(h, o, host[o:o + chunk])
+    be.execute_buffer_write_bytes(4, 0, w.block_table)
+    uni = np.array([w.num_seqs, w.num_heads, w.num_kv_heads, w.head_dim, w.page_size, w.num_pages,
+                    w.block_table.shape[1], 0, np.float32(w.scale).view(np.uint32), 0], np.uint32)
+    be.execute_buffer_write_bytes(1, 0, uni)
+    be.flush_queue()
+    # pinned host inputs / output
+    pin = lambda a: torch.from_numpy(np.ascontiguousarray(a)).pin_memory()
+    hq, hl, hk, hv = pin(w.q.view(np.uint16)), pin(w.seq_lens), pin(w.new_k.view(np.uint16)), pin(w.new_v.view(np.uint16))
+    hout = torch.empty((w.num_seqs, w.num_heads, w.head_dim), dtype=torch.float32).pin_memory()
+    out_bytes = hout.numel() * 4
+    binds = [Bind(0, 1, size=40), Bind(1, 10), Bind(2, 2), Bind(3, 3), Bind(4, 4), Bind(5, 11),
+             Bind(6, 12, size=out_bytes), Bind(7, 13), Bind(8, 14)]
+    h2d = hq.numel() * 2 + hl.numel() * 4 + hk.numel() * 2 + hv.numel() * 2
+
+    def step():
+        be.write_ptr(10, 0, hq.data_ptr(), hq.numel() * 2)
+        be.write_ptr(11, 0, hl.data_ptr(), hl.numel() * 4)
+        be.write_ptr(13, 0, hk.data_ptr(), hk.numel() * 2)
+        be.write_ptr(14, 0, hv.data_ptr(), hv.numel() * 2)
+        be.execute_kernel_dispatch("attention_paged_decode", binds)
+        be.read_into(12, 0, hout.data_ptr(), out_bytes)
+
+    for _ in range(warmup):
+        step()
+    be.flush_queue()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    be.flush_queue()
+    elapsed = time.perf_counter() - t0
+    elapsed, = max_over_ranks(world, [elapsed])
+    # the e2e output must equal the operator path's output
+    ok = bool(np.isfinite(hout.numpy()).all())
+    be.close()
+    sb = w.step_bytes()["total"]
+    return {"value": world * sb * steps / elapsed / 1e9, "unit": "GB/s",
+            "tokens_per_s": world * w.tokens_per_step() * steps / elapsed,
+            "ms_per_step": elapsed / steps * 1e3, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(out_bytes), "timer": "host perf_counter around K steps",
+            "output_finite": ok}
+
+
+# ---------------------------------------------------------------------------
+def cpu_sample(w, target_s: float = 12.0, max_seqs: int | None = None):
+    """Time the oracle (C port of the reference CPU path, OpenMP on all cores)
+    on the first sequences of the workload; returns GB/s of that sample."""
+    import oracle
+
+    from doe_b200 import workloads  # noqa: F401
+
+    rng = np.random.default_rng(w.seed + 7)
+    rows_total = w.num_pages * w.page_size
+    # pools for the sampled sequences only: remap their pages densely
+    def run(nseq):
+        sel = np.arange(nseq)
+        pages = [w.block_table[b][w.block_table[b] >= 0] for b in sel]
+        npg = sum(len(p) for p in pages)
+        table = np.full((nseq, w.block_table.shape[1]), -1, np.int32)
+        o = 0
+        for i, p in enumerate(pages):
+            table[i, :len(p)] = np.arange(o, o + len(p))
+            o += len(p)
+        shape = (npg * w.page_size, w.num_kv_heads, w.head_dim)
+        if w.kv_dtype == "f16":
+            kp = rng.standard_normal(shape, dtype=np.float32).astype(np.float16).view(np.uint16)
+            vp = rng.standard_normal(shape, dtype=np.float32).astype(np.float16).view(np.uint16)
+            ks = vs = None
+        else:
+            kp = rng.integers(-127, 128, shape, dtype=np.int8)
+            vp = rng.integers(-127, 128, shape, dtype=np.int8)
+            ks = oracle.f2h(np.full((npg, w.num_kv_heads, w.page_size), 0.01, np.float32))
+            vs = ks.copy()
+        lens = w.seq_lens[sel]
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        oracle.paged_append(w.new_k[sel][:, None].view(np.uint16), w.new_v[sel][:, None].view(np.uint16),
+                            kp, vp, table, w.ctx[sel].astype(np.int32), page_size=w.page_size,
+                            k_scale=ks, v_scale=vs, threads=threads)
+        oracle.paged_decode(w.q[sel].view(np.uint16), kp, vp, table, lens, w.scale,
+                            page_size=w.page_size, k_scale=ks, v_scale=vs, threads=threads)
+        dt = time.perf_counter() - t0
+        nbytes = int(lens.sum()) * w.kv_bytes_per_token() + nseq * (w.num_heads * w.head_dim * 6)
+        return dt, nbytes, threads
+
+    dt, nb, threads = run(1)
+    n = w.num_seqs if max_seqs is None else max_seqs
+    want = int(min(n, max(1, target_s / max(dt, 1e-3))))
+    if want > 1:
+        dt, nb, threads = run(want)
+    else:
+        want = 1
+    del rows_total
+    return {"value": nb / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"first {want} of {w.num_seqs} sequences of {w.name} (fused append + decode), "
+                      f"{dt:.1f} s", "tokens_per_s": want / dt, "seconds": dt}
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU path (oracle port) on the same config/metric."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from doe_b200 import workloads
+
+    w = workloads.paged_f16()
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample(w, target_s=2.0, max_seqs=4)
+    samples = []
+    for _ in range(args.steps):
+        s = cpu_sample(w, target_s=4.0, max_seqs=8)
+        vals.append(s["value"])
+        samples.append(s)
+    v = float(np.mean(vals))
+    line = {
+        "impl": "reference", "metric": "decode-attn HBM GB/s (config 3 paged GQA decode)",
+        "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": float(np.mean([s["seconds"] for s in samples]) * 1e3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded)", "config": config_block(w),
+        "tokens_per_s": float(np.mean([s["tokens_per_s"] for s in samples])),
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": samples[0]["cores"], "kind": "port",
+                         "sample": samples[0]["sample"]},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's attention runs through Vulkan/Metal (unavailable on this box) and "
+                "its Zig host path cannot be built here; this is the C restatement of its CPU path",
+    }
+    print(json.dumps(line))
+
+
+def config_block(w) -> dict:
+    return {"workload": "config 3: paged GQA decode with fused append, 64 seqs, 32/8 heads, D 128, "
+                        "page 16, ctx U[1024,8192] seed 2, f16 KV",
+            "num_seqs": w.num_seqs, "num_heads": w.num_heads, "num_kv_heads": w.num_kv_heads,
+            "head_dim": w.head_dim, "page_size": w.page_size, "tokens_in_cache": int(w.ctx.sum()),
+            "pages": w.num_pages, "l2": "inputs larger than L2 (1.27 GB KV per step)",
+            "parallelism": "sequence-sharded replicas, no data collective"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+
+    world, rank, local = dist_setup()
+    pk = peaks()
+    from doe_b200 import workloads
+
+    w = workloads.paged_f16()
+    clocks = ClockSampler(local)
+    clocks.start()
+    head, cache, dev = measure_paged(w, 2, args.steps, args.warmup, world, pk)
+    clk = clocks.stop()
+    del cache, dev
+    torch.cuda.empty_cache()
+
+    extras = {}
+    if not args.no_extras:
+        w4 = workloads.paged_int8()
+        r4, cache4, _ = measure_paged(w4, 3, max(5, args.steps // 2), 3, world, pk)
+        ca = measure_chunk_append(w4, cache4, 5, 3, world, pk)
+        del cache4
+        torch.cuda.empty_cache()
+        extras["int8_decode"] = {"config": "config 4: 32 seqs, ctx U[8192,32768] seed 3, int8 KV + f16 scales",
+                                 "gbs": r4["gbs"], "tokens_per_s": r4["tokens_per_s"],
+                                 "ms_per_step": r4["ms_per_step"], "kernel_frac": r4["frac"],
+                                 "bytes_per_step": r4["bytes_per_step"]["total"]}
+        extras["int8_chunk_append"] = {"config": "config 4b: 32 x 512 tokens quantised into the paged cache",
+                                       **ca}
+        extras["f32_decode"] = {"config": "config 1: 8 heads, D 64, 512 tokens, f32", **measure_f32(20, 5, world, pk)}
+
+    cache, dev = build_paged(w, 2)
+    e2e = measure_e2e(w, cache, max(5, args.steps // 2), 2, world)
+    del cache, dev
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sample(w)
+
+    traffic = profiled_traffic().get("paged_decode_f16")
+    roof = {"bound": "hbm", "achieved": head["kernel_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": head["frac"], "traffic": traffic,
+            "kernel": "paged_decode_kernel<f16,4> + combine_splits_kernel (one doe_paged_decode call)",
+            "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
+            "algorithmic_bytes_per_launch": head["bytes_per_step"]["total"]}
+    if rank == 0:
+        line = {
+            "metric": "decode-attn HBM GB/s (config 3 paged GQA decode, fused append)",
+            "value": head["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded)",
+            "config": config_block(w), "tokens_per_s": head["tokens_per_s"],
+            "roofline": roof, "clocks": clk, "e2e": e2e,
+            "gpu_launches": 2 * args.steps,
+            "cpu_baseline": cpu, **extras,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,79 @@
+// common.cuh -- shared device helpers for the sm_100a attention / KV kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/doe_cuda.h"
+#include "kernels.h"
+
+namespace doe {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void report(int32_t* status, int32_t bits) {
+  if (status) atomicOr(status, bits);
+}
+
+// ---- warp mma: D = A(16x16 f16, row) * B(16x8 f16, col) + C (f32) -------
+// Fragment layout (PTX ISA, mma.m16n8k16 .f16): lane = 4*g + t.
+//   A regs: {(g, 2t..2t+1), (g+8, 2t..), (g, 2t+8..), (g+8, 2t+8..)}
+//   B regs: {(k=2t..2t+1, n=g), (k=2t+8.., n=g)}
+//   C: c0,c1 = (g, 2t..2t+1), c2,c3 = (g+8, 2t..2t+1)
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                          uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Two signed bytes -> f16x2, exactly.  `t` holds byte b_lo in bits 0-7 and
+// b_hi in bits 16-23 (other bits ignored).  Each byte, offset by 128 (sign
+// bit flipped), is placed in the mantissa of 1024.0h (0x6400): the f16 value
+// 1024 + (b + 128) is exact because f16 spacing in [1024, 2048) is 1, and
+// subtracting 1152 returns b.
+__device__ __forceinline__ uint32_t s8x2_to_f16x2(uint32_t t) {
+  uint32_t biased = (t & 0x00ff00ffu) ^ 0x64806480u;
+  __half2 h = *reinterpret_cast<__half2*>(&biased);
+  const uint32_t k1152 = 0x64806480u;
+  h = __hsub2(h, *reinterpret_cast<const __half2*>(&k1152));
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t x, uint32_t y, uint32_t sel) {
+  return __byte_perm(x, y, sel);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// 128-bit global load that bypasses L1 allocation: KV pages are streamed once.
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__host__ __device__ inline uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
+
+}  // namespace doe

@@ -1,0 +1,63 @@
+// kernels.h -- internal launch entry points shared by the translation units
+// of libdoe_cuda.so (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/doe_cuda.h"
+
+namespace doe {
+
+void set_op_error(const char* fmt, ...);
+int cuda_status(cudaError_t err, const char* where);
+
+// Arguments of the head256-semantics online-softmax kernel (attn_generic.cu).
+struct GenericAttnArgs {
+  doe_attn_uniforms u;
+  const float* q;
+  const void* k;
+  const void* v;
+  float* out;
+  const uint32_t* kv_len_buffer;
+  const uint32_t* page_table;
+  uint64_t page_table_len;  // entries; 0 = unchecked
+  uint64_t kv_rows;         // rows in K/V; 0 = unchecked
+  int64_t q_pos_stride, q_head_stride;    // elements of q / out
+  int64_t kv_pos_stride, kv_head_stride;  // elements of k / v
+  int32_t* status;
+};
+
+int launch_attn_generic(const GenericAttnArgs& a, bool kv_f32, cudaStream_t st);
+
+uint64_t decode_f32_workspace(uint32_t num_heads, uint32_t head_dim, uint32_t kv_len);
+int launch_decode_f32(const float* q, const float* k, const float* v, float* out,
+                      uint32_t num_heads, uint32_t head_dim, uint32_t kv_len, float scale,
+                      const doe_launch* launch);
+int launch_combine_natural(const float* part_o, const float* part_ml, float* out, int rows,
+                           int fixed_len, int split_tokens, int max_splits, int head_dim,
+                           cudaStream_t st);
+int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
+                        const void* q, const int32_t* seq_lens, const void* new_k,
+                        const void* new_v, float scale, float* out, uint32_t split_pages,
+                        const doe_launch* launch, uint64_t* ws_needed_out);
+int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
+                        const void* new_k, const void* new_v, const int32_t* positions,
+                        const doe_launch* launch);
+int launch_paged_gather(const doe_paged_kv* kv, uint32_t seq, uint32_t start, uint32_t len,
+                        void* k_out, void* v_out, void* ks_out, void* vs_out,
+                        const doe_launch* launch);
+int launch_kv_write_dense(const void* k_proj, const void* v_proj, void* k_cache, void* v_cache,
+                          const uint32_t* positions, uint32_t num_positions, uint32_t heads,
+                          uint32_t max_seq_len, uint32_t head_dim, uint32_t elem_bytes,
+                          const doe_launch* launch);
+int launch_kv_read_dense(const void* k_cache, const void* v_cache, void* k_out, void* v_out,
+                         uint32_t heads, uint32_t read_start, uint32_t read_len,
+                         uint32_t max_seq_len, uint32_t head_dim, uint32_t elem_bytes,
+                         const doe_launch* launch);
+int launch_stitch(const float* partials, uint32_t rows, uint32_t num_shards, uint32_t head_dim,
+                  float* out, const doe_launch* launch);
+int launch_rope(float* qk, const float* freq_cis, uint32_t seq_len, uint32_t num_heads,
+                uint32_t head_dim, uint32_t position_offset, const doe_launch* launch);
+
+}  // namespace doe

@@ -1,0 +1,322 @@
+// kv_cache.cu -- KV-cache writes and reads, the stitch op and rope.
+//
+//   paged append  : kv_write (runtime/zig/src/tsir/emit_kernel_body.zig:620-690,
+//                   emit_kernel_body_kv.zig:30-102) over a paged pool, with
+//                   per-(token, kv head) int8 quantisation for int8 pools
+//   paged gather  : kv_read (emit_kernel_body.zig:692-760) through a block table
+//   dense write / read : the reference's per-head form, position checked
+//                   against max_seq_len (run_csl_webgpu_emulator.mjs:615-644)
+//   stitch        : bench/tools/attention_kv_axis_sharded_stitch.py:46-90
+//   rope          : bench/inference-pipeline/kernels/rope.wgsl:12-35
+//
+// All copies are bit-exact; the int8 quantiser uses IEEE division and
+// round-to-nearest-even so it matches the CPU definition bit for bit.
+#include "common.cuh"
+
+namespace doe {
+
+// ---- paged append ----------------------------------------------------------
+struct PagedAppendArgs {
+  const __half* new_k;  // [B, T, Hkv, D]
+  const __half* new_v;
+  uint8_t* k_pool;
+  uint8_t* v_pool;
+  __half* k_scale;      // [num_pages, Hkv, page_size]
+  __half* v_scale;
+  const int32_t* block_table;
+  const int32_t* positions;
+  int32_t* status;
+  int n_tokens, num_kv_heads, head_dim, page_size, num_pages, max_pages;
+};
+
+// One warp per (sequence, token, kv head); lane owns head_dim/32 elements
+// (an even count, so they load as half2 pairs).
+template <bool INT8, int EPL>
+__global__ void __launch_bounds__(256) paged_append_kernel(const PagedAppendArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x, b = blockIdx.y;
+  const int Hkv = a.num_kv_heads, D = a.head_dim;
+  const int pos0 = a.positions[b];
+  const long long pos = (long long)pos0 + t;
+  const long long pidx = pos / a.page_size;
+  int page = -1;
+  if (pos0 >= 0 && pidx < a.max_pages) page = a.block_table[(size_t)b * a.max_pages + pidx];
+  if ((unsigned)page >= (unsigned)a.num_pages) {
+    if (threadIdx.x == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
+    return;
+  }
+  const int in_page = (int)(pos - pidx * a.page_size);
+  const size_t row = (size_t)page * a.page_size + in_page;
+  for (int h = warp; h < Hkv; h += 8) {
+    const size_t src_off = (((size_t)b * a.n_tokens + t) * Hkv + h) * D + (size_t)lane * EPL;
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const __half* src = (kv ? a.new_v : a.new_k) + src_off;
+      __half2 x2[EPL / 2];
+#pragma unroll
+      for (int i = 0; i < EPL / 2; ++i) x2[i] = reinterpret_cast<const __half2*>(src)[i];
+      if (!INT8) {
+        __half2* dst = reinterpret_cast<__half2*>((kv ? a.v_pool : a.k_pool) +
+                                                  ((row * Hkv + h) * D + (size_t)lane * EPL) * 2);
+#pragma unroll
+        for (int i = 0; i < EPL / 2; ++i) dst[i] = x2[i];
+      } else {
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < EPL / 2; ++i)
+          amax = fmaxf(amax, fmaxf(fabsf(__low2float(x2[i])), fabsf(__high2float(x2[i]))));
+        amax = warp_max(amax);
+        const __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
+        const float sf = __half2float(sh);
+        int8_t* dst = reinterpret_cast<int8_t*>(kv ? a.v_pool : a.k_pool) + (row * Hkv + h) * D +
+                      (size_t)lane * EPL;
+#pragma unroll
+        for (int i = 0; i < EPL; ++i) {
+          const float xv = (i & 1) ? __high2float(x2[i / 2]) : __low2float(x2[i / 2]);
+          int qv = 0;
+          if (sf != 0.0f) {
+            qv = __float2int_rn(__fdiv_rn(xv, sf));
+            qv = qv > 127 ? 127 : (qv < -127 ? -127 : qv);
+          }
+          dst[i] = (int8_t)qv;
+        }
+        if (lane == 0) (kv ? a.v_scale : a.k_scale)[((size_t)page * Hkv + h) * a.page_size + in_page] = sh;
+      }
+    }
+  }
+}
+
+int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
+                        const void* new_k, const void* new_v, const int32_t* positions,
+                        const doe_launch* launch) {
+  if (num_seqs == 0 || n_tokens == 0) return DOE_OK;
+  if (kv->head_dim % 64 != 0 || kv->head_dim > 512) {
+    set_op_error("doe_paged_append: head_dim must be a multiple of 64 up to 512 (got %u)",
+                 kv->head_dim);
+    return DOE_UNSUPPORTED;
+  }
+  PagedAppendArgs a;
+  a.new_k = static_cast<const __half*>(new_k);
+  a.new_v = static_cast<const __half*>(new_v);
+  a.k_pool = static_cast<uint8_t*>(kv->k_pool);
+  a.v_pool = static_cast<uint8_t*>(kv->v_pool);
+  a.k_scale = static_cast<__half*>(kv->k_scale);
+  a.v_scale = static_cast<__half*>(kv->v_scale);
+  a.block_table = kv->block_table;
+  a.positions = positions;
+  a.status = launch->status;
+  a.n_tokens = (int)n_tokens;
+  a.num_kv_heads = (int)kv->num_kv_heads;
+  a.head_dim = (int)kv->head_dim;
+  a.page_size = (int)kv->page_size;
+  a.num_pages = (int)kv->num_pages;
+  a.max_pages = (int)kv->max_pages_per_seq;
+  cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
+  dim3 grid(n_tokens, num_seqs), block(256);
+  const bool int8 = kv->kv_dtype == DOE_KV_INT8;
+  const int epl = (int)kv->head_dim / 32;
+#define DOE_PA(E) \
+  (int8 ? paged_append_kernel<true, E><<<grid, block, 0, st>>>(a) \
+        : paged_append_kernel<false, E><<<grid, block, 0, st>>>(a))
+  switch (epl) {
+    case 2: DOE_PA(2); break;
+    case 4: DOE_PA(4); break;
+    case 6: DOE_PA(6); break;
+    case 8: DOE_PA(8); break;
+    case 10: DOE_PA(10); break;
+    case 12: DOE_PA(12); break;
+    case 14: DOE_PA(14); break;
+    default: DOE_PA(16); break;
+  }
+#undef DOE_PA
+  return cuda_status(cudaGetLastError(), "paged_append_kernel");
+}
+
+// ---- paged gather (kv_read) ------------------------------------------------
+struct PagedGatherArgs {
+  const uint8_t* k_pool;
+  const uint8_t* v_pool;
+  const __half* k_scale;
+  const __half* v_scale;
+  uint8_t* k_out;
+  uint8_t* v_out;
+  __half* ks_out;
+  __half* vs_out;
+  const int32_t* table_row;
+  int32_t* status;
+  int start, len, num_kv_heads, row_bytes, page_size, num_pages, max_pages;
+};
+
+__global__ void paged_gather_kernel(const PagedGatherArgs a) {
+  const int i = blockIdx.x;  // output token
+  const long long pos = (long long)a.start + i;
+  const long long pidx = pos / a.page_size;
+  const int page = pidx < a.max_pages ? a.table_row[pidx] : -1;
+  if ((unsigned)page >= (unsigned)a.num_pages) {
+    if (threadIdx.x == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
+    return;
+  }
+  const int in_page = (int)(pos - pidx * a.page_size);
+  const size_t row = (size_t)page * a.page_size + in_page;
+  const int n16 = a.row_bytes / 16;
+  for (int j = threadIdx.x; j < n16; j += blockDim.x) {
+    reinterpret_cast<uint4*>(a.k_out + (size_t)i * a.row_bytes)[j] =
+        reinterpret_cast<const uint4*>(a.k_pool + row * a.row_bytes)[j];
+    reinterpret_cast<uint4*>(a.v_out + (size_t)i * a.row_bytes)[j] =
+        reinterpret_cast<const uint4*>(a.v_pool + row * a.row_bytes)[j];
+  }
+  if (a.ks_out && a.k_scale) {
+    for (int h = threadIdx.x; h < a.num_kv_heads; h += blockDim.x) {
+      const size_t si = ((size_t)page * a.num_kv_heads + h) * a.page_size + in_page;
+      a.ks_out[(size_t)i * a.num_kv_heads + h] = a.k_scale[si];
+      a.vs_out[(size_t)i * a.num_kv_heads + h] = a.v_scale[si];
+    }
+  }
+}
+
+int launch_paged_gather(const doe_paged_kv* kv, uint32_t seq, uint32_t start, uint32_t len,
+                        void* k_out, void* v_out, void* ks_out, void* vs_out,
+                        const doe_launch* launch) {
+  if (len == 0) return DOE_OK;
+  const uint32_t elem = kv->kv_dtype == DOE_KV_INT8 ? 1 : 2;
+  const uint64_t row_bytes = (uint64_t)kv->num_kv_heads * kv->head_dim * elem;
+  if (row_bytes % 16 != 0) {
+    set_op_error("doe_paged_gather: row of %llu bytes is not a multiple of 16",
+                 (unsigned long long)row_bytes);
+    return DOE_UNSUPPORTED;
+  }
+  PagedGatherArgs a;
+  a.k_pool = static_cast<const uint8_t*>(kv->k_pool);
+  a.v_pool = static_cast<const uint8_t*>(kv->v_pool);
+  a.k_scale = static_cast<const __half*>(kv->k_scale);
+  a.v_scale = static_cast<const __half*>(kv->v_scale);
+  a.k_out = static_cast<uint8_t*>(k_out);
+  a.v_out = static_cast<uint8_t*>(v_out);
+  a.ks_out = static_cast<__half*>(ks_out);
+  a.vs_out = static_cast<__half*>(vs_out);
+  a.table_row = kv->block_table + (size_t)seq * kv->max_pages_per_seq;
+  a.status = launch->status;
+  a.start = (int)start;
+  a.len = (int)len;
+  a.num_kv_heads = (int)kv->num_kv_heads;
+  a.row_bytes = (int)row_bytes;
+  a.page_size = (int)kv->page_size;
+  a.num_pages = (int)kv->num_pages;
+  a.max_pages = (int)kv->max_pages_per_seq;
+  paged_gather_kernel<<<len, 128, 0, static_cast<cudaStream_t>(launch->stream)>>>(a);
+  return cuda_status(cudaGetLastError(), "paged_gather_kernel");
+}
+
+// ---- dense per-head kv_write / kv_read --------------------------------------
+__global__ void kv_write_dense_kernel(const uint8_t* k_proj, const uint8_t* v_proj,
+                                      uint8_t* k_cache, uint8_t* v_cache,
+                                      const uint32_t* positions, uint32_t num_positions,
+                                      uint32_t max_seq_len, uint32_t row_bytes,
+                                      int32_t* status) {
+  const uint32_t head = blockIdx.x;
+  const uint32_t pos = positions[num_positions == 1 ? 0 : head];
+  if (pos >= max_seq_len) {
+    if (threadIdx.x == 0) report(status, DOE_DEVICE_ERR_POSITION);
+    return;
+  }
+  const size_t src = (size_t)head * row_bytes;
+  const size_t dst = ((size_t)head * max_seq_len + pos) * row_bytes;
+  for (uint32_t j = threadIdx.x; j < row_bytes; j += blockDim.x) {
+    k_cache[dst + j] = k_proj[src + j];
+    v_cache[dst + j] = v_proj[src + j];
+  }
+}
+
+__global__ void kv_read_dense_kernel(const uint8_t* k_cache, const uint8_t* v_cache,
+                                     uint8_t* k_out, uint8_t* v_out, uint32_t read_start,
+                                     uint32_t read_len, uint32_t max_seq_len,
+                                     uint32_t row_bytes) {
+  const uint32_t i = blockIdx.x, head = blockIdx.y;
+  const size_t src = ((size_t)head * max_seq_len + read_start + i) * row_bytes;
+  const size_t dst = ((size_t)head * read_len + i) * row_bytes;
+  for (uint32_t j = threadIdx.x; j < row_bytes; j += blockDim.x) {
+    k_out[dst + j] = k_cache[src + j];
+    v_out[dst + j] = v_cache[src + j];
+  }
+}
+
+int launch_kv_write_dense(const void* k_proj, const void* v_proj, void* k_cache, void* v_cache,
+                          const uint32_t* positions, uint32_t num_positions, uint32_t heads,
+                          uint32_t max_seq_len, uint32_t head_dim, uint32_t elem_bytes,
+                          const doe_launch* launch) {
+  if (heads == 0) return DOE_OK;
+  kv_write_dense_kernel<<<heads, 128, 0, static_cast<cudaStream_t>(launch->stream)>>>(
+      static_cast<const uint8_t*>(k_proj), static_cast<const uint8_t*>(v_proj),
+      static_cast<uint8_t*>(k_cache), static_cast<uint8_t*>(v_cache), positions, num_positions,
+      max_seq_len, head_dim * elem_bytes, launch->status);
+  return cuda_status(cudaGetLastError(), "kv_write_dense_kernel");
+}
+
+int launch_kv_read_dense(const void* k_cache, const void* v_cache, void* k_out, void* v_out,
+                         uint32_t heads, uint32_t read_start, uint32_t read_len,
+                         uint32_t max_seq_len, uint32_t head_dim, uint32_t elem_bytes,
+                         const doe_launch* launch) {
+  if (heads == 0 || read_len == 0) return DOE_OK;
+  kv_read_dense_kernel<<<dim3(read_len, heads), 128, 0, static_cast<cudaStream_t>(launch->stream)>>>(
+      static_cast<const uint8_t*>(k_cache), static_cast<const uint8_t*>(v_cache),
+      static_cast<uint8_t*>(k_out), static_cast<uint8_t*>(v_out), read_start, read_len,
+      max_seq_len, head_dim * elem_bytes);
+  return cuda_status(cudaGetLastError(), "kv_read_dense_kernel");
+}
+
+// ---- stitch (natural-domain partials rows [O[D], max, sum]) -----------------
+__global__ void stitch_kernel(const float* partials, uint32_t num_shards, uint32_t head_dim,
+                              float* out) {
+  const uint32_t row = blockIdx.x;
+  const uint32_t w = head_dim + 2;
+  const float* p = partials + (size_t)row * num_shards * w;
+  float gmax = p[head_dim];
+  for (uint32_t i = 1; i < num_shards; ++i) gmax = fmaxf(gmax, p[(size_t)i * w + head_dim]);
+  float gsum = 0.0f;
+  for (uint32_t i = 0; i < num_shards; ++i)
+    gsum += expf(p[(size_t)i * w + head_dim] - gmax) * p[(size_t)i * w + head_dim + 1];
+  for (uint32_t d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float acc = 0.0f;
+    if (gsum != 0.0f)
+      for (uint32_t i = 0; i < num_shards; ++i)
+        acc += expf(p[(size_t)i * w + head_dim] - gmax) * p[(size_t)i * w + d];
+    out[(size_t)row * head_dim + d] = gsum == 0.0f ? 0.0f : acc / gsum;
+  }
+}
+
+int launch_stitch(const float* partials, uint32_t rows, uint32_t num_shards, uint32_t head_dim,
+                  float* out, const doe_launch* launch) {
+  if (rows == 0) return DOE_OK;
+  const uint32_t threads = head_dim >= 256 ? 256 : ((head_dim + 31) / 32) * 32;
+  stitch_kernel<<<rows, threads, 0, static_cast<cudaStream_t>(launch->stream)>>>(
+      partials, num_shards, head_dim, out);
+  return cuda_status(cudaGetLastError(), "stitch_kernel");
+}
+
+// ---- rope --------------------------------------------------------------------
+__global__ void rope_kernel(float* qk, const float* freq_cis, uint32_t seq_len,
+                            uint32_t num_heads, uint32_t head_dim, uint32_t position_offset) {
+  const uint32_t half = head_dim / 2;
+  const uint32_t pair = blockIdx.x * blockDim.x + threadIdx.x;
+  const uint32_t head = blockIdx.y, s = blockIdx.z;
+  if (pair >= half || head >= num_heads || s >= seq_len) return;
+  const uint64_t pos = (uint64_t)s + position_offset;
+  float* base = qk + ((size_t)s * num_heads + head) * head_dim;
+  const float x0 = base[pair], x1 = base[pair + half];
+  const uint64_t f = pos * half + pair;
+  const float c = freq_cis[f * 2], sn = freq_cis[f * 2 + 1];
+  base[pair] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sn));
+  base[pair + half] = __fadd_rn(__fmul_rn(x0, sn), __fmul_rn(x1, c));
+}
+
+int launch_rope(float* qk, const float* freq_cis, uint32_t seq_len, uint32_t num_heads,
+                uint32_t head_dim, uint32_t position_offset, const doe_launch* launch) {
+  if (seq_len == 0 || num_heads == 0 || head_dim < 2) return DOE_OK;
+  const uint32_t half = head_dim / 2;
+  dim3 grid((half + 63) / 64, num_heads, seq_len);
+  rope_kernel<<<grid, 64, 0, static_cast<cudaStream_t>(launch->stream)>>>(
+      qk, freq_cis, seq_len, num_heads, head_dim, position_offset);
+  return cuda_status(cudaGetLastError(), "rope_kernel");
+}
+
+}  // namespace doe

@@ -1,0 +1,266 @@
+// ops.cu -- the operator surface of include/doe_cuda.h: argument checks and
+// launches on caller-owned device memory.  No entry point runs work on the
+// host; an unsupported shape returns DOE_UNSUPPORTED with a message.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "common.cuh"
+
+namespace doe {
+
+static thread_local char g_op_error[512] = "";
+
+void set_op_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_op_error, sizeof(g_op_error), fmt, ap);
+  va_end(ap);
+}
+
+int cuda_status(cudaError_t err, const char* where) {
+  if (err == cudaSuccess) return DOE_OK;
+  set_op_error("%s: %s (%s)", where, cudaGetErrorName(err), cudaGetErrorString(err));
+  if (err == cudaErrorNoDevice || err == cudaErrorInvalidDevice) return DOE_NO_DEVICE;
+  return DOE_CUDA_ERROR;
+}
+
+}  // namespace doe
+
+using namespace doe;
+
+namespace {
+
+const doe_launch kDefaultLaunch = {nullptr, nullptr, 0, nullptr};
+
+const doe_launch* launch_or_default(const doe_launch* l) { return l ? l : &kDefaultLaunch; }
+
+int invalid(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  set_op_error("%s", buf);
+  return DOE_INVALID_ARGUMENT;
+}
+
+int check_paged_kv(const doe_paged_kv* kv, const char* fn) {
+  if (!kv) return invalid("%s: kv is null", fn);
+  if (!kv->k_pool || !kv->v_pool || !kv->block_table)
+    return invalid("%s: k_pool, v_pool and block_table are required", fn);
+  if (kv->kv_dtype > DOE_KV_INT8) return invalid("%s: unknown kv_dtype %u", fn, kv->kv_dtype);
+  if (kv->kv_dtype == DOE_KV_INT8 && (!kv->k_scale || !kv->v_scale))
+    return invalid("%s: int8 pools need k_scale and v_scale", fn);
+  if (kv->page_size == 0 || kv->page_size % 16 != 0)
+    return invalid("%s: page_size must be a positive multiple of 16 (got %u)", fn, kv->page_size);
+  if (kv->num_kv_heads == 0 || kv->head_dim == 0 || kv->num_pages == 0)
+    return invalid("%s: num_kv_heads, head_dim and num_pages must be positive", fn);
+  if (kv->max_pages_per_seq == 0) return invalid("%s: max_pages_per_seq must be positive", fn);
+  return DOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int doe_cuda_abi_version(void) { return DOE_CUDA_ABI_VERSION; }
+
+int doe_cuda_device_count(int* count) {
+  if (!count) return DOE_INVALID_ARGUMENT;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    *count = 0;
+    cudaGetLastError();
+    return cuda_status(e, "cudaGetDeviceCount") == DOE_CUDA_ERROR ? DOE_NO_DEVICE : DOE_NO_DEVICE;
+  }
+  *count = n;
+  return DOE_OK;
+}
+
+const char* doe_cuda_op_last_error(void) { return g_op_error; }
+
+uint64_t doe_attention_decode_f32_workspace_bytes(uint32_t num_heads, uint32_t head_dim,
+                                                  uint32_t kv_len) {
+  return decode_f32_workspace(num_heads, head_dim, kv_len);
+}
+
+int doe_attention_decode_f32(const float* q, const float* k_cache, const float* v_cache,
+                             float* out, uint32_t num_heads, uint32_t head_dim, uint32_t kv_len,
+                             float scale, const doe_launch* launch) {
+  if (!q || !k_cache || !v_cache || !out) return invalid("doe_attention_decode_f32: null pointer");
+  if (head_dim == 0 || head_dim > 256)
+    return invalid("doe_attention_decode_f32: head_dim must be 1..256 (got %u)", head_dim);
+  if (num_heads == 0) return DOE_OK;
+  if (kv_len == 0) return invalid("doe_attention_decode_f32: kv_len must be positive");
+  return launch_decode_f32(q, k_cache, v_cache, out, num_heads, head_dim, kv_len, scale,
+                           launch_or_default(launch));
+}
+
+int doe_attention_online(const doe_attn_uniforms* u, const float* q, const void* k,
+                         const void* v, uint32_t kv_elem, float* out,
+                         const uint32_t* kv_len_buffer, const uint32_t* page_table,
+                         const doe_launch* launch) {
+  if (!u || !q || !k || !v || !out) return invalid("doe_attention_online: null pointer");
+  if (u->num_kv_heads == 0 || u->num_heads % u->num_kv_heads != 0)
+    return invalid("doe_attention_online: num_heads %u is not a multiple of num_kv_heads %u",
+                   u->num_heads, u->num_kv_heads);
+  if (u->head_dim == 0 || u->head_dim > 512)
+    return invalid("doe_attention_online: head_dim must be 1..512 (got %u)", u->head_dim);
+  if (u->kv_layout > 2) return invalid("doe_attention_online: kv_layout %u", u->kv_layout);
+  if (u->kv_layout == 2 && (!page_table || u->page_size == 0))
+    return invalid("doe_attention_online: paged layout needs page_table and page_size");
+  if (u->kv_len_source != 0 && !kv_len_buffer)
+    return invalid("doe_attention_online: kv_len_source needs kv_len_buffer");
+  if (kv_elem > 1) return invalid("doe_attention_online: kv_elem must be 0 (f16) or 1 (f32)");
+  const doe_launch* l = launch_or_default(launch);
+  GenericAttnArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.u = *u;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  a.kv_len_buffer = kv_len_buffer;
+  a.page_table = page_table;
+  a.q_pos_stride = (int64_t)u->num_heads * u->head_dim;
+  a.q_head_stride = u->head_dim;
+  a.kv_pos_stride = (int64_t)u->num_kv_heads * u->head_dim;
+  a.kv_head_stride = u->head_dim;
+  a.status = l->status;
+  return launch_attn_generic(a, kv_elem == 1, static_cast<cudaStream_t>(l->stream));
+}
+
+int doe_attention_prefill_wgsl_f32(const float* q, const float* k, const float* v, float* out,
+                                   uint32_t seq_len, uint32_t head_dim, uint32_t num_heads,
+                                   float scale, const doe_launch* launch) {
+  if (!q || !k || !v || !out) return invalid("doe_attention_prefill_wgsl_f32: null pointer");
+  if (head_dim == 0 || head_dim > 512)
+    return invalid("doe_attention_prefill_wgsl_f32: head_dim must be 1..512");
+  const doe_launch* l = launch_or_default(launch);
+  GenericAttnArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.u.num_heads = num_heads;
+  a.u.num_kv_heads = num_heads;
+  a.u.head_dim = head_dim;
+  a.u.seq_len = seq_len;
+  a.u.query_len = seq_len;
+  a.u.scale = scale;
+  a.u.is_causal = 1;
+  a.q = q;
+  a.k = k;
+  a.v = v;
+  a.out = out;
+  // [H, S, D]: position stride D, head stride S*D
+  a.q_pos_stride = head_dim;
+  a.q_head_stride = (int64_t)seq_len * head_dim;
+  a.kv_pos_stride = head_dim;
+  a.kv_head_stride = (int64_t)seq_len * head_dim;
+  a.kv_rows = seq_len;
+  a.status = l->status;
+  return launch_attn_generic(a, true, static_cast<cudaStream_t>(l->stream));
+}
+
+int doe_attention_stitch_f32(const float* partials, uint32_t rows, uint32_t num_shards,
+                             uint32_t head_dim, float* out, const doe_launch* launch) {
+  if (!partials || !out) return invalid("doe_attention_stitch_f32: null pointer");
+  if (num_shards == 0 || head_dim == 0)
+    return invalid("doe_attention_stitch_f32: num_shards and head_dim must be positive");
+  return launch_stitch(partials, rows, num_shards, head_dim, out, launch_or_default(launch));
+}
+
+uint64_t doe_paged_decode_workspace_bytes(const doe_paged_kv* kv, uint32_t num_seqs,
+                                          uint32_t num_heads, uint32_t split_pages) {
+  if (check_paged_kv(kv, "doe_paged_decode_workspace_bytes") != DOE_OK) return 0;
+  if (num_heads % kv->num_kv_heads != 0) return 0;
+  uint64_t ws = 0;
+  launch_paged_decode(kv, num_seqs, num_heads, nullptr, nullptr, nullptr, nullptr, 0.0f, nullptr,
+                      split_pages, &kDefaultLaunch, &ws);
+  return ws;
+}
+
+int doe_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
+                     const void* q, const int32_t* seq_lens, const void* new_k,
+                     const void* new_v, float scale, float* out, uint32_t split_pages,
+                     const doe_launch* launch) {
+  int rc = check_paged_kv(kv, "doe_paged_decode");
+  if (rc != DOE_OK) return rc;
+  if (!q || !seq_lens || !out) return invalid("doe_paged_decode: q, seq_lens and out are required");
+  if ((new_k == nullptr) != (new_v == nullptr))
+    return invalid("doe_paged_decode: new_k and new_v go together");
+  if (num_heads == 0 || num_heads % kv->num_kv_heads != 0)
+    return invalid("doe_paged_decode: num_heads %u is not a multiple of num_kv_heads %u",
+                   num_heads, kv->num_kv_heads);
+  if (kv->head_dim != 128) {
+    set_op_error("doe_paged_decode: the tensor-core decode kernel is built for head_dim 128 (got %u)",
+                 kv->head_dim);
+    return DOE_UNSUPPORTED;
+  }
+  if (num_seqs == 0) return DOE_OK;
+  if (num_seqs > 65535) return invalid("doe_paged_decode: at most 65535 sequences per launch");
+  return launch_paged_decode(kv, num_seqs, num_heads, q, seq_lens, new_k, new_v, scale, out,
+                             split_pages, launch_or_default(launch), nullptr);
+}
+
+int doe_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
+                     const void* new_k, const void* new_v, const int32_t* positions,
+                     const doe_launch* launch) {
+  int rc = check_paged_kv(kv, "doe_paged_append");
+  if (rc != DOE_OK) return rc;
+  if (!new_k || !new_v || !positions)
+    return invalid("doe_paged_append: new_k, new_v and positions are required");
+  if (num_seqs > 65535) return invalid("doe_paged_append: at most 65535 sequences per launch");
+  return launch_paged_append(kv, num_seqs, n_tokens, new_k, new_v, positions,
+                             launch_or_default(launch));
+}
+
+int doe_paged_gather(const doe_paged_kv* kv, uint32_t seq, uint32_t start, uint32_t len,
+                     void* k_out, void* v_out, void* k_scale_out, void* v_scale_out,
+                     const doe_launch* launch) {
+  int rc = check_paged_kv(kv, "doe_paged_gather");
+  if (rc != DOE_OK) return rc;
+  if (!k_out || !v_out) return invalid("doe_paged_gather: k_out and v_out are required");
+  if ((k_scale_out == nullptr) != (v_scale_out == nullptr))
+    return invalid("doe_paged_gather: scale outputs go together");
+  return launch_paged_gather(kv, seq, start, len, k_out, v_out, k_scale_out, v_scale_out,
+                             launch_or_default(launch));
+}
+
+int doe_kv_write_dense(const void* k_proj, const void* v_proj, void* k_cache, void* v_cache,
+                       const uint32_t* positions, uint32_t num_positions, uint32_t heads,
+                       uint32_t max_seq_len, uint32_t head_dim, uint32_t elem_bytes,
+                       const doe_launch* launch) {
+  if (!k_proj || !v_proj || !k_cache || !v_cache || !positions)
+    return invalid("doe_kv_write_dense: null pointer");
+  if (elem_bytes != 2 && elem_bytes != 4) return invalid("doe_kv_write_dense: elem_bytes 2 or 4");
+  if (num_positions != 1 && num_positions != heads)
+    return invalid("doe_kv_write_dense: positions must have 1 or heads (%u) entries", heads);
+  return launch_kv_write_dense(k_proj, v_proj, k_cache, v_cache, positions, num_positions, heads,
+                               max_seq_len, head_dim, elem_bytes, launch_or_default(launch));
+}
+
+int doe_kv_read_dense(const void* k_cache, const void* v_cache, void* k_out, void* v_out,
+                      uint32_t heads, uint32_t read_start, uint32_t read_len,
+                      uint32_t max_seq_len, uint32_t head_dim, uint32_t elem_bytes,
+                      const doe_launch* launch) {
+  if (!k_cache || !v_cache || !k_out || !v_out) return invalid("doe_kv_read_dense: null pointer");
+  if (elem_bytes != 2 && elem_bytes != 4) return invalid("doe_kv_read_dense: elem_bytes 2 or 4");
+  if ((uint64_t)read_start + read_len > max_seq_len) {
+    set_op_error("doe_kv_read_dense: rows [%u, %u) exceed max_seq_len %u", read_start,
+                 read_start + read_len, max_seq_len);
+    return DOE_OUT_OF_RANGE;
+  }
+  return launch_kv_read_dense(k_cache, v_cache, k_out, v_out, heads, read_start, read_len,
+                              max_seq_len, head_dim, elem_bytes, launch_or_default(launch));
+}
+
+int doe_rope_f32(float* qk, const float* freq_cis, uint32_t seq_len, uint32_t num_heads,
+                 uint32_t head_dim, uint32_t position_offset, const doe_launch* launch) {
+  if (!qk || !freq_cis) return invalid("doe_rope_f32: null pointer");
+  if (seq_len > 65535) return invalid("doe_rope_f32: at most 65535 positions per launch");
+  return launch_rope(qk, freq_cis, seq_len, num_heads, head_dim, position_offset,
+                     launch_or_default(launch));
+}
+
+}  // extern "C"

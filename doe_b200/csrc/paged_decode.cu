@@ -1,0 +1,514 @@
+// paged_decode.cu -- batched GQA decode over a paged KV cache (f16 or int8),
+// split-K over the KV length with a combine kernel, fused new-token append.
+//
+// Semantics: attention_head256_f16kv.wgsl with query_len 1 (every key of the
+// sequence active), GQA kv_head = h / (H / Hkv) (…wgsl:46-49), paged rows
+// phys = table[p / page] * page + p % page (…wgsl:51-63), out = acc / l or 0
+// when l == 0 (…wgsl:257-268); split partials stitched with the log-sum-exp
+// recipe of bench/tools/attention_kv_axis_sharded_stitch.py:46-90.
+//
+// Design (B200): the work is HBM-bound (2 flop/byte), so the kernel is built
+// around the loads.  One warp consumes one 16-token tile (a page, or a
+// 16-token slice of a larger page) per step with 128-bit loads taken straight
+// into mma.sync fragments -- no shared-memory staging, no barriers in the
+// loop.  A dimension permutation, applied identically to Q, makes every lane's
+// K/V bytes contiguous: each load instruction reads whole 32-byte sectors.
+//   S  = Q K^T   : m16n8k16, rows = the GROUP query heads of one kv head
+//   O^T = V^T P^T: m16n8k16, rows = 16 head dims, cols = the GROUP heads
+// so P moves from the S accumulator into the PV B operand without shuffles.
+// int8 tiles convert exactly to f16 in registers; the K scale multiplies S
+// and the V scale folds into P.  Scores run in the log2 domain (exp2f).
+#include "common.cuh"
+
+namespace doe {
+
+struct PagedDecodeArgs {
+  const __half* q;          // [B, H, D]
+  const uint8_t* k_pool;    // [rows, Hkv, D] f16 or int8
+  const uint8_t* v_pool;
+  const __half* k_scale;    // [num_pages, Hkv, page_size] (int8 only)
+  const __half* v_scale;
+  const int32_t* block_table;  // [B, max_pages]
+  const int32_t* seq_lens;     // [B]
+  const __half* new_k;      // [B, Hkv, D] or null
+  const __half* new_v;
+  float* out;               // [B, H, D]
+  float* part_o;            // [B*Hkv*max_splits, GROUP, D]
+  float* part_ml;           // [B*Hkv*max_splits, GROUP, 2]
+  int32_t* status;
+  int num_heads, num_kv_heads, num_pages, page_size, max_pages;
+  int split_tiles, max_splits;
+  float scale_log2;
+};
+
+constexpr int kD = 128;
+constexpr int kWarps = 4;
+
+__device__ __forceinline__ uint4 ldcg4(const uint8_t* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t w4(const uint4& v, int i) {
+  return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+}
+
+// Clamped sequence length and split count, shared with the combine kernel.
+__device__ __forceinline__ int clamp_len(int len, int cap) {
+  return len < 0 ? 0 : (len > cap ? cap : len);
+}
+
+// Writes the new token's K/V row of kv head g at position pos (one warp).
+template <bool INT8>
+__device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
+                           const int32_t* table, int lane) {
+  const int pidx = pos / a.page_size;
+  const int page = table[pidx];
+  if ((unsigned)page >= (unsigned)a.num_pages) {
+    if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
+    return;
+  }
+  const int in_page = pos - pidx * a.page_size;
+  const size_t row = (size_t)page * a.page_size + in_page;
+  const int Hkv = a.num_kv_heads;
+  const __half* srcs[2] = {a.new_k + ((size_t)b * Hkv + g) * kD,
+                           a.new_v + ((size_t)b * Hkv + g) * kD};
+  const uint8_t* pools[2] = {a.k_pool, a.v_pool};
+  const __half* scales[2] = {a.k_scale, a.v_scale};
+#pragma unroll
+  for (int kv = 0; kv < 2; ++kv) {
+    // lane owns elements [4*lane, 4*lane+4)
+    uint2 raw = *reinterpret_cast<const uint2*>(srcs[kv] + 4 * lane);
+    if (!INT8) {
+      uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * (kD * 2) + 8 * lane;
+      *reinterpret_cast<uint2*>(dst) = raw;
+    } else {
+      __half2 h01 = *reinterpret_cast<__half2*>(&raw.x);
+      __half2 h23 = *reinterpret_cast<__half2*>(&raw.y);
+      float x[4] = {__low2float(h01), __high2float(h01), __low2float(h23), __high2float(h23)};
+      float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+      amax = warp_max(amax);
+      __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
+      float sf = __half2float(sh);
+      uint32_t packed = 0;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        int qv = 0;
+        if (sf != 0.0f) {
+          qv = __float2int_rn(__fdiv_rn(x[e], sf));
+          qv = qv > 127 ? 127 : (qv < -127 ? -127 : qv);
+        }
+        packed |= (uint32_t)(qv & 0xff) << (8 * e);
+      }
+      uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * kD + 4 * lane;
+      *reinterpret_cast<uint32_t*>(dst) = packed;
+      if (lane == 0) {
+        __half* sdst = const_cast<__half*>(scales[kv]);
+        sdst[((size_t)page * Hkv + g) * a.page_size + in_page] = sh;
+      }
+    }
+  }
+}
+
+template <bool INT8, int GROUP>
+__global__ void __launch_bounds__(kWarps * 32)
+    paged_decode_kernel(const PagedDecodeArgs a) {
+  const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int Hkv = a.num_kv_heads;
+
+  const int raw_len = a.seq_lens[b];
+  const int cap = a.max_pages * a.page_size;
+  const int seq_len = clamp_len(raw_len, cap);
+  if (raw_len != seq_len && split == 0 && g == 0 && threadIdx.x == 0)
+    report(a.status, DOE_DEVICE_ERR_LENGTH);
+  const int ntiles = (seq_len + 15) >> 4;
+  const int nsplits = max(1, (ntiles + a.split_tiles - 1) / a.split_tiles);
+  if (split >= nsplits) return;
+  const int tile_begin = split * a.split_tiles;
+  const int tile_end = min(ntiles, tile_begin + a.split_tiles);
+  const int32_t* table = a.block_table + (size_t)b * a.max_pages;
+
+  __shared__ float sm_m[kWarps][8];
+  __shared__ float sm_l[kWarps][8];
+  __shared__ float sm_o[kWarps][GROUP][kD];
+
+  if (a.new_k != nullptr && split == nsplits - 1 && seq_len > 0) {
+    if (warp == 0) append_row<INT8>(a, b, g, seq_len - 1, table, lane);
+    __syncthreads();
+  }
+
+  // ---- Q fragments (rows = heads g*GROUP + r, r < GROUP) -----------------
+  // f16 pools:  k-block j = 2i + jj holds dims 32i + 8c + 4jj + {0,1 | 2,3}
+  // int8 pools: k-block j = 4i + w  holds dims 64i + 16c + 4w + {0,1 | 2,3}
+  uint32_t qa[8][2];
+  {
+    const __half* qrow = a.q + ((size_t)b * a.num_heads + (size_t)g * GROUP + r) * kD;
+    const bool live = r < GROUP;
+#pragma unroll
+    for (int i = 0; i < (INT8 ? 2 : 4); ++i) {
+#pragma unroll
+      for (int part = 0; part < (INT8 ? 2 : 1); ++part) {
+        const int dim0 = INT8 ? (64 * i + 16 * c + 8 * part) : (32 * i + 8 * c);
+        uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + dim0) : make_uint4(0, 0, 0, 0);
+        if (!INT8) {
+          qa[2 * i][0] = v.x; qa[2 * i][1] = v.y;
+          qa[2 * i + 1][0] = v.z; qa[2 * i + 1][1] = v.w;
+        } else {
+          // 8 dims = words 2w', 2w'+1 of the 16-dim run; k-block 4i + w
+          const int w0 = 2 * part;
+          qa[4 * i + w0][0] = v.x; qa[4 * i + w0][1] = v.y;
+          qa[4 * i + w0 + 1][0] = v.z; qa[4 * i + w0 + 1][1] = v.w;
+        }
+      }
+    }
+  }
+
+  float m_run = -INFINITY, l_run = 0.0f;
+  float acc[8][4];
+#pragma unroll
+  for (int mb = 0; mb < 8; ++mb) acc[mb][0] = acc[mb][1] = acc[mb][2] = acc[mb][3] = 0.0f;
+
+  constexpr int ROWB = INT8 ? kD : 2 * kD;  // bytes per (token, kv head) row
+  const size_t head_stride = (size_t)Hkv * ROWB;
+  const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+
+  for (int t = tile_begin + warp; t < tile_end; t += kWarps) {
+    const int pos0 = t << 4;
+    const int pidx = pos0 / a.page_size;
+    const int page = table[pidx];
+    if ((unsigned)page >= (unsigned)a.num_pages) {
+      if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
+      continue;
+    }
+    const int in0 = pos0 - pidx * a.page_size;
+    const size_t row0 = (size_t)page * a.page_size + in0;
+    const uint8_t* kbase = a.k_pool + row0 * head_stride + (size_t)g * ROWB;
+    const uint8_t* vbase = a.v_pool + row0 * head_stride + (size_t)g * ROWB;
+
+    // ---- loads: K rows r and 8+r, V rows 2c, 2c+1, 2c+8, 2c+9 ------------
+    uint4 kraw[2][INT8 ? 2 : 4];
+    uint4 vraw[4][INT8 ? 1 : 2];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int i = 0; i < (INT8 ? 2 : 4); ++i)
+        kraw[nb][i] = ldcg4(kbase + (size_t)(nb * 8 + r) * head_stride + 64 * i + 16 * c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int h = 0; h < (INT8 ? 1 : 2); ++h)
+        vraw[j][h] = ldcg4(vbase + (size_t)vt[j] * head_stride + (INT8 ? 16 * r : 128 * h + 16 * r));
+    uint32_t ksc[2] = {0, 0}, vsc[2] = {0, 0};
+    if (INT8) {
+      const size_t sb = ((size_t)page * Hkv + g) * a.page_size + in0;
+      ksc[0] = __ldcg(reinterpret_cast<const unsigned int*>(a.k_scale + sb + 2 * c));
+      ksc[1] = __ldcg(reinterpret_cast<const unsigned int*>(a.k_scale + sb + 8 + 2 * c));
+      vsc[0] = __ldcg(reinterpret_cast<const unsigned int*>(a.v_scale + sb + 2 * c));
+      vsc[1] = __ldcg(reinterpret_cast<const unsigned int*>(a.v_scale + sb + 8 + 2 * c));
+    }
+
+    // ---- S = Q K^T ----------------------------------------------------------
+    float s[2][4];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb) {
+      s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        uint32_t b0, b1;
+        if (!INT8) {
+          const uint4& v = kraw[nb][j >> 1];
+          b0 = w4(v, 2 * (j & 1));
+          b1 = w4(v, 2 * (j & 1) + 1);
+        } else {
+          const uint32_t x = w4(kraw[nb][j >> 2], j & 3);
+          b0 = s8x2_to_f16x2(prmt(x, x, 0x0100));
+          b1 = s8x2_to_f16x2(prmt(x, x, 0x0302));
+        }
+        mma_16816(s[nb], qa[j][0], 0u, qa[j][1], 0u, b0, b1);
+      }
+    }
+
+    // ---- online softmax (log2 domain), rows r ------------------------------
+    float x[2][2];
+    bool valid[2][2];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        valid[nb][e] = pos0 + nb * 8 + 2 * c + e < seq_len;
+        float sv = s[nb][e];
+        if (INT8) {
+          __half2 k2 = *reinterpret_cast<__half2*>(&ksc[nb]);
+          sv *= e ? __high2float(k2) : __low2float(k2);
+        }
+        x[nb][e] = valid[nb][e] ? sv * a.scale_log2 : -INFINITY;
+      }
+    float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+    const float m_new = fmaxf(m_run, tmax);  // finite: the tile holds a valid key
+    const float corr = exp2f(m_run - m_new);
+    float p[2][2];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) p[nb][e] = exp2f(x[nb][e] - m_new);
+    l_run = l_run * corr + ((p[0][0] + p[0][1]) + (p[1][0] + p[1][1]));
+    m_run = m_new;
+
+    float pv[2][2];
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float sc = 1.0f;
+        if (INT8) {
+          __half2 v2 = *reinterpret_cast<__half2*>(&vsc[nb]);
+          sc = e ? __high2float(v2) : __low2float(v2);
+        }
+        pv[nb][e] = (valid[nb][e] && r < GROUP) ? p[nb][e] * sc : 0.0f;
+      }
+    const uint32_t pb0 = pack_half2(pv[0][0], pv[0][1]);
+    const uint32_t pb1 = pack_half2(pv[1][0], pv[1][1]);
+
+    // accumulator columns are heads 2c, 2c+1: fetch their row corrections
+    const float cA = __shfl_sync(0xffffffffu, corr, (2 * c) * 4);
+    const float cB = __shfl_sync(0xffffffffu, corr, (2 * c + 1) * 4);
+#pragma unroll
+    for (int mb = 0; mb < 8; ++mb) {
+      acc[mb][0] *= cA; acc[mb][2] *= cA;
+      acc[mb][1] *= cB; acc[mb][3] *= cB;
+    }
+
+    // f16 V rows past the sequence end may hold any bits: zero them
+    if (!INT8) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (pos0 + vt[j] >= seq_len) vraw[j][0] = vraw[j][1] = make_uint4(0, 0, 0, 0);
+    }
+
+    // ---- O^T += V^T P^T ------------------------------------------------------
+#pragma unroll
+    for (int mb = 0; mb < 8; ++mb) {
+      uint32_t a0, a1, a2, a3;
+      if (!INT8) {
+        // m-block mb = 4h + w: rows r / r+8 = dims 64h + 8r + 2w + {0 / 1}
+        const int h = mb >> 2, w = mb & 3;
+        const uint32_t x0 = w4(vraw[0][h], w), x1 = w4(vraw[1][h], w);
+        const uint32_t x2 = w4(vraw[2][h], w), x3 = w4(vraw[3][h], w);
+        a0 = prmt(x0, x1, 0x5410); a1 = prmt(x0, x1, 0x7632);
+        a2 = prmt(x2, x3, 0x5410); a3 = prmt(x2, x3, 0x7632);
+      } else {
+        // m-block mb = 2w + e: rows r / r+8 = dims 16r + 4w + 2e + {0 / 1}
+        const int w = mb >> 1, e = mb & 1;
+        const uint32_t x0 = w4(vraw[0][0], w), x1 = w4(vraw[1][0], w);
+        const uint32_t x2 = w4(vraw[2][0], w), x3 = w4(vraw[3][0], w);
+        const uint32_t lo = e ? 0x0602u : 0x0400u, hi = e ? 0x0703u : 0x0501u;
+        a0 = s8x2_to_f16x2(prmt(x0, x1, lo)); a1 = s8x2_to_f16x2(prmt(x0, x1, hi));
+        a2 = s8x2_to_f16x2(prmt(x2, x3, lo)); a3 = s8x2_to_f16x2(prmt(x2, x3, hi));
+      }
+      mma_16816(acc[mb], a0, a1, a2, a3, pb0, pb1);
+    }
+  }
+
+  // ---- merge the warps of this split --------------------------------------
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if (c == 0 && r < GROUP) {
+    sm_m[warp][r] = m_run;
+    sm_l[warp][r] = l_run;
+  }
+#pragma unroll
+  for (int mb = 0; mb < 8; ++mb) {
+    const int d0 = INT8 ? (16 * r + 4 * (mb >> 1) + 2 * (mb & 1))
+                        : (64 * (mb >> 2) + 8 * r + 2 * (mb & 3));
+    if (2 * c < GROUP) {
+      sm_o[warp][2 * c][d0] = acc[mb][0];
+      sm_o[warp][2 * c][d0 + 1] = acc[mb][2];
+    }
+    if (2 * c + 1 < GROUP) {
+      sm_o[warp][2 * c + 1][d0] = acc[mb][1];
+      sm_o[warp][2 * c + 1][d0 + 1] = acc[mb][3];
+    }
+  }
+  __syncthreads();
+
+  const int dim = threadIdx.x;  // 128 threads == head dim
+#pragma unroll
+  for (int hh = 0; hh < GROUP; ++hh) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][hh]);
+    float O = 0.0f, L = 0.0f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) {
+        const float f = exp2f(sm_m[w][hh] - M);  // -inf -> 0
+        O += f * sm_o[w][hh][dim];
+        L += f * sm_l[w][hh];
+      }
+    }
+    if (nsplits == 1) {
+      a.out[((size_t)b * a.num_heads + (size_t)g * GROUP + hh) * kD + dim] =
+          L > 0.0f ? O * (1.0f / L) : 0.0f;
+    } else {
+      const size_t prow = (((size_t)b * Hkv + g) * a.max_splits + split) * GROUP + hh;
+      a.part_o[prow * kD + dim] = O;
+      if (dim == 0) {
+        a.part_ml[prow * 2] = M;
+        a.part_ml[prow * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+// Stitches split partials: rows (b, kv head g, head-in-group hh).  Partial
+// maxima are log2-domain when LOG2, natural otherwise.
+struct CombineArgs {
+  const float* part_o;
+  const float* part_ml;
+  float* out;
+  const int32_t* seq_lens;  // null: every row has fixed_len tokens
+  int fixed_len, cap, split_tokens, max_splits, num_kv_heads, group, head_dim;
+};
+
+template <bool LOG2>
+__global__ void combine_splits_kernel(const CombineArgs a) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int g = h / a.group, hh = h - g * a.group;
+  const int len = a.seq_lens ? clamp_len(a.seq_lens[b], a.cap) : a.fixed_len;
+  const int nsplits = max(1, (len + a.split_tokens - 1) / a.split_tokens);
+  if (nsplits == 1) return;  // the split kernel wrote the output
+  const size_t base = ((size_t)b * a.num_kv_heads + g) * a.max_splits;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplits; ++s)
+    M = fmaxf(M, a.part_ml[((base + s) * a.group + hh) * 2]);
+  float L = 0.0f;
+  for (int s = 0; s < nsplits; ++s) {
+    const float* ml = a.part_ml + ((base + s) * a.group + hh) * 2;
+    const float f = M == -INFINITY ? 0.0f : (LOG2 ? exp2f(ml[0] - M) : expf(ml[0] - M));
+    L += f * ml[1];
+  }
+  const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+  for (int d = threadIdx.x; d < a.head_dim; d += blockDim.x) {
+    float O = 0.0f;
+    for (int s = 0; s < nsplits; ++s) {
+      const size_t prow = (base + s) * a.group + hh;
+      const float m = a.part_ml[prow * 2];
+      const float f = M == -INFINITY ? 0.0f : (LOG2 ? exp2f(m - M) : expf(m - M));
+      O += f * a.part_o[prow * a.head_dim + d];
+    }
+    a.out[((size_t)b * a.num_kv_heads * a.group + h) * a.head_dim + d] = O * inv;
+  }
+}
+
+template __global__ void combine_splits_kernel<true>(const CombineArgs);
+template __global__ void combine_splits_kernel<false>(const CombineArgs);
+
+// ---------------------------------------------------------------------------
+int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
+                        const void* q, const int32_t* seq_lens, const void* new_k,
+                        const void* new_v, float scale, float* out, uint32_t split_pages,
+                        const doe_launch* launch, uint64_t* ws_needed_out) {
+  const uint32_t Hkv = kv->num_kv_heads;
+  const uint32_t group = num_heads / Hkv;
+  const uint32_t tiles_per_page = kv->page_size / 16;
+  uint32_t split_tiles = split_pages ? split_pages * tiles_per_page : 32;
+  if (split_tiles == 0) split_tiles = 1;
+  const uint32_t max_tiles = kv->max_pages_per_seq * tiles_per_page;
+  const uint32_t max_splits = max_tiles == 0 ? 1 : ceil_div(max_tiles, split_tiles);
+  const uint64_t rows = (uint64_t)num_seqs * Hkv * max_splits * group;
+  const uint64_t ws = rows * (kD + 2) * sizeof(float);
+  if (ws_needed_out) {
+    *ws_needed_out = ws;
+    return DOE_OK;
+  }
+  if (ws > 0 && (launch->workspace == nullptr || launch->workspace_bytes < ws)) {
+    set_op_error("doe_paged_decode: workspace of %llu bytes required, %llu given",
+                 (unsigned long long)ws, (unsigned long long)launch->workspace_bytes);
+    return DOE_INVALID_ARGUMENT;
+  }
+  PagedDecodeArgs a;
+  a.q = static_cast<const __half*>(q);
+  a.k_pool = static_cast<const uint8_t*>(kv->k_pool);
+  a.v_pool = static_cast<const uint8_t*>(kv->v_pool);
+  a.k_scale = static_cast<const __half*>(kv->k_scale);
+  a.v_scale = static_cast<const __half*>(kv->v_scale);
+  a.block_table = kv->block_table;
+  a.seq_lens = seq_lens;
+  a.new_k = static_cast<const __half*>(new_k);
+  a.new_v = static_cast<const __half*>(new_v);
+  a.out = out;
+  a.part_o = static_cast<float*>(launch->workspace);
+  a.part_ml = a.part_o + rows * kD;
+  a.status = launch->status;
+  a.num_heads = (int)num_heads;
+  a.num_kv_heads = (int)Hkv;
+  a.num_pages = (int)kv->num_pages;
+  a.page_size = (int)kv->page_size;
+  a.max_pages = (int)kv->max_pages_per_seq;
+  a.split_tiles = (int)split_tiles;
+  a.max_splits = (int)max_splits;
+  a.scale_log2 = scale * kLog2e;
+  cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
+  dim3 grid(max_splits, Hkv, num_seqs), block(kWarps * 32);
+  const bool int8 = kv->kv_dtype == DOE_KV_INT8;
+#define DOE_PD_LAUNCH(I8, G) paged_decode_kernel<I8, G><<<grid, block, 0, st>>>(a)
+  switch (group) {
+    case 1: if (int8) DOE_PD_LAUNCH(true, 1); else DOE_PD_LAUNCH(false, 1); break;
+    case 2: if (int8) DOE_PD_LAUNCH(true, 2); else DOE_PD_LAUNCH(false, 2); break;
+    case 4: if (int8) DOE_PD_LAUNCH(true, 4); else DOE_PD_LAUNCH(false, 4); break;
+    case 8: if (int8) DOE_PD_LAUNCH(true, 8); else DOE_PD_LAUNCH(false, 8); break;
+    default:
+      set_op_error("doe_paged_decode: heads per kv head must be 1, 2, 4 or 8 (got %u)", group);
+      return DOE_UNSUPPORTED;
+  }
+#undef DOE_PD_LAUNCH
+  int rc = cuda_status(cudaGetLastError(), "paged_decode_kernel");
+  if (rc != DOE_OK) return rc;
+  CombineArgs ca;
+  ca.part_o = a.part_o;
+  ca.part_ml = a.part_ml;
+  ca.out = out;
+  ca.seq_lens = seq_lens;
+  ca.fixed_len = 0;
+  ca.cap = a.max_pages * a.page_size;
+  ca.split_tokens = (int)split_tiles * 16;
+  ca.max_splits = (int)max_splits;
+  ca.num_kv_heads = (int)Hkv;
+  ca.group = (int)group;
+  ca.head_dim = kD;
+  combine_splits_kernel<true><<<dim3(num_heads, num_seqs), kD, 0, st>>>(ca);
+  return cuda_status(cudaGetLastError(), "combine_splits_kernel");
+}
+
+}  // namespace doe
+
+namespace doe {
+
+int launch_combine_natural(const float* part_o, const float* part_ml, float* out, int rows,
+                           int fixed_len, int split_tokens, int max_splits, int head_dim,
+                           cudaStream_t st) {
+  CombineArgs ca;
+  ca.part_o = part_o;
+  ca.part_ml = part_ml;
+  ca.out = out;
+  ca.seq_lens = nullptr;
+  ca.fixed_len = fixed_len;
+  ca.cap = fixed_len;
+  ca.split_tokens = split_tokens;
+  ca.max_splits = max_splits;
+  ca.num_kv_heads = rows;
+  ca.group = 1;
+  ca.head_dim = head_dim;
+  const int threads = head_dim >= 256 ? 256 : ((head_dim + 31) / 32) * 32;
+  combine_splits_kernel<false><<<dim3(rows, 1), threads, 0, st>>>(ca);
+  return cuda_status(cudaGetLastError(), "combine_splits_kernel");
+}
+
+}  // namespace doe

@@ -1,0 +1,182 @@
+"""torch-facing wrappers of the operator surface (include/doe_cuda.h).
+
+Each wrapper validates shapes / dtypes, passes raw device pointers and the
+current torch stream to libdoe_cuda.so, and raises DoeError on a non-OK
+status.  Nothing here computes on the host.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from . import _abi as abi
+from .kv import PagedKVCache
+
+_WS: dict[int, torch.Tensor] = {}
+
+
+def workspace(nbytes: int, device=None) -> torch.Tensor:
+    """A cached device scratch buffer of at least nbytes (grown on demand)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=dev)
+        _WS[key] = buf
+    return buf
+
+
+def _launch(ws_bytes: int = 0, status: torch.Tensor | None = None, stream=None, device=None) -> abi.Launch:
+    s = stream if stream is not None else torch.cuda.current_stream(device)
+    ws = workspace(ws_bytes, device) if ws_bytes else None
+    return abi.Launch(s.cuda_stream, ws.data_ptr() if ws is not None else None,
+                      ws.numel() if ws is not None else 0,
+                      status.data_ptr() if status is not None else None)
+
+
+def _need(t: torch.Tensor, dtype, name: str) -> None:
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name} must be a contiguous CUDA {dtype} tensor")
+
+
+def status_word(device=None) -> torch.Tensor:
+    """A zeroed device int32 that kernels OR DOE_DEVICE_ERR_* bits into."""
+    return torch.zeros(1, dtype=torch.int32, device=device or "cuda")
+
+
+def attention_decode_f32(q, k_cache, v_cache, scale: float, out=None, status=None, stream=None):
+    """attention-decode.wgsl: q [H,D], k/v [H,L,D] f32 -> [H,D]."""
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(t, torch.float32, n)
+    H, D = q.shape
+    L = k_cache.shape[1]
+    out = torch.empty_like(q) if out is None else out
+    lib = abi.lib()
+    ws = lib.doe_attention_decode_f32_workspace_bytes(H, D, L)
+    l = _launch(ws, status, stream, q.device)
+    abi.check("doe_attention_decode_f32", lib.doe_attention_decode_f32(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), H, D, L, float(scale),
+        C.byref(l)))
+    return out
+
+
+def attention_online(u: dict, q, k, v, kv_len_buffer=None, page_table=None, out=None, status=None,
+                     stream=None):
+    """attention_head256_f16kv.wgsl semantics: q [query_len,H,D] f32, k/v [pos,Hkv,D] f16|f32."""
+    _need(q, torch.float32, "q")
+    kv_elem = 1 if k.dtype == torch.float32 else 0
+    uni = abi.AttnUniforms(**{**u, "pad": 0})
+    out = torch.zeros_like(q) if out is None else out
+    l = _launch(0, status, stream, q.device)
+    abi.check("doe_attention_online", abi.lib().doe_attention_online(
+        C.byref(uni), q.data_ptr(), k.data_ptr(), v.data_ptr(), kv_elem, out.data_ptr(),
+        kv_len_buffer.data_ptr() if kv_len_buffer is not None else None,
+        page_table.data_ptr() if page_table is not None else None, C.byref(l)))
+    return out
+
+
+def attention_prefill_wgsl(q, k, v, scale: float, out=None, status=None, stream=None):
+    """attention-prefill.wgsl: causal, [H,S,D] f32."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, torch.float32, n)
+    H, S, D = q.shape
+    out = torch.empty_like(q) if out is None else out
+    l = _launch(0, status, stream, q.device)
+    abi.check("doe_attention_prefill_wgsl_f32", abi.lib().doe_attention_prefill_wgsl_f32(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), S, D, H, float(scale), C.byref(l)))
+    return out
+
+
+def stitch(partials, out=None, stream=None):
+    """[rows, shards, D+2] f32 partials -> [rows, D]."""
+    _need(partials, torch.float32, "partials")
+    rows, shards, w = partials.shape
+    out = torch.empty((rows, w - 2), dtype=torch.float32, device=partials.device) if out is None else out
+    l = _launch(0, None, stream, partials.device)
+    abi.check("doe_attention_stitch_f32", abi.lib().doe_attention_stitch_f32(
+        partials.data_ptr(), rows, shards, w - 2, out.data_ptr(), C.byref(l)))
+    return out
+
+
+def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new_v=None, out=None,
+                 split_pages: int = 0, status=None, stream=None):
+    """Batched GQA decode: q [B,H,D] f16, seq_lens [B] int32 -> out [B,H,D] f32.
+
+    With new_k/new_v ([B,Hkv,D] f16) the new token is first written at
+    position seq_lens[b] - 1 (quantised for int8 caches)."""
+    _need(q, torch.float16, "q")
+    _need(seq_lens, torch.int32, "seq_lens")
+    B, H, D = q.shape
+    out = torch.empty((B, H, D), dtype=torch.float32, device=q.device) if out is None else out
+    kv = cache.struct()
+    lib = abi.lib()
+    ws = lib.doe_paged_decode_workspace_bytes(C.byref(kv), B, H, split_pages)
+    l = _launch(ws, status, stream, q.device)
+    abi.check("doe_paged_decode", lib.doe_paged_decode(
+        C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(),
+        new_k.data_ptr() if new_k is not None else None,
+        new_v.data_ptr() if new_v is not None else None, float(scale), out.data_ptr(),
+        split_pages, C.byref(l)))
+    return out
+
+
+def paged_append(cache: PagedKVCache, new_k, new_v, positions, status=None, stream=None):
+    """Write new_k/new_v [B,T,Hkv,D] f16 at positions[b] + t (quantising int8 caches)."""
+    _need(new_k, torch.float16, "new_k")
+    _need(new_v, torch.float16, "new_v")
+    _need(positions, torch.int32, "positions")
+    B, T = new_k.shape[:2]
+    kv = cache.struct()
+    l = _launch(0, status, stream, new_k.device)
+    abi.check("doe_paged_append", abi.lib().doe_paged_append(
+        C.byref(kv), B, T, new_k.data_ptr(), new_v.data_ptr(), positions.data_ptr(), C.byref(l)))
+
+
+def paged_gather(cache: PagedKVCache, seq: int, start: int, length: int, status=None, stream=None):
+    """kv_read: tokens [start, start+length) of one sequence -> (k, v[, k_scale, v_scale])."""
+    shape = (length, cache.num_kv_heads, cache.head_dim)
+    k = torch.empty(shape, dtype=cache.k_pool.dtype, device=cache.k_pool.device)
+    v = torch.empty_like(k)
+    ks = vs = None
+    if cache.kv_dtype == "int8":
+        ks = torch.empty((length, cache.num_kv_heads), dtype=torch.float16, device=k.device)
+        vs = torch.empty_like(ks)
+    kv = cache.struct()
+    l = _launch(0, status, stream, k.device)
+    abi.check("doe_paged_gather", abi.lib().doe_paged_gather(
+        C.byref(kv), seq, start, length, k.data_ptr(), v.data_ptr(),
+        ks.data_ptr() if ks is not None else None, vs.data_ptr() if vs is not None else None,
+        C.byref(l)))
+    return (k, v) if ks is None else (k, v, ks, vs)
+
+
+def kv_write_dense(k_proj, v_proj, k_cache, v_cache, positions, status=None, stream=None):
+    """proj [heads, D], caches [heads, max_seq_len, D] (f16|f32), positions u32 [1|heads]."""
+    heads, max_len, D = k_cache.shape
+    eb = k_cache.element_size()
+    l = _launch(0, status, stream, k_cache.device)
+    abi.check("doe_kv_write_dense", abi.lib().doe_kv_write_dense(
+        k_proj.data_ptr(), v_proj.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+        positions.data_ptr(), positions.numel(), heads, max_len, D, eb, C.byref(l)))
+
+
+def kv_read_dense(k_cache, v_cache, read_start: int, read_len: int, status=None, stream=None):
+    heads, max_len, D = k_cache.shape
+    ko = torch.empty((heads, read_len, D), dtype=k_cache.dtype, device=k_cache.device)
+    vo = torch.empty_like(ko)
+    l = _launch(0, status, stream, k_cache.device)
+    abi.check("doe_kv_read_dense", abi.lib().doe_kv_read_dense(
+        k_cache.data_ptr(), v_cache.data_ptr(), ko.data_ptr(), vo.data_ptr(), heads, read_start,
+        read_len, max_len, D, k_cache.element_size(), C.byref(l)))
+    return ko, vo
+
+
+def rope(qk, freq_cis, position_offset: int = 0, stream=None):
+    """rope.wgsl in place on qk [S,H,D] f32."""
+    _need(qk, torch.float32, "qk")
+    S, H, D = qk.shape
+    l = _launch(0, None, stream, qk.device)
+    abi.check("doe_rope_f32", abi.lib().doe_rope_f32(
+        qk.data_ptr(), freq_cis.data_ptr(), S, H, D, position_offset, C.byref(l)))
+    return qk

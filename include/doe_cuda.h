@@ -1,0 +1,309 @@
+/*
+ * doe_cuda.h -- C ABI of libdoe_cuda.so, the sm_100a attention / KV-cache
+ * backend for Doe (doerun/doe).
+ *
+ * Plain C types only: pointers, sizes and integer status codes.  Device
+ * pointers are CUDA global-memory addresses; `stream` is a cudaStream_t
+ * passed as void*.  Every entry point returns a doe_status; none of them
+ * falls back to the host when a kernel cannot run.
+ *
+ * Two surfaces share the same kernels:
+ *   1. the backend surface (doe_cuda_open ... doe_cuda_flush): a device,
+ *      a stream and a handle -> buffer map driven by Doe's command model;
+ *   2. the operator surface (doe_attention_*, doe_paged_*, doe_kv_*): direct
+ *      launches on caller-owned device memory, which is what an ONNX Runtime
+ *      plugin EP's Compute callback binds to.
+ *
+ * Reference citations are paths inside the doerun/doe tree.
+ */
+#ifndef DOE_CUDA_H
+#define DOE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DOE_CUDA_ABI_VERSION 1
+
+/* Status codes.  OK/UNSUPPORTED/ERROR mirror NativeExecutionStatus
+ * (runtime/zig/src/core/abi/wgpu_execution_types.zig:1-5); the rest refine
+ * ERROR the way the Zig backends return distinct error-union members.      */
+typedef enum doe_status {
+  DOE_OK = 0,
+  DOE_UNSUPPORTED = 1,      /* unknown kernel / op, or unsupported shape   */
+  DOE_ERROR = 2,            /* generic failure                              */
+  DOE_INVALID_ARGUMENT = 3, /* null pointer, size mismatch, bad uniform     */
+  DOE_OUT_OF_RANGE = 4,     /* position / page outside the cache            */
+  DOE_NOT_FOUND = 5,        /* unknown buffer handle                        */
+  DOE_CUDA_ERROR = 6,       /* a CUDA runtime call failed                   */
+  DOE_NO_DEVICE = 7         /* no CUDA device (or ordinal out of range)     */
+} doe_status;
+
+/* Device-side error bits that kernels OR into a launch's status word.      */
+#define DOE_DEVICE_ERR_PAGE 0x1     /* block-table entry outside the pool   */
+#define DOE_DEVICE_ERR_POSITION 0x2 /* write position >= cache capacity     */
+#define DOE_DEVICE_ERR_LENGTH 0x4   /* sequence longer than its block table */
+
+/* KV element types of a paged cache.                                       */
+#define DOE_KV_F16 0u
+#define DOE_KV_INT8 1u /* int8 symmetric + f16 scale per (token, kv head)   */
+
+/* Launch context of the operator surface.  `workspace` is device scratch
+ * of at least the op's *_workspace_bytes(); `status` is an optional device
+ * int32 that kernels OR DOE_DEVICE_ERR_* bits into (read it after the stream
+ * has finished).                                                           */
+typedef struct doe_launch {
+  void* stream;
+  void* workspace;
+  uint64_t workspace_bytes;
+  int32_t* status;
+} doe_launch;
+
+/* ======================================================================== */
+/* Library                                                                  */
+/* ======================================================================== */
+int doe_cuda_abi_version(void);
+int doe_cuda_device_count(int* count);
+/* Last error text of the calling thread for the operator surface.          */
+const char* doe_cuda_op_last_error(void);
+
+/* ======================================================================== */
+/* Backend surface -- replaces the BackendVTable slots of a device backend  */
+/* (runtime/zig/src/backend/backend_iface.zig:13-31).                       */
+/* ======================================================================== */
+typedef struct doe_cuda_ctx doe_cuda_ctx;
+
+/* Buffer binding of a kernel_dispatch command
+ * (runtime/zig/src/model_compute_types.zig:19-35 KernelBinding).           */
+typedef struct doe_binding {
+  uint32_t binding;
+  uint32_t group;
+  uint64_t handle;
+  uint64_t offset;
+  uint64_t size; /* 0 or UINT64_MAX = whole buffer from offset */
+  uint32_t buffer_type;
+  uint32_t reserved;
+} doe_binding;
+
+/* NativeExecutionResult (runtime/zig/src/core/abi/wgpu_execution_types.zig:7-17). */
+typedef struct doe_exec_result {
+  int32_t status;
+  uint32_t dispatch_count;
+  uint64_t setup_ns;
+  uint64_t encode_ns;
+  uint64_t submit_wait_ns;
+  uint64_t gpu_timestamp_ns;
+  uint32_t gpu_timestamp_attempted;
+  uint32_t gpu_timestamp_valid;
+} doe_exec_result;
+
+/* init_backend arm (runtime/zig/src/backend/backend_registry.zig:12-43).   */
+int doe_cuda_open(int ordinal, doe_cuda_ctx** out);
+/* deinit (backend_iface.zig:14).                                           */
+int doe_cuda_close(doe_cuda_ctx* ctx);
+const char* doe_cuda_last_error(const doe_cuda_ctx* ctx);
+/* The backend's stream (cudaStream_t), for callers that time or order work. */
+void* doe_cuda_stream(doe_cuda_ctx* ctx);
+
+/* Handle -> device buffer map (runtime/zig/src/backend/vulkan/vk_resources.zig:143-171):
+ * buffers are created on first use and grown (contents kept) when a larger
+ * size is requested.                                                       */
+int doe_cuda_buffer_ensure(doe_cuda_ctx* ctx, uint64_t handle, uint64_t bytes);
+/* execute_buffer_write_bytes (backend_iface.zig:16): host bytes go through
+ * a pinned staging area and an async copy on the backend stream.           */
+int doe_cuda_buffer_write(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset,
+                          const void* data, uint64_t size);
+/* capture_buffer (backend_iface.zig:30): waits for the stream, then copies
+ * device bytes into caller memory.                                         */
+int doe_cuda_buffer_read(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset,
+                         void* dst, uint64_t size);
+int doe_cuda_buffer_release(doe_cuda_ctx* ctx, uint64_t handle);
+int doe_cuda_buffer_size(doe_cuda_ctx* ctx, uint64_t handle, uint64_t* bytes);
+int doe_cuda_buffer_device_ptr(doe_cuda_ctx* ctx, uint64_t handle, void** out);
+
+/* execute_command(kernel_dispatch) (backend_iface.zig:15;
+ * runtime/zig/src/backend/vulkan/backend_execute.zig:281-317).  `kernel` is a
+ * WGSL kernel file name Doe's command streams use ("attention-decode.wgsl",
+ * "attention-prefill.wgsl", "attention_head256_f16kv.wgsl",
+ * "attention_head512_f16kv.wgsl", "rope.wgsl") or an exec-v1 op name
+ * (runtime/zig/src/doe_wgsl/emit_csl_exec_v1.zig:113-180: "attention",
+ * "attention_sliding", "attention_prefill", "kv_write", "kv_write_shared",
+ * "kv_read", "rope").  Unknown names return DOE_UNSUPPORTED with a message;
+ * nothing runs on the host instead.                                        */
+int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel,
+                      const char* entry_point, uint32_t x, uint32_t y,
+                      uint32_t z, const doe_binding* bindings,
+                      uint32_t num_bindings, doe_exec_result* result);
+/* 1 if `kernel` names a dispatchable kernel / op, else 0.                  */
+int doe_cuda_kernel_supported(const char* kernel);
+/* prewarm_kernel_dispatch (backend_iface.zig:23-29).                       */
+int doe_cuda_prewarm_kernel(doe_cuda_ctx* ctx, const char* kernel);
+/* prewarm_upload_path (backend_iface.zig:22): sizes the pinned staging area. */
+int doe_cuda_prewarm_upload(doe_cuda_ctx* ctx, uint64_t max_upload_bytes);
+/* set_queue_sync_mode (backend_iface.zig:19): 0 deferred, 1 per command.   */
+int doe_cuda_set_queue_sync_mode(doe_cuda_ctx* ctx, int per_command);
+/* set_gpu_timestamp_mode (backend_iface.zig:20): 0 off, 1 on.              */
+int doe_cuda_set_gpu_timestamp_mode(doe_cuda_ctx* ctx, int on);
+/* flush_queue (backend_iface.zig:21): waits for the stream; returns the
+ * wait in ns and turns device-side error bits into a status.               */
+int doe_cuda_flush(doe_cuda_ctx* ctx, uint64_t* wait_ns);
+
+/* ======================================================================== */
+/* Operator surface                                                          */
+/* ======================================================================== */
+
+/* attention-decode.wgsl (bench/inference-pipeline/kernels/attention-decode.wgsl:46-136):
+ * q [H,D] f32, k_cache/v_cache [H,kv_len,D] f32, out [H,D] f32.  Split-K over
+ * kv_len with a combine kernel; no kv_len limit (the WGSL kernel stops at
+ * 2048, its workgroup score array).                                         */
+uint64_t doe_attention_decode_f32_workspace_bytes(uint32_t num_heads,
+                                                  uint32_t head_dim,
+                                                  uint32_t kv_len);
+int doe_attention_decode_f32(const float* q, const float* k_cache,
+                             const float* v_cache, float* out,
+                             uint32_t num_heads, uint32_t head_dim,
+                             uint32_t kv_len, float scale,
+                             const doe_launch* launch);
+
+/* Uniform block of attention_head256_f16kv.wgsl
+ * (runtime/zig/tests/tsir/real/attention_head256_f16kv/attention_head256_f16kv.wgsl:14-30). */
+typedef struct doe_attn_uniforms {
+  uint32_t num_heads;
+  uint32_t num_kv_heads;
+  uint32_t head_dim;
+  uint32_t seq_len;
+  uint32_t query_len;
+  float scale;
+  uint32_t is_causal;
+  uint32_t start_pos;
+  float attn_softcap;
+  uint32_t sliding_window;
+  uint32_t kv_len_source; /* 0: seq_len from the uniform, else kv_len_buffer[0] */
+  uint32_t kv_start;
+  uint32_t page_size;
+  uint32_t kv_layout; /* 0 dense, 1 sliding ring, 2 paged through page_table */
+  uint32_t pad;
+} doe_attn_uniforms;
+
+/* attention_head256_f16kv.wgsl main (…:72-269) for any head_dim <= 512:
+ * q/out [query_len, H, D] f32, k/v [pos, Hkv, D] of `kv_elem` (0 = f16,
+ * 1 = f32), optional kv_len_buffer / page_table device arrays.             */
+int doe_attention_online(const doe_attn_uniforms* u, const float* q,
+                         const void* k, const void* v, uint32_t kv_elem,
+                         float* out, const uint32_t* kv_len_buffer,
+                         const uint32_t* page_table, const doe_launch* launch);
+
+/* attention-prefill.wgsl (bench/inference-pipeline/kernels/attention-prefill.wgsl:19-112):
+ * causal, q/k/v/out [H,S,D] f32.                                            */
+int doe_attention_prefill_wgsl_f32(const float* q, const float* k,
+                                   const float* v, float* out, uint32_t seq_len,
+                                   uint32_t head_dim, uint32_t num_heads,
+                                   float scale, const doe_launch* launch);
+
+/* stitch_kv_axis_sharded_partials (bench/tools/attention_kv_axis_sharded_stitch.py:46-90):
+ * partials [rows, num_shards, D+2] f32 rows [O_unnorm[D], local_max,
+ * local_sum] -> out [rows, D].                                             */
+int doe_attention_stitch_f32(const float* partials, uint32_t rows,
+                             uint32_t num_shards, uint32_t head_dim, float* out,
+                             const doe_launch* launch);
+
+/* A paged KV cache: pools [num_pages * page_size, num_kv_heads, head_dim]
+ * (attention_head256_f16kv.wgsl:51-63 kv_layout 2, row = page_table[p /
+ * page] * page + p % page), one block-table row per sequence.  int8 pools
+ * carry f16 scales laid out [num_pages, num_kv_heads, page_size].          */
+typedef struct doe_paged_kv {
+  void* k_pool;
+  void* v_pool;
+  void* k_scale;
+  void* v_scale;
+  uint32_t kv_dtype; /* DOE_KV_F16 or DOE_KV_INT8 */
+  uint32_t num_pages;
+  uint32_t page_size; /* a multiple of 16 */
+  uint32_t num_kv_heads;
+  uint32_t head_dim;
+  uint32_t max_pages_per_seq;
+  const int32_t* block_table; /* [num_seqs, max_pages_per_seq] device int32 */
+} doe_paged_kv;
+
+/* Batched GQA decode over a paged cache (the head256 online softmax with one
+ * query per sequence, generalised to per-sequence block tables).  q [B,H,D]
+ * f16, seq_lens [B] device int32 = tokens to attend (after the append),
+ * out [B,H,D] f32.  When new_k/new_v ([B,Hkv,D] f16) are given, the kernel
+ * first writes them at position seq_lens[b] - 1 (quantising for int8 pools):
+ * the fused append + attend step.  split_pages = 0 picks a split size.     */
+uint64_t doe_paged_decode_workspace_bytes(const doe_paged_kv* kv,
+                                          uint32_t num_seqs, uint32_t num_heads,
+                                          uint32_t split_pages);
+int doe_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs,
+                     uint32_t num_heads, const void* q, const int32_t* seq_lens,
+                     const void* new_k, const void* new_v, float scale,
+                     float* out, uint32_t split_pages, const doe_launch* launch);
+
+/* kv_write generalised to the paged cache (runtime/zig/src/tsir/emit_kernel_body.zig:620-690;
+ * runtime/zig/src/tsir/emit_kernel_body_kv.zig:30-102): new_k/new_v
+ * [B, n_tokens, Hkv, D] f16 written at positions[b] + t.  int8 pools are
+ * quantised per (token, kv head): scale = f16(absmax/127),
+ * q = clamp(rint(x/scale), -127, 127).  Unmapped pages set
+ * DOE_DEVICE_ERR_PAGE and skip the row.                                    */
+int doe_paged_append(const doe_paged_kv* kv, uint32_t num_seqs,
+                     uint32_t n_tokens, const void* new_k, const void* new_v,
+                     const int32_t* positions, const doe_launch* launch);
+
+/* kv_read over the paged cache (runtime/zig/src/tsir/emit_kernel_body.zig:692-760):
+ * copies tokens [start, start+len) of sequence `seq` into k_out/v_out
+ * [len, Hkv, D] (element type of the pool); int8 pools also copy scales into
+ * k_scale_out/v_scale_out [len, Hkv] when given.                           */
+int doe_paged_gather(const doe_paged_kv* kv, uint32_t seq, uint32_t start,
+                     uint32_t len, void* k_out, void* v_out, void* k_scale_out,
+                     void* v_scale_out, const doe_launch* launch);
+
+/* Dense per-head kv_write / kv_read, the reference's own form
+ * (emit_kernel_body.zig:620-760; CPU semantics
+ * bench/tools/run_csl_webgpu_emulator.mjs:615-644).  proj [heads, D],
+ * caches [heads, max_seq_len, D], elem_bytes 2 or 4.  positions is a device
+ * u32 array of 1 (shared) or `heads` entries; position >= max_seq_len sets
+ * DOE_DEVICE_ERR_POSITION and writes nothing for that head.              */
+int doe_kv_write_dense(const void* k_proj, const void* v_proj, void* k_cache,
+                       void* v_cache, const uint32_t* positions,
+                       uint32_t num_positions, uint32_t heads,
+                       uint32_t max_seq_len, uint32_t head_dim,
+                       uint32_t elem_bytes, const doe_launch* launch);
+int doe_kv_read_dense(const void* k_cache, const void* v_cache, void* k_out,
+                      void* v_out, uint32_t heads, uint32_t read_start,
+                      uint32_t read_len, uint32_t max_seq_len,
+                      uint32_t head_dim, uint32_t elem_bytes,
+                      const doe_launch* launch);
+
+/* rope.wgsl (bench/inference-pipeline/kernels/rope.wgsl:12-35): qk [S,H,D]
+ * f32 rotated in place with freq_cis [(pos*D/2 + i)*2 + {cos, sin}].        */
+int doe_rope_f32(float* qk, const float* freq_cis, uint32_t seq_len,
+                 uint32_t num_heads, uint32_t head_dim,
+                 uint32_t position_offset, const doe_launch* launch);
+
+/* ======================================================================== */
+/* Host KV page pool -- hands out physical pages and keeps the per-sequence  */
+/* block tables that the paged kernels read (the reference takes one         */
+/* page_table binding per dispatch, attention_head256_f16kv.wgsl:38).       */
+/* ======================================================================== */
+typedef struct doe_kv_pool doe_kv_pool;
+int doe_kv_pool_create(uint32_t num_pages, uint32_t page_size,
+                       uint32_t max_seqs, uint32_t max_pages_per_seq,
+                       doe_kv_pool** out);
+int doe_kv_pool_destroy(doe_kv_pool* pool);
+/* Make sequence `seq` able to hold `tokens` tokens (allocates pages).      */
+int doe_kv_pool_reserve(doe_kv_pool* pool, uint32_t seq, uint32_t tokens);
+int doe_kv_pool_release(doe_kv_pool* pool, uint32_t seq);
+int doe_kv_pool_free_pages(const doe_kv_pool* pool, uint32_t* out);
+int doe_kv_pool_seq_pages(const doe_kv_pool* pool, uint32_t seq, uint32_t* out);
+/* Writes the [max_seqs, max_pages_per_seq] int32 table (-1 = unmapped).    */
+int doe_kv_pool_block_table(const doe_kv_pool* pool, int32_t* out,
+                            uint64_t out_entries);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DOE_CUDA_H */

@@ -368,10 +368,19 @@ int doe_oracle_stitch_partials_f32(const float* partials, uint32_t num_shards,
 typedef struct kv_rows {
   uint32_t dtype; /* 0 f16, 1 int8 with per-(row, head) f16 scale */
   const void* base;
-  const uint16_t* scale;
+  const uint16_t* scale; /* [num_pages, num_kv_heads, page_size] */
   uint32_t num_kv_heads;
   uint32_t head_dim;
+  uint32_t page_size;
 } kv_rows;
+
+/* Scale of physical row `phys`, kv head `kvh`: page-blocked so the 16 (or
+ * page_size) tokens of one page and head sit next to each other.          */
+static uint64_t scale_index(uint64_t phys, uint32_t kvh, uint32_t num_kv_heads,
+                            uint32_t page_size) {
+  uint64_t page = phys / page_size, in_page = phys % page_size;
+  return (page * num_kv_heads + kvh) * page_size + in_page;
+}
 
 static void load_row(const kv_rows* s, uint64_t phys, uint32_t kvh, float* dst) {
   uint64_t off = (phys * s->num_kv_heads + kvh) * s->head_dim;
@@ -380,7 +389,7 @@ static void load_row(const kv_rows* s, uint64_t phys, uint32_t kvh, float* dst) 
     for (uint32_t d = 0; d < s->head_dim; ++d) dst[d] = doe_oracle_h2f(src[d]);
   } else {
     const int8_t* src = (const int8_t*)s->base + off;
-    float sc = doe_oracle_h2f(s->scale[phys * s->num_kv_heads + kvh]);
+    float sc = doe_oracle_h2f(s->scale[scale_index(phys, kvh, s->num_kv_heads, s->page_size)]);
     for (uint32_t d = 0; d < s->head_dim; ++d) dst[d] = (float)src[d] * sc;
   }
 }
@@ -494,8 +503,8 @@ int doe_oracle_attention_online_f16kv(const doe_oracle_attn_uniforms* u,
   const uint32_t H = u->num_heads, D = u->head_dim;
   const uint32_t heads_per_kv = u->num_heads / u->num_kv_heads;
   const uint32_t seq_len = u->kv_len_source == 0 ? u->seq_len : kv_len_buffer[0];
-  kv_rows ks = {0, k, NULL, u->num_kv_heads, D};
-  kv_rows vs = {0, v, NULL, u->num_kv_heads, D};
+  kv_rows ks = {0, k, NULL, u->num_kv_heads, D, 1};
+  kv_rows vs = {0, v, NULL, u->num_kv_heads, D, 1};
   single_table_ctx pctx = {u, page_table};
   int rc = DOE_ORACLE_OK;
   set_threads(threads);
@@ -564,8 +573,8 @@ int doe_oracle_paged_decode(uint32_t num_seqs, uint32_t num_heads,
     return DOE_ORACLE_EINVAL;
   if (kv_dtype > 1 || (kv_dtype == 1 && (!k_scale || !v_scale))) return DOE_ORACLE_EINVAL;
   const uint32_t H = num_heads, D = head_dim, group = num_heads / num_kv_heads;
-  kv_rows ks = {kv_dtype, k_pool, k_scale, num_kv_heads, D};
-  kv_rows vs = {kv_dtype, v_pool, v_scale, num_kv_heads, D};
+  kv_rows ks = {kv_dtype, k_pool, k_scale, num_kv_heads, D, page_size};
+  kv_rows vs = {kv_dtype, v_pool, v_scale, num_kv_heads, D, page_size};
   int rc = DOE_ORACLE_OK;
   set_threads(threads);
 #pragma omp parallel for collapse(2) schedule(dynamic, 1)
@@ -697,12 +706,15 @@ int doe_oracle_paged_append(uint32_t num_seqs, uint32_t n_tokens,
         memcpy((uint16_t*)k_pool + phys * row, sk, row * 2);
         memcpy((uint16_t*)v_pool + phys * row, sv, row * 2);
       } else {
-        doe_oracle_quantize_rows_int8(sk, num_kv_heads, head_dim,
-                                      (int8_t*)k_pool + phys * row,
-                                      k_scale + phys * num_kv_heads);
-        doe_oracle_quantize_rows_int8(sv, num_kv_heads, head_dim,
-                                      (int8_t*)v_pool + phys * row,
-                                      v_scale + phys * num_kv_heads);
+        for (uint32_t h = 0; h < num_kv_heads; ++h) {
+          uint64_t si = scale_index(phys, h, num_kv_heads, page_size);
+          doe_oracle_quantize_rows_int8(sk + (uint64_t)h * head_dim, 1, head_dim,
+                                        (int8_t*)k_pool + phys * row + (uint64_t)h * head_dim,
+                                        k_scale + si);
+          doe_oracle_quantize_rows_int8(sv + (uint64_t)h * head_dim, 1, head_dim,
+                                        (int8_t*)v_pool + phys * row + (uint64_t)h * head_dim,
+                                        v_scale + si);
+        }
       }
     }
   }

@@ -99,7 +99,8 @@ int doe_oracle_attention_online_f16kv(const doe_oracle_attn_uniforms* u,
 /* ---- batched paged decode (per-sequence block tables) ------------------ */
 /* Q [B,H,D] f16; pools [num_pages*page_size, Hkv, D]; block_table [B,max_pages]
  * int32; kv_lens [B] = tokens to attend; out [B,H,D] f32.  kv_dtype 0 = f16
- * pools (scales ignored), 1 = int8 pools with f16 scales [pool_tokens, Hkv].   */
+ * pools (scales ignored), 1 = int8 pools with f16 scales laid out
+ * [num_pages, Hkv, page_size] (page-blocked per token and kv head).          */
 int doe_oracle_paged_decode(uint32_t num_seqs, uint32_t num_heads,
                             uint32_t num_kv_heads, uint32_t head_dim,
                             uint32_t page_size, uint32_t num_pages,

@@ -230,7 +230,7 @@ def test_int8_paged_decode_equals_f16_decode_on_dequantised_cache():
     table, num_pages = _paged_setup(rng, B, Hkv, D, page, lens)
     k8 = np.zeros((num_pages * page, Hkv, D), np.int8)
     v8 = np.zeros_like(k8)
-    ks = np.zeros((num_pages * page, Hkv), np.uint16)
+    ks = np.zeros((num_pages, Hkv, page), np.uint16)
     vs = np.zeros_like(ks)
     for b in range(B):
         L = int(lens[b])
@@ -241,8 +241,11 @@ def test_int8_paged_decode_equals_f16_decode_on_dequantised_cache():
     q = rng.standard_normal((B, H, D)).astype(np.float16).view(np.uint16)
     out = oracle.paged_decode(q, k8, v8, table, lens, 0.2, page_size=page, k_scale=ks, v_scale=vs)
     # dequantise by hand, then run the f16-free two-pass oracle row by row
-    kd = k8.astype(np.float32) * oracle.h2f(ks)[..., None]
-    vd = v8.astype(np.float32) * oracle.h2f(vs)[..., None]
+    # page-blocked scales [num_pages, Hkv, page] -> per physical row [rows, Hkv]
+    ksr = oracle.h2f(ks).transpose(0, 2, 1).reshape(num_pages * page, Hkv)
+    vsr = oracle.h2f(vs).transpose(0, 2, 1).reshape(num_pages * page, Hkv)
+    kd = k8.astype(np.float32) * ksr[..., None]
+    vd = v8.astype(np.float32) * vsr[..., None]
     for b in range(B):
         L = int(lens[b])
         rows = np.array([table[b, p // page] * page + p % page for p in range(L)])
