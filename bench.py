@@ -58,47 +58,61 @@ def profiled_traffic() -> dict:
 
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled (NVML, ~2 ms) during a timed region."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown",
+               0x4: "sw_power_cap"}
 
     def __init__(self, index: int):
+        import threading
+
         self.index = index
-        self.proc = None
-        self.path = Path(f"/tmp/doe_bench_clocks_{os.getpid()}.csv")
+        self.samples: list[tuple[float, float, int]] = []
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
+
+    def _run(self):
+        nv = self._nvml
+        h = nv.nvmlDeviceGetHandleByIndex(self.index)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), float(mx), int(reasons)))
+            except Exception:
+                pass
+            self._stop.wait(0.002)
 
     def start(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+        except Exception:
+            self._nvml = None
+            return
+        self._thread = threading.Thread(target=self._run, daemon=True)
+        self._thread.start()
 
     def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        rows = []
-        for line in self.path.read_text().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
-        self.path.unlink(missing_ok=True)
-        if not rows:
+        if self._thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
+        self._stop.set()
+        self._thread.join(timeout=5)
+        if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        sm = [x[0] for x in self.samples]
+        bits = 0
+        for x in self.samples:
+            bits |= x[2]
+        reasons = sorted(n for b, n in self.REASONS.items() if bits & b)
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(x[1] for x in self.samples),
+                "reasons": reasons, "samples": len(self.samples), "source": "nvml"}
 
 
 # ---------------------------------------------------------------------------
@@ -183,18 +197,18 @@ def build_paged(w, fill_seed):
     return cache, dev
 
 
-def paged_step_fn(w, cache, dev):
+def paged_step_fn(w, cache, dev, split_pages=0):
     from doe_b200 import ops
 
     def step():
         ops.paged_decode(cache, dev["q"], dev["lens"], w.scale, new_k=dev["nk"], new_v=dev["nv"],
-                         out=dev["out"], status=dev["status"])
+                         out=dev["out"], status=dev["status"], split_pages=split_pages)
     return step
 
 
-def measure_paged(w, fill_seed, steps, warmup, world, pk):
+def measure_paged(w, fill_seed, steps, warmup, world, pk, split_pages=0):
     cache, dev = build_paged(w, fill_seed)
-    step = paged_step_fn(w, cache, dev)
+    step = paged_step_fn(w, cache, dev, split_pages)
     total, each = time_steps(step, steps, warmup, world)
     total, kern = max_over_ranks(world, [total, float(np.mean(each))])
     assert int(dev["status"].item()) == 0, f"device status {int(dev['status'].item()):#x}"
@@ -251,6 +265,9 @@ def measure_f32(steps, warmup, world, pk):
     times = []
     for i in range(warmup + steps):
         flush.fill_(i & 0xff)
+        # keep the GPU busy while the host enqueues the timed launches, so the
+        # events bracket device time rather than host launch latency
+        torch.cuda._sleep(200_000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         ops.attention_decode_f32(q, k, v, d.scale, out=out)
@@ -261,6 +278,43 @@ def measure_f32(steps, warmup, world, pk):
     ms, = max_over_ranks(world, [float(np.mean(times))])
     return {"us_per_step": ms * 1e3, "gbs": world * d.bytes_per_step / (ms / 1e3) / 1e9,
             "bytes_per_step": d.bytes_per_step, "l2": "flushed (256 MB write) between steps"}
+
+
+def measure_prefill(steps, warmup, world, pk):
+    """Config 2: causal prefill (tcgen05) incl. the fused paged KV-cache write."""
+    import torch
+
+    from doe_b200 import ops, workloads
+    from doe_b200.kv import PagedKVCache
+
+    w = workloads.prefill_f16()
+    S = w.q.shape[0]
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    q, k, v = t(w.q), t(w.k), t(w.v)
+    out = torch.empty((S, w.q.shape[1], 128), dtype=torch.float32, device="cuda")
+    cache = PagedKVCache(num_pages=S // 16, page_size=16, num_kv_heads=w.k.shape[1], head_dim=128,
+                         block_table=np.arange(S // 16, dtype=np.int32)[None])
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    times = []
+    for i in range(warmup + steps):
+        flush.fill_(i & 0xff)  # 48 MB of inputs + outputs would otherwise stay in L2
+        torch.cuda._sleep(200_000)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        ops.attention_prefill_f16(q, k, v, w.scale, cache=cache, out=out, status=status)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= warmup:
+            times.append(a.elapsed_time(b))
+    assert int(status.item()) == 0, f"prefill status {int(status.item()):#x}"
+    ms, = max_over_ranks(world, [float(np.mean(times))])
+    tflops = w.flops / (ms / 1e3) / 1e12
+    return {"config": "config 2: causal prefill S 2048, 32 heads, D 128, f16 in / f32 acc, seed 1, "
+                      "+ paged KV-cache write", "ms": ms, "tflops": tflops * world,
+            "frac_of_dense_peak": tflops / pk["bf16_tflops"], "flops": w.flops,
+            "peak_tflops": pk["bf16_tflops"], "peak_note": "measured dense bf16 burst (f16 runs at the same rate)",
+            "l2": "flushed (256 MB write) between steps"}
 
 
 def measure_e2e(w, cache, steps, warmup, world):
@@ -428,6 +482,12 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8"], default="all",
+                    help="time one workload only (no e2e or CPU leg): headline = config 3")
+    ap.add_argument("--split-pages", type=int, default=0,
+                    help="pages per split of the paged decode (0 = the library's choice)")
+    ap.add_argument("--seqs", type=int, default=0,
+                    help="override the number of sequences (smaller cases for ncu captures)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -440,10 +500,27 @@ def main():
     pk = peaks()
     from doe_b200 import workloads
 
-    w = workloads.paged_f16()
+    if args.only in ("prefill", "f32", "int8"):
+        if args.only == "prefill":
+            r = measure_prefill(args.steps, args.warmup, world, pk)
+        elif args.only == "f32":
+            r = measure_f32(args.steps, args.warmup, world, pk)
+        else:
+            w4 = workloads.paged_int8(num_seqs=args.seqs) if args.seqs else workloads.paged_int8()
+            r, _, _ = measure_paged(w4, 3, args.steps, args.warmup, world, pk, args.split_pages)
+        if rank == 0:
+            print(json.dumps({"only": args.only, **r}))
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+    w = workloads.paged_f16(num_seqs=args.seqs) if args.seqs else workloads.paged_f16()
+    if args.only == "headline":
+        args.no_extras = args.no_cpu = True
     clocks = ClockSampler(local)
     clocks.start()
-    head, cache, dev = measure_paged(w, 2, args.steps, args.warmup, world, pk)
+    head, cache, dev = measure_paged(w, 2, args.steps, args.warmup, world, pk, args.split_pages)
     clk = clocks.stop()
     del cache, dev
     torch.cuda.empty_cache()
@@ -462,10 +539,16 @@ def main():
         extras["int8_chunk_append"] = {"config": "config 4b: 32 x 512 tokens quantised into the paged cache",
                                        **ca}
         extras["f32_decode"] = {"config": "config 1: 8 heads, D 64, 512 tokens, f32", **measure_f32(20, 5, world, pk)}
+        try:
+            extras["prefill"] = measure_prefill(10, 3, world, pk)
+        except Exception as e:  # reported, never hidden
+            extras["prefill"] = {"error": str(e)[:300]}
 
-    cache, dev = build_paged(w, 2)
-    e2e = measure_e2e(w, cache, max(5, args.steps // 2), 2, world)
-    del cache, dev
+    e2e = None
+    if args.only == "all":
+        cache, dev = build_paged(w, 2)
+        e2e = measure_e2e(w, cache, max(5, args.steps // 2), 2, world)
+        del cache, dev
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -474,7 +557,7 @@ def main():
     traffic = profiled_traffic().get("paged_decode_f16")
     roof = {"bound": "hbm", "achieved": head["kernel_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
             "frac": head["frac"], "traffic": traffic,
-            "kernel": "paged_decode_kernel<f16,4> + combine_splits_kernel (one doe_paged_decode call)",
+            "kernel": "paged_decode_kernel<f16,4> (one launch per doe_paged_decode call, split stitch fused)",
             "peak_source": pk["source"] + " (MEASURED_PEAKS.json hbm_gbs, burst copy)",
             "algorithmic_bytes_per_launch": head["bytes_per_step"]["total"]}
     if rank == 0:
@@ -485,7 +568,7 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded)",
             "config": config_block(w), "tokens_per_s": head["tokens_per_s"],
             "roofline": roof, "clocks": clk, "e2e": e2e,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": args.steps,  # one paged_decode_kernel per step (plus a 2 KB counter memset)
             "cpu_baseline": cpu, **extras,
         }
         print(json.dumps(line))

@@ -29,6 +29,7 @@ STATUS_NAMES = {
 DOE_DEVICE_ERR_PAGE = 0x1
 DOE_DEVICE_ERR_POSITION = 0x2
 DOE_DEVICE_ERR_LENGTH = 0x4
+DOE_DEVICE_ERR_TIMEOUT = 0x8
 
 DOE_KV_F16 = 0
 DOE_KV_INT8 = 1
@@ -107,6 +108,8 @@ SIGNATURES = {
     "doe_attention_online": (_I, [C.POINTER(AttnUniforms), _P, _P, _P, _U32, _P, _P, _P, _LP]),
     "doe_attention_prefill_wgsl_f32": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _F, _LP]),
     "doe_attention_stitch_f32": (_I, [_P, _U32, _U32, _U32, _P, _LP]),
+    "doe_attention_prefill_f16": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _F, _U32,
+                                       C.POINTER(PagedKV), _U32, _U32, _LP]),
     "doe_paged_decode_workspace_bytes": (_U64, [C.POINTER(PagedKV), _U32, _U32, _U32]),
     "doe_paged_decode": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _P, _F, _P, _U32, _LP]),
     "doe_paged_append": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _LP]),

@@ -57,6 +57,10 @@ int launch_kv_read_dense(const void* k_cache, const void* v_cache, void* k_out, 
                          const doe_launch* launch);
 int launch_stitch(const float* partials, uint32_t rows, uint32_t num_shards, uint32_t head_dim,
                   float* out, const doe_launch* launch);
+int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, uint32_t seq_len,
+                       uint32_t num_heads, uint32_t num_kv_heads, float scale, uint32_t causal,
+                       const doe_paged_kv* cache, uint32_t cache_seq, uint32_t cache_start,
+                       const doe_launch* launch);
 int launch_rope(float* qk, const float* freq_cis, uint32_t seq_len, uint32_t num_heads,
                 uint32_t head_dim, uint32_t position_offset, const doe_launch* launch);
 

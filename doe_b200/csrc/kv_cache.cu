@@ -86,6 +86,80 @@ __global__ void __launch_bounds__(256) paged_append_kernel(const PagedAppendArgs
   }
 }
 
+// head_dim 128 fast path: one warp per (sequence, token); each half-warp owns
+// a (K or V, kv head) row per step, 16 lanes x 16 bytes.  All of the token's
+// rows are loaded before any is written, so a warp keeps Hkv x 512 bytes in
+// flight.  Same arithmetic as paged_append_kernel.
+template <bool INT8, int HKV>
+__global__ void __launch_bounds__(128) paged_append_d128_kernel(const PagedAppendArgs a) {
+  constexpr int D = 128;
+  constexpr int ROWS = 2 * HKV;          // K and V rows of one token
+  constexpr int PER = (ROWS + 1) / 2;    // rows per half-warp
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hw = lane >> 4, l16 = lane & 15;
+  const int t = blockIdx.x * 4 + warp, b = blockIdx.y;
+  if (t >= a.n_tokens) return;
+  const int pos0 = a.positions[b];
+  const long long pos = (long long)pos0 + t;
+  const long long pidx = pos / a.page_size;
+  int page = -1;
+  if (pos0 >= 0 && pidx < a.max_pages) page = a.block_table[(size_t)b * a.max_pages + pidx];
+  if ((unsigned)page >= (unsigned)a.num_pages) {
+    if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
+    return;
+  }
+  const int in_page = (int)(pos - pidx * a.page_size);
+  const size_t row = (size_t)page * a.page_size + in_page;
+  const size_t src_tok = ((size_t)b * a.n_tokens + t) * HKV * D;
+  uint4 x[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int rr = 2 * i + hw;  // 0..HKV-1: K heads, HKV..: V heads
+    if (rr < ROWS) {
+      const __half* src = (rr < HKV ? a.new_k : a.new_v) + src_tok + (size_t)(rr % HKV) * D + 8 * l16;
+      x[i] = *reinterpret_cast<const uint4*>(src);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int rr = 2 * i + hw;
+    if (rr >= ROWS) continue;  // uniform per half-warp; shuffles below stay inside it
+    const int h = rr % HKV;
+    uint8_t* pool = rr < HKV ? a.k_pool : a.v_pool;
+    if (!INT8) {
+      *reinterpret_cast<uint4*>(pool + ((row * HKV + h) * D + 8 * l16) * 2) = x[i];
+      continue;
+    }
+    const __half2* hx = reinterpret_cast<const __half2*>(&x[i]);
+    float v[8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      v[2 * e] = __low2float(hx[e]);
+      v[2 * e + 1] = __high2float(hx[e]);
+      amax = fmaxf(amax, fmaxf(fabsf(v[2 * e]), fabsf(v[2 * e + 1])));
+    }
+    // both half-warps run this together (ROWS is even); offsets <= 8 stay in a half
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
+    const float sf = __half2float(sh);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      int qv = 0;
+      if (sf != 0.0f) {
+        qv = __float2int_rn(__fdiv_rn(v[e], sf));
+        qv = qv > 127 ? 127 : (qv < -127 ? -127 : qv);
+      }
+      if (e < 4) lo |= (uint32_t)(qv & 0xff) << (8 * e);
+      else hi |= (uint32_t)(qv & 0xff) << (8 * (e - 4));
+    }
+    *reinterpret_cast<uint2*>(pool + (row * HKV + h) * D + 8 * l16) = make_uint2(lo, hi);
+    if (l16 == 0) (rr < HKV ? a.k_scale : a.v_scale)[((size_t)page * HKV + h) * a.page_size + in_page] = sh;
+  }
+}
+
 int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
                         const void* new_k, const void* new_v, const int32_t* positions,
                         const doe_launch* launch) {
@@ -112,8 +186,23 @@ int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_to
   a.num_pages = (int)kv->num_pages;
   a.max_pages = (int)kv->max_pages_per_seq;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
-  dim3 grid(n_tokens, num_seqs), block(256);
   const bool int8 = kv->kv_dtype == DOE_KV_INT8;
+  if (kv->head_dim == 128 && (kv->num_kv_heads == 8 || kv->num_kv_heads == 4 ||
+                              kv->num_kv_heads == 2 || kv->num_kv_heads == 1)) {
+    dim3 g2((n_tokens + 3) / 4, num_seqs);
+#define DOE_PA2(H) \
+  (int8 ? paged_append_d128_kernel<true, H><<<g2, 128, 0, st>>>(a) \
+        : paged_append_d128_kernel<false, H><<<g2, 128, 0, st>>>(a))
+    switch (kv->num_kv_heads) {
+      case 8: DOE_PA2(8); break;
+      case 4: DOE_PA2(4); break;
+      case 2: DOE_PA2(2); break;
+      default: DOE_PA2(1); break;
+    }
+#undef DOE_PA2
+    return cuda_status(cudaGetLastError(), "paged_append_d128_kernel");
+  }
+  dim3 grid(n_tokens, num_seqs), block(256);
   const int epl = (int)kv->head_dim / 32;
 #define DOE_PA(E) \
   (int8 ? paged_append_kernel<true, E><<<grid, block, 0, st>>>(a) \

@@ -162,6 +162,38 @@ int doe_attention_prefill_wgsl_f32(const float* q, const float* k, const float* 
   return launch_attn_generic(a, true, static_cast<cudaStream_t>(l->stream));
 }
 
+int doe_attention_prefill_f16(const void* q, const void* k, const void* v, float* out,
+                              uint32_t seq_len, uint32_t num_heads, uint32_t num_kv_heads,
+                              uint32_t head_dim, float scale, uint32_t causal,
+                              const doe_paged_kv* cache, uint32_t cache_seq, uint32_t cache_start,
+                              const doe_launch* launch) {
+  if (!q || !k || !v || !out) return invalid("doe_attention_prefill_f16: null pointer");
+  if (head_dim != 128) {
+    set_op_error("doe_attention_prefill_f16: the tcgen05 prefill kernel is built for head_dim 128 (got %u)",
+                 head_dim);
+    return DOE_UNSUPPORTED;
+  }
+  if (num_kv_heads == 0 || num_heads == 0 || num_heads % num_kv_heads != 0)
+    return invalid("doe_attention_prefill_f16: num_heads %u is not a multiple of num_kv_heads %u",
+                   num_heads, num_kv_heads);
+  if (seq_len == 0) return DOE_OK;
+  if ((uint64_t)num_heads * ((seq_len + 127) / 128) > 0x7fffffffull)
+    return invalid("doe_attention_prefill_f16: grid too large");
+  if (cache != nullptr) {
+    int rc = check_paged_kv(cache, "doe_attention_prefill_f16");
+    if (rc != DOE_OK) return rc;
+    if (cache->kv_dtype != DOE_KV_F16 || cache->head_dim != 128 || cache->num_kv_heads != num_kv_heads)
+      return invalid("doe_attention_prefill_f16: the cache must be f16 with the same kv heads and head_dim 128");
+    if (!causal || seq_len % 16 != 0 || cache_start % 16 != 0) {
+      set_op_error("doe_attention_prefill_f16: the fused cache write needs a causal prefill with "
+                   "seq_len and cache_start multiples of 16 (use doe_paged_append otherwise)");
+      return DOE_UNSUPPORTED;
+    }
+  }
+  return launch_prefill_f16(q, k, v, out, seq_len, num_heads, num_kv_heads, scale, causal, cache,
+                            cache_seq, cache_start, launch_or_default(launch));
+}
+
 int doe_attention_stitch_f32(const float* partials, uint32_t rows, uint32_t num_shards,
                              uint32_t head_dim, float* out, const doe_launch* launch) {
   if (!partials || !out) return invalid("doe_attention_stitch_f32: null pointer");

@@ -35,6 +35,7 @@ struct PagedDecodeArgs {
   float* out;               // [B, H, D]
   float* part_o;            // [B*Hkv*max_splits, GROUP, D]
   float* part_ml;           // [B*Hkv*max_splits, GROUP, 2]
+  unsigned* counters;       // [B*Hkv] arrivals per (b, g); zeroed before each launch
   int32_t* status;
   int num_heads, num_kv_heads, num_pages, page_size, max_pages;
   int split_tiles, max_splits;
@@ -113,9 +114,50 @@ __device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
   }
 }
 
+// Per-warp shared-memory ring.  Lane l copies exactly the 16-byte pieces it
+// will later feed to its own mma fragments into slot [piece][l]: the copy and
+// the read-back are private to the lane (no barrier, no bank conflicts), and
+// cp.async keeps several tiles of HBM traffic in flight per warp.
+template <bool INT8>
+struct StageLayout {
+  static constexpr int kK = INT8 ? 4 : 8;     // K pieces (16 B) per lane per tile
+  static constexpr int kV = INT8 ? 4 : 8;     // V pieces
+  static constexpr int kPieces = kK + kV;
+  static constexpr int kScaleOff = kPieces * 512;           // int8: 4 x u32 scales per lane
+  static constexpr int kBytes = kPieces * 512 + (INT8 ? 4 * 128 : 0);
+  static constexpr int kStages = INT8 ? 4 : 2;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(v) : "r"(addr));
+  return v;
+}
+
 template <bool INT8, int GROUP>
 __global__ void __launch_bounds__(kWarps * 32)
     paged_decode_kernel(const PagedDecodeArgs a) {
+  using SL = StageLayout<INT8>;
+  constexpr int P = SL::kStages;
+  extern __shared__ __align__(128) uint8_t dsmem[];
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
@@ -135,11 +177,20 @@ __global__ void __launch_bounds__(kWarps * 32)
 
   __shared__ float sm_m[kWarps][8];
   __shared__ float sm_l[kWarps][8];
-  __shared__ float sm_o[kWarps][GROUP][kD];
+  __shared__ int sm_last;
 
   if (a.new_k != nullptr && split == nsplits - 1 && seq_len > 0) {
     if (warp == 0) append_row<INT8>(a, b, g, seq_len - 1, table, lane);
-    __syncthreads();
+    __syncthreads();  // the appended row is read back below (through L2)
+  }
+
+  // ---- this warp's tiles: tile_begin + warp + 4k, k < nt; page ids up front
+  const int span = tile_end - tile_begin - warp;
+  const int nt = span > 0 ? (span + kWarps - 1) / kWarps : 0;
+  int pg = -1;
+  if (lane < nt) {
+    const int pos = (tile_begin + warp + kWarps * lane) << 4;
+    pg = table[pos / a.page_size];
   }
 
   // ---- Q fragments (rows = heads g*GROUP + r, r < GROUP) -----------------
@@ -168,48 +219,83 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
   }
 
+  constexpr int ROWB = INT8 ? kD : 2 * kD;  // bytes per (token, kv head) row
+  const size_t head_stride = (size_t)Hkv * ROWB;
+  const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+  const uint32_t wbase = static_cast<uint32_t>(__cvta_generic_to_shared(dsmem)) + warp * P * SL::kBytes;
+
+  // Copies tile k's pieces for this lane into stage k % P.
+  auto issue = [&](int k) {
+    const int page = __shfl_sync(0xffffffffu, pg, k & 31);
+    if ((unsigned)page >= (unsigned)a.num_pages) return;
+    const int pos0 = (tile_begin + warp + kWarps * k) << 4;
+    const int pidx = pos0 / a.page_size;
+    const int in0 = pos0 - pidx * a.page_size;
+    const size_t row0 = (size_t)page * a.page_size + in0;
+    const uint8_t* kbase = a.k_pool + row0 * head_stride + (size_t)g * ROWB;
+    const uint8_t* vbase = a.v_pool + row0 * head_stride + (size_t)g * ROWB;
+    const uint32_t sb = wbase + (k % P) * SL::kBytes + lane * 16;
+#pragma unroll
+    for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+      for (int i = 0; i < (INT8 ? 2 : 4); ++i)
+        cp_async16(sb + (nb * (INT8 ? 2 : 4) + i) * 512,
+                   kbase + (size_t)(nb * 8 + r) * head_stride + 64 * i + 16 * c);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int h = 0; h < (INT8 ? 1 : 2); ++h)
+        cp_async16(sb + (SL::kK + j * (INT8 ? 1 : 2) + h) * 512,
+                   vbase + (size_t)vt[j] * head_stride + (INT8 ? 16 * r : 128 * h + 16 * r));
+    if (INT8) {
+      const size_t sidx = ((size_t)page * Hkv + g) * a.page_size + in0;
+      const uint32_t ss = wbase + (k % P) * SL::kBytes + SL::kScaleOff + lane * 4;
+      cp_async4(ss + 0 * 128, a.k_scale + sidx + 2 * c);
+      cp_async4(ss + 1 * 128, a.k_scale + sidx + 8 + 2 * c);
+      cp_async4(ss + 2 * 128, a.v_scale + sidx + 2 * c);
+      cp_async4(ss + 3 * 128, a.v_scale + sidx + 8 + 2 * c);
+    }
+  };
+
   float m_run = -INFINITY, l_run = 0.0f;
   float acc[8][4];
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) acc[mb][0] = acc[mb][1] = acc[mb][2] = acc[mb][3] = 0.0f;
 
-  constexpr int ROWB = INT8 ? kD : 2 * kD;  // bytes per (token, kv head) row
-  const size_t head_stride = (size_t)Hkv * ROWB;
-  const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-
-  for (int t = tile_begin + warp; t < tile_end; t += kWarps) {
-    const int pos0 = t << 4;
-    const int pidx = pos0 / a.page_size;
-    const int page = table[pidx];
+#pragma unroll
+  for (int s0 = 0; s0 < P - 1; ++s0) {
+    if (s0 < nt) issue(s0);
+    cp_async_commit();
+  }
+  for (int k = 0; k < nt; ++k) {
+    if (k + P - 1 < nt) issue(k + P - 1);
+    cp_async_commit();
+    cp_async_wait<P - 1>();  // tile k's pieces have landed
+    const int page = __shfl_sync(0xffffffffu, pg, k & 31);
     if ((unsigned)page >= (unsigned)a.num_pages) {
       if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
       continue;
     }
-    const int in0 = pos0 - pidx * a.page_size;
-    const size_t row0 = (size_t)page * a.page_size + in0;
-    const uint8_t* kbase = a.k_pool + row0 * head_stride + (size_t)g * ROWB;
-    const uint8_t* vbase = a.v_pool + row0 * head_stride + (size_t)g * ROWB;
+    const int pos0 = (tile_begin + warp + kWarps * k) << 4;
+    const uint32_t sb = wbase + (k % P) * SL::kBytes + lane * 16;
 
-    // ---- loads: K rows r and 8+r, V rows 2c, 2c+1, 2c+8, 2c+9 ------------
     uint4 kraw[2][INT8 ? 2 : 4];
     uint4 vraw[4][INT8 ? 1 : 2];
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
-      for (int i = 0; i < (INT8 ? 2 : 4); ++i)
-        kraw[nb][i] = ldcg4(kbase + (size_t)(nb * 8 + r) * head_stride + 64 * i + 16 * c);
+      for (int i = 0; i < (INT8 ? 2 : 4); ++i) kraw[nb][i] = lds128(sb + (nb * (INT8 ? 2 : 4) + i) * 512);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int h = 0; h < (INT8 ? 1 : 2); ++h)
-        vraw[j][h] = ldcg4(vbase + (size_t)vt[j] * head_stride + (INT8 ? 16 * r : 128 * h + 16 * r));
+      for (int h = 0; h < (INT8 ? 1 : 2); ++h) vraw[j][h] = lds128(sb + (SL::kK + j * (INT8 ? 1 : 2) + h) * 512);
     uint32_t ksc[2] = {0, 0}, vsc[2] = {0, 0};
     if (INT8) {
-      const size_t sb = ((size_t)page * Hkv + g) * a.page_size + in0;
-      ksc[0] = __ldcg(reinterpret_cast<const unsigned int*>(a.k_scale + sb + 2 * c));
-      ksc[1] = __ldcg(reinterpret_cast<const unsigned int*>(a.k_scale + sb + 8 + 2 * c));
-      vsc[0] = __ldcg(reinterpret_cast<const unsigned int*>(a.v_scale + sb + 2 * c));
-      vsc[1] = __ldcg(reinterpret_cast<const unsigned int*>(a.v_scale + sb + 8 + 2 * c));
+      const uint32_t ss = wbase + (k % P) * SL::kBytes + SL::kScaleOff + lane * 4;
+      ksc[0] = lds32(ss);
+      ksc[1] = lds32(ss + 128);
+      vsc[0] = lds32(ss + 256);
+      vsc[1] = lds32(ss + 384);
     }
 
     // ---- S = Q K^T ----------------------------------------------------------
@@ -315,55 +401,91 @@ __global__ void __launch_bounds__(kWarps * 32)
       mma_16816(acc[mb], a0, a1, a2, a3, pb0, pb1);
     }
   }
+  cp_async_wait<0>();
 
-  // ---- merge the warps of this split --------------------------------------
+  // ---- merge the warps of this split (O staged in this warp's own ring) ----
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
   if (c == 0 && r < GROUP) {
     sm_m[warp][r] = m_run;
     sm_l[warp][r] = l_run;
   }
+  float* my_o = reinterpret_cast<float*>(dsmem + warp * P * SL::kBytes);  // [GROUP][kD]
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) {
     const int d0 = INT8 ? (16 * r + 4 * (mb >> 1) + 2 * (mb & 1))
                         : (64 * (mb >> 2) + 8 * r + 2 * (mb & 3));
     if (2 * c < GROUP) {
-      sm_o[warp][2 * c][d0] = acc[mb][0];
-      sm_o[warp][2 * c][d0 + 1] = acc[mb][2];
+      my_o[(2 * c) * kD + d0] = acc[mb][0];
+      my_o[(2 * c) * kD + d0 + 1] = acc[mb][2];
     }
     if (2 * c + 1 < GROUP) {
-      sm_o[warp][2 * c + 1][d0] = acc[mb][1];
-      sm_o[warp][2 * c + 1][d0 + 1] = acc[mb][3];
+      my_o[(2 * c + 1) * kD + d0] = acc[mb][1];
+      my_o[(2 * c + 1) * kD + d0 + 1] = acc[mb][3];
     }
   }
   __syncthreads();
 
   const int dim = threadIdx.x;  // 128 threads == head dim
+  float O[GROUP], L[GROUP], M[GROUP];
 #pragma unroll
   for (int hh = 0; hh < GROUP; ++hh) {
-    float M = -INFINITY;
+    M[hh] = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, sm_m[w][hh]);
-    float O = 0.0f, L = 0.0f;
-    if (M != -INFINITY) {
+    for (int w = 0; w < kWarps; ++w) M[hh] = fmaxf(M[hh], sm_m[w][hh]);
+    O[hh] = 0.0f;
+    L[hh] = 0.0f;
+    if (M[hh] != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
-        const float f = exp2f(sm_m[w][hh] - M);  // -inf -> 0
-        O += f * sm_o[w][hh][dim];
-        L += f * sm_l[w][hh];
+        const float f = exp2f(sm_m[w][hh] - M[hh]);  // -inf -> 0
+        O[hh] += f * reinterpret_cast<const float*>(dsmem + w * P * SL::kBytes)[hh * kD + dim];
+        L[hh] += f * sm_l[w][hh];
       }
     }
-    if (nsplits == 1) {
-      a.out[((size_t)b * a.num_heads + (size_t)g * GROUP + hh) * kD + dim] =
-          L > 0.0f ? O * (1.0f / L) : 0.0f;
-    } else {
-      const size_t prow = (((size_t)b * Hkv + g) * a.max_splits + split) * GROUP + hh;
-      a.part_o[prow * kD + dim] = O;
-      if (dim == 0) {
-        a.part_ml[prow * 2] = M;
-        a.part_ml[prow * 2 + 1] = L;
+  }
+  float* out_row = a.out + ((size_t)b * a.num_heads + (size_t)g * GROUP) * kD;
+  if (nsplits == 1) {
+#pragma unroll
+    for (int hh = 0; hh < GROUP; ++hh) out_row[hh * kD + dim] = L[hh] > 0.0f ? O[hh] * (1.0f / L[hh]) : 0.0f;
+    return;
+  }
+  // ---- split partials; the last split of (b, g) to finish stitches them ---
+  const size_t base = ((size_t)b * Hkv + g) * a.max_splits;
+#pragma unroll
+  for (int hh = 0; hh < GROUP; ++hh) {
+    const size_t prow = (base + split) * GROUP + hh;
+    a.part_o[prow * kD + dim] = O[hh];
+    if (dim == 0) {
+      a.part_ml[prow * 2] = M[hh];
+      a.part_ml[prow * 2 + 1] = L[hh];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(&a.counters[(size_t)b * Hkv + g], 1u);
+    sm_last = old == (unsigned)(nsplits - 1);
+    if (sm_last) a.counters[(size_t)b * Hkv + g] = 0u;  // ready for the next launch
+  }
+  __syncthreads();
+  if (!sm_last) return;
+  __threadfence();
+#pragma unroll
+  for (int hh = 0; hh < GROUP; ++hh) {
+    float MM = -INFINITY;
+    for (int sp = 0; sp < nsplits; ++sp)
+      MM = fmaxf(MM, __ldcg(a.part_ml + ((base + sp) * GROUP + hh) * 2));
+    float OO = 0.0f, LL = 0.0f;
+    if (MM != -INFINITY) {
+      for (int sp = 0; sp < nsplits; ++sp) {
+        const size_t prow = (base + sp) * GROUP + hh;
+        const float f = exp2f(__ldcg(a.part_ml + prow * 2) - MM);
+        OO += f * __ldcg(a.part_o + prow * kD + dim);
+        LL += f * __ldcg(a.part_ml + prow * 2 + 1);
       }
     }
+    out_row[hh * kD + dim] = LL > 0.0f ? OO * (1.0f / LL) : 0.0f;
   }
 }
 
@@ -411,6 +533,22 @@ template __global__ void combine_splits_kernel<true>(const CombineArgs);
 template __global__ void combine_splits_kernel<false>(const CombineArgs);
 
 // ---------------------------------------------------------------------------
+template <bool INT8, int GROUP>
+static int launch_one(const PagedDecodeArgs& a, dim3 grid, cudaStream_t st) {
+  using SL = StageLayout<INT8>;
+  constexpr int smem = kWarps * SL::kStages * SL::kBytes;
+  static bool attr = false;  // per instantiation
+  if (!attr) {
+    int rc = cuda_status(cudaFuncSetAttribute(paged_decode_kernel<INT8, GROUP>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                         "cudaFuncSetAttribute(paged_decode)");
+    if (rc != DOE_OK) return rc;
+    attr = true;
+  }
+  paged_decode_kernel<INT8, GROUP><<<grid, kWarps * 32, smem, st>>>(a);
+  return cuda_status(cudaGetLastError(), "paged_decode_kernel");
+}
+
 int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
                         const void* q, const int32_t* seq_lens, const void* new_k,
                         const void* new_v, float scale, float* out, uint32_t split_pages,
@@ -420,15 +558,18 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   const uint32_t tiles_per_page = kv->page_size / 16;
   uint32_t split_tiles = split_pages ? split_pages * tiles_per_page : 32;
   if (split_tiles == 0) split_tiles = 1;
+  if (split_tiles > 4 * 32) split_tiles = 4 * 32;  // 4 warps x 32 prefetched page ids
   const uint32_t max_tiles = kv->max_pages_per_seq * tiles_per_page;
   const uint32_t max_splits = max_tiles == 0 ? 1 : ceil_div(max_tiles, split_tiles);
   const uint64_t rows = (uint64_t)num_seqs * Hkv * max_splits * group;
-  const uint64_t ws = rows * (kD + 2) * sizeof(float);
+  const uint64_t part_bytes = rows * (kD + 2) * sizeof(float);
+  const uint64_t ctr_off = (part_bytes + 255) / 256 * 256;
+  const uint64_t ws = ctr_off + (uint64_t)num_seqs * Hkv * sizeof(unsigned);
   if (ws_needed_out) {
     *ws_needed_out = ws;
     return DOE_OK;
   }
-  if (ws > 0 && (launch->workspace == nullptr || launch->workspace_bytes < ws)) {
+  if (launch->workspace == nullptr || launch->workspace_bytes < ws) {
     set_op_error("doe_paged_decode: workspace of %llu bytes required, %llu given",
                  (unsigned long long)ws, (unsigned long long)launch->workspace_bytes);
     return DOE_INVALID_ARGUMENT;
@@ -446,6 +587,7 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.out = out;
   a.part_o = static_cast<float*>(launch->workspace);
   a.part_ml = a.part_o + rows * kD;
+  a.counters = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(launch->workspace) + ctr_off);
   a.status = launch->status;
   a.num_heads = (int)num_heads;
   a.num_kv_heads = (int)Hkv;
@@ -456,35 +598,21 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.max_splits = (int)max_splits;
   a.scale_log2 = scale * kLog2e;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
-  dim3 grid(max_splits, Hkv, num_seqs), block(kWarps * 32);
+  // arrival counters of the split stitch start at zero on every launch
+  int rc = cuda_status(cudaMemsetAsync(a.counters, 0, (size_t)num_seqs * Hkv * sizeof(unsigned), st),
+                       "cudaMemsetAsync(split counters)");
+  if (rc != DOE_OK) return rc;
+  dim3 grid(max_splits, Hkv, num_seqs);
   const bool int8 = kv->kv_dtype == DOE_KV_INT8;
-#define DOE_PD_LAUNCH(I8, G) paged_decode_kernel<I8, G><<<grid, block, 0, st>>>(a)
   switch (group) {
-    case 1: if (int8) DOE_PD_LAUNCH(true, 1); else DOE_PD_LAUNCH(false, 1); break;
-    case 2: if (int8) DOE_PD_LAUNCH(true, 2); else DOE_PD_LAUNCH(false, 2); break;
-    case 4: if (int8) DOE_PD_LAUNCH(true, 4); else DOE_PD_LAUNCH(false, 4); break;
-    case 8: if (int8) DOE_PD_LAUNCH(true, 8); else DOE_PD_LAUNCH(false, 8); break;
+    case 1: return int8 ? launch_one<true, 1>(a, grid, st) : launch_one<false, 1>(a, grid, st);
+    case 2: return int8 ? launch_one<true, 2>(a, grid, st) : launch_one<false, 2>(a, grid, st);
+    case 4: return int8 ? launch_one<true, 4>(a, grid, st) : launch_one<false, 4>(a, grid, st);
+    case 8: return int8 ? launch_one<true, 8>(a, grid, st) : launch_one<false, 8>(a, grid, st);
     default:
       set_op_error("doe_paged_decode: heads per kv head must be 1, 2, 4 or 8 (got %u)", group);
       return DOE_UNSUPPORTED;
   }
-#undef DOE_PD_LAUNCH
-  int rc = cuda_status(cudaGetLastError(), "paged_decode_kernel");
-  if (rc != DOE_OK) return rc;
-  CombineArgs ca;
-  ca.part_o = a.part_o;
-  ca.part_ml = a.part_ml;
-  ca.out = out;
-  ca.seq_lens = seq_lens;
-  ca.fixed_len = 0;
-  ca.cap = a.max_pages * a.page_size;
-  ca.split_tokens = (int)split_tiles * 16;
-  ca.max_splits = (int)max_splits;
-  ca.num_kv_heads = (int)Hkv;
-  ca.group = (int)group;
-  ca.head_dim = kD;
-  combine_splits_kernel<true><<<dim3(num_heads, num_seqs), kD, 0, st>>>(ca);
-  return cuda_status(cudaGetLastError(), "combine_splits_kernel");
 }
 
 }  // namespace doe

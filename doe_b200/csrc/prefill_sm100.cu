@@ -1,0 +1,531 @@
+// prefill_sm100.cu -- causal prefill attention on the 5th-generation tensor
+// cores (tcgen05 + TMEM + TMA), with the prompt's K/V written into a paged
+// KV cache on the way.
+//
+// Semantics: attention_head256_f16kv.wgsl with query_len = seq_len,
+// is_causal, start_pos = kv_start = 0, dense K/V (…wgsl:113-136 key bounds,
+// 181-217 online softmax, 257-268 out = acc / l), f16 Q/K/V in [S, H, D]
+// ([B,S,H,D] with B = 1), f32 accumulation and f32 output; GQA kv head =
+// h / (H / Hkv).  The cache write is kv_write generalised to the paged pool
+// (runtime/zig/src/tsir/emit_kernel_body.zig:620-690).
+//
+// One CTA owns 128 query rows of one head and walks the 128-key tiles up to
+// the diagonal (heaviest tiles are launched first):
+//   warp 5     TMA producer: Q once, K/V tiles into a 2-stage ring; on the
+//              diagonal tile it also TMA-stores K/V into the paged cache
+//   warp 4     TMEM owner + MMA issuer (one thread): S = Q K^T into one of two
+//              TMEM S buffers, then O += P V into the TMEM O accumulator
+//   warps 0-3  softmax: thread r owns query row r (TMEM lane r): reads S
+//              (tcgen05.ld), keeps the running max in the log2 domain with a
+//              lazy rescale (O is rescaled in TMEM only when the max grows by
+//              more than 2^8), writes P as f16 into swizzled shared memory;
+//              finally reads O, divides by l and stores f32 rows.
+// Operands are K-major SWIZZLE_128B tiles (Q, K, P) and an MN-major tile (V)
+// described by tcgen05 shared-memory descriptors.  No cluster multicast.
+// Every mbarrier wait is bounded (about one second of clock cycles); on
+// timeout the kernel records DOE_DEVICE_ERR_TIMEOUT, the roles stop, all
+// issued MMAs are waited for (bounded) and TMEM is freed before returning.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace doe {
+namespace pf {
+
+constexpr int BM = 128, BN = 128, HD = 128;
+constexpr int kThreads = 192;
+constexpr uint32_t kSub = 128 * 128;      // one 128-row x 64-half swizzled sub-tile (16 KB)
+constexpr uint32_t kTile = 2 * kSub;      // 128 x 128 f16 tile (32 KB)
+constexpr uint32_t OFF_Q = 0;
+constexpr uint32_t OFF_K = OFF_Q + kTile;           // 2 stages
+constexpr uint32_t OFF_V = OFF_K + 2 * kTile;       // 2 stages
+constexpr uint32_t OFF_P = OFF_V + 2 * kTile;
+constexpr uint32_t OFF_BAR = OFF_P + kTile;          // barriers + TMEM slot
+constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;  // + alignment slack
+constexpr uint32_t kTmemCols = 512;                  // S0 [0,128) S1 [128,256) O [256,384)
+constexpr long long kWaitCycles = 4000000000LL;      // ~2 s at 1.9 GHz
+
+enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1, S_FULL0, S_FULL1,
+           P_FULL, O_FULL, MMA_DONE, NUM_BARS };
+
+struct Args {
+  float* out;               // [S, H, D] f32
+  int32_t* status;
+  const int32_t* table;     // block-table row of the cache sequence (or null)
+  int seq_len, num_heads, num_kv_heads, n_qtiles, causal;
+  int cache_page_size, cache_num_pages, cache_max_pages, cache_start;
+  float scale_log2;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "selp.b32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false (and an error bit, and the CTA abort flag) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int32_t* status) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      report(status, DOE_DEVICE_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int x, int y,
+                                             int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];\n" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
+// tcgen05 shared-memory descriptor: SWIZZLE_128B, version 1 (sm_100).
+//   K-major: rows 128 B apart, 8-row groups 1024 B apart (SBO), LBO unused (1).
+//   MN-major: 64-element runs contiguous, the next 64 elements LBO bytes away,
+//             K rows 128 B apart, 8-row groups SBO = 1024 B apart.
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: f16 A/B, f32 accumulate, M = 128, N = 128.
+__host__ __device__ constexpr uint32_t idesc_f16(bool b_mn_major) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | ((b_mn_major ? 1u : 0u) << 16) |
+         ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                     uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+
+#define DOE_R32(r)                                                                            \
+  "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),       \
+      "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), \
+      "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),           \
+      "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),           \
+      "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+#define DOE_W32(r)                                                                            \
+  "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),   \
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),       \
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),     \
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),     \
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+
+// 32 consecutive TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : DOE_R32(r)
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n" ::"r"(
+          taddr),
+      DOE_W32(r)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_ck,
+                   const __grid_constant__ CUtensorMap tm_cv, const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_BAR + 8 * NUM_BARS);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_BAR + 8 * NUM_BARS + 8);
+  auto bar = [&](int i) { return smem_u32(&bars[i]); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.num_heads;
+  const int t_order = blockIdx.x / H;
+  const int h = blockIdx.x - t_order * H;
+  const int qtile = a.n_qtiles - 1 - t_order;  // heaviest (longest) rows first
+  const int hk = h / (H / a.num_kv_heads);
+  const int q0 = qtile * BM;
+  const int n_kv = a.causal ? qtile + 1 : (a.seq_len + BN - 1) / BN;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), i == P_FULL ? 4u : 1u);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 4) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 5) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      mbar_expect_tx(bar(Q_FULL), kTile);
+      tma_load_3d(sbase + OFF_Q, &tm_q, bar(Q_FULL), 0, h, q0);
+      tma_load_3d(sbase + OFF_Q + kSub, &tm_q, bar(Q_FULL), 64, h, q0);
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int st = j & 1;
+        if (j >= 2) ok = mbar_wait(bar(KV_EMPTY0 + st), ((j >> 1) - 1) & 1, abort_flag, a.status);
+        if (!ok) break;
+        const uint32_t kd = sbase + OFF_K + st * kTile, vd = sbase + OFF_V + st * kTile;
+        mbar_expect_tx(bar(K_FULL0 + st), kTile);
+        tma_load_3d(kd, &tm_k, bar(K_FULL0 + st), 0, hk, j * BN);
+        tma_load_3d(kd + kSub, &tm_k, bar(K_FULL0 + st), 64, hk, j * BN);
+        mbar_expect_tx(bar(V_FULL0 + st), kTile);
+        tma_load_3d(vd, &tm_v, bar(V_FULL0 + st), 0, hk, j * BN);
+        tma_load_3d(vd + kSub, &tm_v, bar(V_FULL0 + st), 64, hk, j * BN);
+      }
+      // the diagonal CTA of the first head of each kv group writes this
+      // tile's K/V rows into the paged cache (16-row boxes: one page slice each)
+      const int j = n_kv - 1;
+      if (ok && a.table != nullptr && a.causal && (h % (H / a.num_kv_heads)) == 0) {
+        const int st = j & 1;
+        ok = mbar_wait(bar(K_FULL0 + st), (j >> 1) & 1, abort_flag, a.status) &&
+             mbar_wait(bar(V_FULL0 + st), (j >> 1) & 1, abort_flag, a.status);
+        if (ok) {
+          asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+          for (int m = 0; m < BN / 16; ++m) {
+            const int tok = j * BN + m * 16;
+            if (tok + 16 > a.seq_len) break;
+            const int pos = a.cache_start + tok;
+            const int pidx = pos / a.cache_page_size;
+            const int page = pidx < a.cache_max_pages ? a.table[pidx] : -1;
+            if ((unsigned)page >= (unsigned)a.cache_num_pages) {
+              report(a.status, DOE_DEVICE_ERR_PAGE);
+              continue;
+            }
+            const int row = page * a.cache_page_size + (pos - pidx * a.cache_page_size);
+            for (int sub = 0; sub < 2; ++sub) {
+              const uint32_t off = st * kTile + sub * kSub + m * 16 * 128;
+              tma_store_3d(&tm_ck, sbase + OFF_K + off, sub * 64, hk, row);
+              tma_store_3d(&tm_cv, sbase + OFF_V + off, sub * 64, hk, row);
+            }
+          }
+          asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+          asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idq = idesc_f16(false), idp = idesc_f16(true);
+      auto issue_s = [&](int j) {
+        const int st = j & 1;
+        const uint32_t kb = sbase + OFF_K + st * kTile;
+        const uint32_t d = tmem + st * 128;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
+          umma(d, sdesc(sbase + OFF_Q + off, 16, 1024), sdesc(kb + off, 16, 1024), idq, kk > 0);
+        }
+        umma_commit(bar(S_FULL0 + st));
+      };
+      bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag, a.status) &&
+                mbar_wait(bar(K_FULL0), 0, abort_flag, a.status);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv) {
+          const int st = (j + 1) & 1;
+          ok = mbar_wait(bar(K_FULL0 + st), ((j + 1) >> 1) & 1, abort_flag, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        ok = mbar_wait(bar(P_FULL), j & 1, abort_flag, a.status) &&
+             mbar_wait(bar(V_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t vb = sbase + OFF_V + (j & 1) * kTile;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          // A = P (K-major over keys), B = V (MN-major: head dims contiguous)
+          const uint32_t pa = sbase + OFF_P + (kk >> 2) * kSub + (kk & 3) * 32;
+          umma(tmem + 256, sdesc(pa, 16, 1024), sdesc(vb + kk * 16 * 128, kSub, 1024), idp,
+               (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(bar(O_FULL));
+        umma_commit(bar(KV_EMPTY0 + (j & 1)));
+      }
+      // every MMA this thread issued has finished once MMA_DONE flips
+      umma_commit(bar(MMA_DONE));
+      mbar_wait(bar(MMA_DONE), 0, abort_flag, a.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int row = warp * 32 + lane;
+    const int q_idx = q0 + row;
+    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    float m_used = -INFINITY, l = 0.0f;
+    bool ok = true;
+    uint8_t* prow = smem + OFF_P + row * 128;
+    for (int j = 0; j < n_kv; ++j) {
+      ok = ok && mbar_wait(bar(S_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
+      // warp-collective TMEM traffic: a timed-out lane keeps its warp in step
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      float x[BN];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(lane_base + (j & 1) * 128 + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]);
+      }
+      const int k0 = j * BN;
+      float m_t = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN; ++c) {
+        const int key = k0 + c;
+        const bool valid = key < a.seq_len && (!a.causal || key <= q_idx);
+        x[c] = valid ? x[c] * a.scale_log2 : -INFINITY;
+        m_t = fmaxf(m_t, x[c]);
+      }
+      const bool grow = m_t > m_used + 8.0f;
+      const float m_new = grow ? m_t : m_used;
+      const float corr = (grow && m_used != -INFINITY) ? exp2f(m_used - m_new) : 1.0f;
+      float sum = 0.0f;
+      uint32_t ph[BN / 2];
+#pragma unroll
+      for (int c = 0; c < BN; c += 2) {
+        const float p0 = m_new == -INFINITY ? 0.0f : exp2f(x[c] - m_new);
+        const float p1 = m_new == -INFINITY ? 0.0f : exp2f(x[c + 1] - m_new);
+        sum += p0 + p1;
+        ph[c / 2] = pack_half2(p0, p1);
+      }
+      l = l * corr + sum;
+      m_used = m_new;
+      if (j > 0) {
+        // PV(j-1) must be done: it reads the P buffer and owns O
+        ok = mbar_wait(bar(O_FULL), (j - 1) & 1, abort_flag, a.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, grow)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(lane_base + 256 + c * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+            tmem_st32(lane_base + 256 + c * 32, r);
+          }
+          tmem_wait_st();
+        }
+      }
+      // P row -> two swizzled 128-byte lines (16-byte chunk ch lands at ch ^ (row & 7))
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        const int sub = ch >> 3, cc = ch & 7;
+        uint4 v = make_uint4(ph[ch * 4], ph[ch * 4 + 1], ph[ch * 4 + 2], ph[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(prow + sub * kSub + ((cc ^ (row & 7)) << 4)) = v;
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(P_FULL));
+    }
+    // ---- epilogue: O / l -> out
+    if (ok) ok = mbar_wait(bar(O_FULL), (n_kv - 1) & 1, abort_flag, a.status);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+      float* orow = a.out + ((size_t)q_idx * H + h) * HD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(lane_base + 256 + c * 32, r);
+        tmem_wait_ld();
+        if (q_idx < a.seq_len) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float4 o = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                   __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+            *reinterpret_cast<float4*>(orow + c * 32 + i) = o;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+}  // namespace pf
+
+// ---- host -----------------------------------------------------------------
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int get_encoder() {
+  if (g_encode) return DOE_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+    cudaGetLastError();
+    set_op_error("prefill: cuTensorMapEncodeTiled is not available from the driver");
+    return DOE_CUDA_ERROR;
+  }
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return DOE_OK;
+}
+
+// [rows, heads, 128] f16 viewed as a 3-D tensor {128, heads, rows}; boxes of
+// 64 x 1 x box_rows elements with the 128-byte swizzle.
+int make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t heads, uint32_t box_rows) {
+  const cuuint64_t dims[3] = {128, heads, rows};
+  const cuuint64_t strides[2] = {128 * 2, heads * 128 * 2};
+  const cuuint32_t box[3] = {64, 1, box_rows};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_op_error("prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return DOE_CUDA_ERROR;
+  }
+  return DOE_OK;
+}
+
+}  // namespace
+
+int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, uint32_t seq_len,
+                       uint32_t num_heads, uint32_t num_kv_heads, float scale, uint32_t causal,
+                       const doe_paged_kv* cache, uint32_t cache_seq, uint32_t cache_start,
+                       const doe_launch* launch) {
+  int rc = get_encoder();
+  if (rc != DOE_OK) return rc;
+  for (const void* p : {q, k, v, (const void*)out})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) {
+      set_op_error("prefill: q, k, v and out must be 16-byte aligned");
+      return DOE_INVALID_ARGUMENT;
+    }
+  CUtensorMap mq, mk, mv, mck, mcv;
+  rc = make_map(&mq, q, seq_len, num_heads, 128);
+  if (rc == DOE_OK) rc = make_map(&mk, k, seq_len, num_kv_heads, 128);
+  if (rc == DOE_OK) rc = make_map(&mv, v, seq_len, num_kv_heads, 128);
+  pf::Args a;
+  a.out = out;
+  a.status = launch->status;
+  a.table = nullptr;
+  a.seq_len = (int)seq_len;
+  a.num_heads = (int)num_heads;
+  a.num_kv_heads = (int)num_kv_heads;
+  a.n_qtiles = (int)((seq_len + 127) / 128);
+  a.causal = causal ? 1 : 0;
+  a.cache_page_size = a.cache_num_pages = a.cache_max_pages = a.cache_start = 0;
+  a.scale_log2 = scale * kLog2e;
+  if (rc == DOE_OK && cache != nullptr) {
+    const uint64_t rows = (uint64_t)cache->num_pages * cache->page_size;
+    rc = make_map(&mck, cache->k_pool, rows, cache->num_kv_heads, 16);
+    if (rc == DOE_OK) rc = make_map(&mcv, cache->v_pool, rows, cache->num_kv_heads, 16);
+    a.table = cache->block_table + (size_t)cache_seq * cache->max_pages_per_seq;
+    a.cache_page_size = (int)cache->page_size;
+    a.cache_num_pages = (int)cache->num_pages;
+    a.cache_max_pages = (int)cache->max_pages_per_seq;
+    a.cache_start = (int)cache_start;
+  } else {
+    mck = mk;
+    mcv = mv;
+  }
+  if (rc != DOE_OK) return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    rc = cuda_status(cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          pf::kSmemBytes),
+                     "cudaFuncSetAttribute(prefill)");
+    if (rc != DOE_OK) return rc;
+    attr_set = true;
+  }
+  const uint64_t ctas = (uint64_t)a.n_qtiles * num_heads;
+  pf::prefill_kernel<<<(unsigned)ctas, pf::kThreads, pf::kSmemBytes,
+                       static_cast<cudaStream_t>(launch->stream)>>>(mq, mk, mv, mck, mcv, a);
+  return cuda_status(cudaGetLastError(), "prefill_kernel");
+}
+
+}  // namespace doe

@@ -180,3 +180,22 @@ def rope(qk, freq_cis, position_offset: int = 0, stream=None):
     abi.check("doe_rope_f32", abi.lib().doe_rope_f32(
         qk.data_ptr(), freq_cis.data_ptr(), S, H, D, position_offset, C.byref(l)))
     return qk
+
+
+def attention_prefill_f16(q, k, v, scale: float, causal: bool = True, cache: PagedKVCache | None = None,
+                          cache_seq: int = 0, cache_start: int = 0, out=None, status=None, stream=None):
+    """tcgen05 prefill: q [S,H,128], k/v [S,Hkv,128] f16 -> out [S,H,128] f32.
+
+    With `cache`, the prompt's K/V rows are also written into the paged cache."""
+    for t, n in ((q, "q"), (k, "k"), (v, "v")):
+        _need(t, torch.float16, n)
+    S, H, D = q.shape
+    Hkv = k.shape[1]
+    out = torch.empty((S, H, D), dtype=torch.float32, device=q.device) if out is None else out
+    kv = cache.struct() if cache is not None else None
+    l = _launch(0, status, stream, q.device)
+    abi.check("doe_attention_prefill_f16", abi.lib().doe_attention_prefill_f16(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), S, H, Hkv, D, float(scale),
+        1 if causal else 0, C.byref(kv) if kv is not None else None, cache_seq, cache_start,
+        C.byref(l)))
+    return out

@@ -40,6 +40,28 @@ def decode_f32(seed: int = 0, heads: int = 8, head_dim: int = 64, kv_len: int = 
 
 
 @dataclass
+class PrefillF16:
+    q: np.ndarray  # [S, H, D] f16
+    k: np.ndarray  # [S, Hkv, D] f16
+    v: np.ndarray
+    scale: float
+    flops: int     # causal-exact: 4 * H * D * S (S + 1) / 2
+    io_bytes: int  # q, k, v read + f32 out + the K/V cache write
+
+
+def prefill_f16(seed: int = 1, seq_len: int = 2048, heads: int = 32, kv_heads: int = 32,
+                head_dim: int = 128) -> PrefillF16:
+    """Config 2: causal prefill, Q/K/V ~ N(0,1) * 0.5 cast to f16, [B=1, S, H, D]."""
+    g = np.random.default_rng(seed)
+    q = (g.standard_normal((seq_len, heads, head_dim), dtype=np.float32) * np.float32(0.5)).astype(np.float16)
+    k = (g.standard_normal((seq_len, kv_heads, head_dim), dtype=np.float32) * np.float32(0.5)).astype(np.float16)
+    v = (g.standard_normal((seq_len, kv_heads, head_dim), dtype=np.float32) * np.float32(0.5)).astype(np.float16)
+    flops = 4 * heads * head_dim * seq_len * (seq_len + 1) // 2
+    io = (q.nbytes + k.nbytes + v.nbytes) + seq_len * heads * head_dim * 4 + k.nbytes + v.nbytes
+    return PrefillF16(q, k, v, 1.0 / float(np.sqrt(head_dim)), flops, io)
+
+
+@dataclass
 class PagedWorkload:
     """A batched decode step over a paged cache (configs 3 and 4)."""
 

@@ -46,6 +46,7 @@ typedef enum doe_status {
 #define DOE_DEVICE_ERR_PAGE 0x1     /* block-table entry outside the pool   */
 #define DOE_DEVICE_ERR_POSITION 0x2 /* write position >= cache capacity     */
 #define DOE_DEVICE_ERR_LENGTH 0x4   /* sequence longer than its block table */
+#define DOE_DEVICE_ERR_TIMEOUT 0x8  /* a bounded in-kernel wait gave up     */
 
 /* KV element types of a paged cache.                                       */
 #define DOE_KV_F16 0u
@@ -202,6 +203,23 @@ int doe_attention_prefill_wgsl_f32(const float* q, const float* k,
                                    const float* v, float* out, uint32_t seq_len,
                                    uint32_t head_dim, uint32_t num_heads,
                                    float scale, const doe_launch* launch);
+
+/* Causal prefill on the tcgen05 tensor cores: the head256 online softmax with
+ * query_len = seq_len, is_causal, start_pos = kv_start = 0
+ * (attention_head256_f16kv.wgsl:113-136, 181-268), f16 q [S,H,D] and k/v
+ * [S,Hkv,D] (the [B,S,H,D] layout with B = 1), f32 out [S,H,D], f32
+ * accumulation, head_dim 128.  When `cache` is given (causal only, seq_len and
+ * cache_start multiples of 16, f16 pools) the prompt's K/V rows are also
+ * written into the paged cache at positions cache_start.. of block-table row
+ * `cache_seq` (kv_write, runtime/zig/src/tsir/emit_kernel_body.zig:620-690).
+ * Pointers must be 16-byte aligned.                                         */
+int doe_attention_prefill_f16(const void* q, const void* k, const void* v,
+                              float* out, uint32_t seq_len, uint32_t num_heads,
+                              uint32_t num_kv_heads, uint32_t head_dim,
+                              float scale, uint32_t causal,
+                              const struct doe_paged_kv* cache,
+                              uint32_t cache_seq, uint32_t cache_start,
+                              const doe_launch* launch);
 
 /* stitch_kv_axis_sharded_partials (bench/tools/attention_kv_axis_sharded_stitch.py:46-90):
  * partials [rows, num_shards, D+2] f32 rows [O_unnorm[D], local_max,

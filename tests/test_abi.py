@@ -99,8 +99,10 @@ def test_workspace_queries_are_host_side():
     fake = C.c_void_p(0x1000)
     kv = abi.PagedKV(fake, fake, None, None, abi.DOE_KV_F16, 19369, 16, 8, 128, 513, fake)
     ws = lib.doe_paged_decode_workspace_bytes(C.byref(kv), 64, 32, 0)
-    # 64 seqs x 8 kv heads x 17 splits (513 pages / 32-tile splits) x 4 heads x (128 + 2) floats
-    assert ws == 64 * 8 * 17 * 4 * 130 * 4
+    # 64 seqs x 8 kv heads x 17 splits (513 pages / 32-tile splits) x 4 heads x (128 + 2)
+    # floats of partials, then one arrival counter per (sequence, kv head)
+    parts = 64 * 8 * 17 * 4 * 130 * 4
+    assert ws == (parts + 255) // 256 * 256 + 64 * 8 * 4
     assert lib.doe_attention_decode_f32_workspace_bytes(8, 64, 512) == 8 * 8 * 66 * 4
 
 
