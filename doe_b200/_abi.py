@@ -117,6 +117,7 @@ SIGNATURES = {
     "doe_kv_write_dense": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _LP]),
     "doe_kv_read_dense": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _LP]),
     "doe_rope_f32": (_I, [_P, _P, _U32, _U32, _U32, _U32, _LP]),
+    "doe_attention_decode_f32_noalloc": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _F, _P]),
     "doe_kv_pool_create": (_I, [_U32, _U32, _U32, _U32, C.POINTER(_P)]),
     "doe_kv_pool_destroy": (_I, [_P]),
     "doe_kv_pool_reserve": (_I, [_P, _U32, _U32]),

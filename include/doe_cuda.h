@@ -302,6 +302,32 @@ int doe_rope_f32(float* qk, const float* freq_cis, uint32_t seq_len,
                  uint32_t position_offset, const doe_launch* launch);
 
 /* ======================================================================== */
+/* Allocation-free f32 decode.  This entry point has no counterpart in the   */
+/* reference; it exists for callers that cannot allocate device memory.      */
+/* ======================================================================== */
+
+/* Bytes of the scratch array compiled into the library (one per device).   */
+#define DOE_NOALLOC_SCRATCH_BYTES (1u << 18)
+
+/* doe_attention_decode_f32 without a workspace argument, for embedders that
+ * cannot hand the library scratch memory and must not have it allocate any
+ * (a plugin callback with no allocator for temporaries, a serving loop whose
+ * device memory is fixed up front).  The split partials live in a 256 KiB
+ * array inside the library, held on every device that loads it until the
+ * process exits.  The call allocates nothing: no cudaMalloc / cudaFree.
+ *   - Problems whose partials exceed DOE_NOALLOC_SCRATCH_BYTES (num_heads x
+ *     splits x (head_dim + 2) floats) return DOE_INVALID_ARGUMENT.
+ *   - The first call on a device looks up the array's device address; make
+ *     it before any stream capture on that device.
+ *   - All calls share the array: calls whose kernels may overlap on the GPU
+ *     race and must be ordered by the caller.
+ * `stream` is a cudaStream_t (NULL = legacy default stream).               */
+int doe_attention_decode_f32_noalloc(const float* q, const float* k_cache,
+                                     const float* v_cache, float* out,
+                                     uint32_t num_heads, uint32_t head_dim,
+                                     uint32_t kv_len, float scale, void* stream);
+
+/* ======================================================================== */
 /* Host KV page pool -- hands out physical pages and keeps the per-sequence  */
 /* block tables that the paged kernels read (the reference takes one         */
 /* page_table binding per dispatch, attention_head256_f16kv.wgsl:38).       */
