@@ -206,20 +206,37 @@ def paged_step_fn(w, cache, dev, split_pages=0):
     return step
 
 
-def measure_paged(w, fill_seed, steps, warmup, world, pk, split_pages=0):
+def sharded(make, world, rank):
+    """This rank's shard of the global batch: `world` copies of the config
+    (seeds s, s+1, ...) split by sequence with LPT on token counts."""
+    from doe_b200 import shard, workloads
+
+    if world == 1:
+        w = make(0)
+        return w, w
+    gw = workloads.concat([make(r) for r in range(world)])
+    mine = shard.lpt_assign(gw.seq_lens, world)[rank]
+    return workloads.subset(gw, mine), gw
+
+
+def measure_paged(w, fill_seed, steps, warmup, world, pk, split_pages=0, gw=None):
+    gw = gw if gw is not None else w
     cache, dev = build_paged(w, fill_seed)
     step = paged_step_fn(w, cache, dev, split_pages)
     total, each = time_steps(step, steps, warmup, world)
-    total, kern = max_over_ranks(world, [total, float(np.mean(each))])
+    kern_local = float(np.mean(each))
+    total, kern = max_over_ranks(world, [total, kern_local])
     assert int(dev["status"].item()) == 0, f"device status {int(dev['status'].item()):#x}"
     sb = w.step_bytes()
     res = {
         "ms_per_step": total / steps,
-        "gbs": world * sb["total"] * steps / (total / 1e3) / 1e9,
-        "tokens_per_s": world * w.tokens_per_step() * steps / (total / 1e3),
-        "kernel_ms": kern,
-        "kernel_gbs": sb["total"] / (kern / 1e3) / 1e9,
+        "gbs": gw.step_bytes()["total"] * steps / (total / 1e3) / 1e9,
+        "tokens_per_s": gw.tokens_per_step() * steps / (total / 1e3),
+        "kernel_ms": kern_local,
+        "kernel_gbs": sb["total"] / (kern_local / 1e3) / 1e9,
         "bytes_per_step": sb,
+        "global_bytes_per_step": gw.step_bytes()["total"],
+        "sequences_this_rank": w.num_seqs,
     }
     res["frac"] = res["kernel_gbs"] / pk["hbm_gbs"]
     return res, cache, dev
@@ -241,6 +258,7 @@ def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512):
     def step():
         ops.paged_append(cache, nk, nv, pos, status=status)
     total, each = time_steps(step, steps, warmup, world)
+    local_ms = total
     total, = max_over_ranks(world, [total])
     assert int(status.item()) == 0
     rows = w.num_seqs * chunk * w.num_kv_heads
@@ -248,7 +266,7 @@ def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512):
     wr = 2 * rows * (w.head_dim + 2)
     gbs = world * (rd + wr) * steps / (total / 1e3) / 1e9
     return {"ms_per_step": total / steps, "gbs": gbs, "bytes_per_step": rd + wr,
-            "frac": gbs / world / pk["hbm_gbs"]}
+            "frac": (rd + wr) * steps / (local_ms / 1e3) / 1e9 / pk["hbm_gbs"]}
 
 
 def measure_f32(steps, warmup, world, pk):
@@ -317,8 +335,9 @@ def measure_prefill(steps, warmup, world, pk):
             "l2": "flushed (256 MB write) between steps"}
 
 
-def measure_e2e(w, cache, steps, warmup, world):
+def measure_e2e(w, cache, steps, warmup, world, gw=None):
     """Same decode step through doe_cuda_dispatch with host buffers."""
+    gw = gw if gw is not None else w
     import ctypes as C
 
     import torch
@@ -368,9 +387,9 @@ def measure_e2e(w, cache, steps, warmup, world):
     # the e2e output must equal the operator path's output
     ok = bool(np.isfinite(hout.numpy()).all())
     be.close()
-    sb = w.step_bytes()["total"]
-    return {"value": world * sb * steps / elapsed / 1e9, "unit": "GB/s",
-            "tokens_per_s": world * w.tokens_per_step() * steps / elapsed,
+    sb = gw.step_bytes()["total"]
+    return {"value": sb * steps / elapsed / 1e9, "unit": "GB/s",
+            "tokens_per_s": gw.tokens_per_step() * steps / elapsed,
             "ms_per_step": elapsed / steps * 1e3, "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(out_bytes), "timer": "host perf_counter around K steps",
             "output_finite": ok}
@@ -471,7 +490,8 @@ def config_block(w) -> dict:
             "num_seqs": w.num_seqs, "num_heads": w.num_heads, "num_kv_heads": w.num_kv_heads,
             "head_dim": w.head_dim, "page_size": w.page_size, "tokens_in_cache": int(w.ctx.sum()),
             "pages": w.num_pages, "l2": "inputs larger than L2 (1.27 GB KV per step)",
-            "parallelism": "sequence-sharded replicas, no data collective"}
+            "parallelism": "N copies of the config (seeds 2..) sharded by sequence (LPT on tokens), "
+                           "no data collective"}
 
 
 def main():
@@ -506,8 +526,9 @@ def main():
         elif args.only == "f32":
             r = measure_f32(args.steps, args.warmup, world, pk)
         else:
-            w4 = workloads.paged_int8(num_seqs=args.seqs) if args.seqs else workloads.paged_int8()
-            r, _, _ = measure_paged(w4, 3, args.steps, args.warmup, world, pk, args.split_pages)
+            w4, g4 = sharded(lambda r: workloads.paged_int8(seed=3 + r, num_seqs=args.seqs or 32),
+                             world, rank)
+            r, _, _ = measure_paged(w4, 3, args.steps, args.warmup, world, pk, args.split_pages, g4)
         if rank == 0:
             print(json.dumps({"only": args.only, **r}))
         if world > 1:
@@ -515,20 +536,20 @@ def main():
 
             dist.destroy_process_group()
         return
-    w = workloads.paged_f16(num_seqs=args.seqs) if args.seqs else workloads.paged_f16()
+    w, gw = sharded(lambda r: workloads.paged_f16(seed=2 + r, num_seqs=args.seqs or 64), world, rank)
     if args.only == "headline":
         args.no_extras = args.no_cpu = True
     clocks = ClockSampler(local)
     clocks.start()
-    head, cache, dev = measure_paged(w, 2, args.steps, args.warmup, world, pk, args.split_pages)
+    head, cache, dev = measure_paged(w, 2, args.steps, args.warmup, world, pk, args.split_pages, gw)
     clk = clocks.stop()
     del cache, dev
     torch.cuda.empty_cache()
 
     extras = {}
     if not args.no_extras:
-        w4 = workloads.paged_int8()
-        r4, cache4, _ = measure_paged(w4, 3, max(5, args.steps // 2), 3, world, pk)
+        w4, g4 = sharded(lambda r: workloads.paged_int8(seed=3 + r), world, rank)
+        r4, cache4, _ = measure_paged(w4, 3, max(5, args.steps // 2), 3, world, pk, 0, g4)
         ca = measure_chunk_append(w4, cache4, 5, 3, world, pk)
         del cache4
         torch.cuda.empty_cache()
@@ -547,7 +568,7 @@ def main():
     e2e = None
     if args.only == "all":
         cache, dev = build_paged(w, 2)
-        e2e = measure_e2e(w, cache, max(5, args.steps // 2), 2, world)
+        e2e = measure_e2e(w, cache, max(5, args.steps // 2), 2, world, gw)
         del cache, dev
 
     cpu = None
@@ -566,7 +587,7 @@ def main():
             "value": head["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded)",
-            "config": config_block(w), "tokens_per_s": head["tokens_per_s"],
+            "config": config_block(gw), "tokens_per_s": head["tokens_per_s"],
             "roofline": roof, "clocks": clk, "e2e": e2e,
             "gpu_launches": args.steps,  # one paged_decode_kernel per step (plus a 2 KB counter memset)
             "cpu_baseline": cpu, **extras,

@@ -52,11 +52,13 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const 
   }
   float m = -INFINITY, l = 0.0f;
 
-  // four tokens per step: loads issued together, one rescale per step
-  for (int t0 = t_begin + 4 * warp; t0 < t_end; t0 += 4 * kF32Warps) {
-    float kv_k[4][PER_LANE], kv_v[4][PER_LANE];
+  // TOK tokens per warp step (all their K/V loads issued together), one
+  // rescale per step; TOK * PER_LANE = 16 keeps 32 loaded floats per lane
+  constexpr int TOK = 16 / PER_LANE;
+  for (int t0 = t_begin + TOK * warp; t0 < t_end; t0 += TOK * kF32Warps) {
+    float kv_k[TOK][PER_LANE], kv_v[TOK][PER_LANE];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < TOK; ++j) {
       const int t = t0 + j;
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
@@ -66,9 +68,9 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const 
         kv_v[j][i] = ok ? __ldcg(vh + (size_t)t * D + d) : 0.0f;
       }
     }
-    float s[4];
+    float s[TOK];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < TOK; ++j) {
       float part = 0.0f;
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) part = fmaf(qr[i], kv_k[j][i], part);
@@ -77,24 +79,28 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const 
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
+      for (int j = 0; j < TOK; ++j) s[j] += __shfl_xor_sync(0xffffffffu, s[j], o);
     float smax = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < TOK; ++j) {
       s[j] = (t0 + j < t_end) ? s[j] * a.scale : -INFINITY;
       smax = fmaxf(smax, s[j]);
     }
     const float m_new = fmaxf(m, smax);
     const float corr = expf(m - m_new);
-    float p[4];
+    float p[TOK];
+    float psum = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) p[j] = expf(s[j] - m_new);
-    l = l * corr + ((p[0] + p[1]) + (p[2] + p[3]));
+    for (int j = 0; j < TOK; ++j) {
+      p[j] = expf(s[j] - m_new);
+      psum += p[j];
+    }
+    l = l * corr + psum;
 #pragma unroll
     for (int i = 0; i < PER_LANE; ++i) {
       float x = acc[i] * corr;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) x = fmaf(p[j], kv_v[j][i], x);
+      for (int j = 0; j < TOK; ++j) x = fmaf(p[j], kv_v[j][i], x);
       acc[i] = x;
     }
     m = m_new;
@@ -136,13 +142,16 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const 
   }
 }
 
-static void decode_f32_plan(uint32_t num_heads, uint32_t kv_len, int* split_tokens,
-                            int* max_splits) {
-  // aim for >= ~2 CTAs per SM over all heads; 16-token granularity
+static void decode_f32_plan(uint32_t num_heads, uint32_t head_dim, uint32_t kv_len,
+                            int* split_tokens, int* max_splits) {
+  // aim for ~2 CTAs per SM over all heads; a split is a whole number of
+  // 4-warp steps (TOK = 16 / per-lane dims tokens per warp step)
+  const uint32_t per_lane = head_dim <= 64 ? 2 : (head_dim <= 128 ? 4 : 8);
+  const uint32_t chunk = kF32Warps * (16 / per_lane);
   const uint32_t want = num_heads == 0 ? 1 : (296 + num_heads - 1) / num_heads;
   uint32_t st = (kv_len + want - 1) / (want ? want : 1);
-  st = (st + 15) / 16 * 16;
-  if (st < 64) st = 64;
+  st = (st + chunk - 1) / chunk * chunk;
+  if (st < chunk) st = chunk;
   *split_tokens = (int)st;
   *max_splits = (int)((kv_len + st - 1) / st);
   if (*max_splits < 1) *max_splits = 1;
@@ -150,7 +159,7 @@ static void decode_f32_plan(uint32_t num_heads, uint32_t kv_len, int* split_toke
 
 uint64_t decode_f32_workspace(uint32_t num_heads, uint32_t head_dim, uint32_t kv_len) {
   int st, ms;
-  decode_f32_plan(num_heads, kv_len, &st, &ms);
+  decode_f32_plan(num_heads, head_dim, kv_len, &st, &ms);
   if (ms <= 1) return 0;
   return (uint64_t)num_heads * ms * (head_dim + 2) * sizeof(float);
 }
@@ -159,7 +168,7 @@ int launch_decode_f32(const float* q, const float* k, const float* v, float* out
                       uint32_t num_heads, uint32_t head_dim, uint32_t kv_len, float scale,
                       const doe_launch* launch) {
   int st, ms;
-  decode_f32_plan(num_heads, kv_len, &st, &ms);
+  decode_f32_plan(num_heads, head_dim, kv_len, &st, &ms);
   const uint64_t ws = decode_f32_workspace(num_heads, head_dim, kv_len);
   if (ws > 0 && (launch->workspace == nullptr || launch->workspace_bytes < ws)) {
     set_op_error("doe_attention_decode_f32: workspace of %llu bytes required, %llu given",

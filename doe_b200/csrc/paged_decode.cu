@@ -501,30 +501,49 @@ struct CombineArgs {
 
 template <bool LOG2>
 __global__ void combine_splits_kernel(const CombineArgs a) {
+  // all partial (max, sum) pairs of the row are fetched in parallel (one per
+  // thread), weights computed once in shared memory, then every head dim
+  // reads its split values with independent loads.
+  __shared__ float w_sm[1024];
+  __shared__ float inv_sm;
   const int h = blockIdx.x, b = blockIdx.y;
   const int g = h / a.group, hh = h - g * a.group;
   const int len = a.seq_lens ? clamp_len(a.seq_lens[b], a.cap) : a.fixed_len;
   const int nsplits = max(1, (len + a.split_tokens - 1) / a.split_tokens);
   if (nsplits == 1) return;  // the split kernel wrote the output
   const size_t base = ((size_t)b * a.num_kv_heads + g) * a.max_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplits; ++s)
-    M = fmaxf(M, a.part_ml[((base + s) * a.group + hh) * 2]);
-  float L = 0.0f;
-  for (int s = 0; s < nsplits; ++s) {
-    const float* ml = a.part_ml + ((base + s) * a.group + hh) * 2;
-    const float f = M == -INFINITY ? 0.0f : (LOG2 ? exp2f(ml[0] - M) : expf(ml[0] - M));
-    L += f * ml[1];
+  const int tid = threadIdx.x;
+  float m = -INFINITY, lsum = 0.0f;
+  if (tid < nsplits) {
+    const float* ml = a.part_ml + ((base + tid) * a.group + hh) * 2;
+    m = ml[0];
+    lsum = ml[1];
   }
-  const float inv = L > 0.0f ? 1.0f / L : 0.0f;
-  for (int d = threadIdx.x; d < a.head_dim; d += blockDim.x) {
+  float M = m;
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  __shared__ float wmax[32];
+  if ((tid & 31) == 0) wmax[tid >> 5] = M;
+  __syncthreads();
+  M = -INFINITY;
+  for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) M = fmaxf(M, wmax[i]);
+  const float f = (tid < nsplits && M != -INFINITY) ? (LOG2 ? exp2f(m - M) : expf(m - M)) : 0.0f;
+  if (tid < nsplits) w_sm[tid] = f;
+  float fl = f * lsum;
+  for (int o = 16; o > 0; o >>= 1) fl += __shfl_xor_sync(0xffffffffu, fl, o);
+  __syncthreads();
+  if ((tid & 31) == 0) wmax[tid >> 5] = fl;
+  __syncthreads();
+  if (tid == 0) {
+    float L = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) L += wmax[i];
+    inv_sm = L > 0.0f ? 1.0f / L : 0.0f;
+  }
+  __syncthreads();
+  const float inv = inv_sm;
+  for (int d = tid; d < a.head_dim; d += blockDim.x) {
     float O = 0.0f;
-    for (int s = 0; s < nsplits; ++s) {
-      const size_t prow = (base + s) * a.group + hh;
-      const float m = a.part_ml[prow * 2];
-      const float f = M == -INFINITY ? 0.0f : (LOG2 ? exp2f(m - M) : expf(m - M));
-      O += f * a.part_o[prow * a.head_dim + d];
-    }
+    for (int sp = 0; sp < nsplits; ++sp)
+      O += w_sm[sp] * a.part_o[((base + sp) * a.group + hh) * a.head_dim + d];
     a.out[((size_t)b * a.num_kv_heads * a.group + h) * a.head_dim + d] = O * inv;
   }
 }
@@ -556,10 +575,20 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   const uint32_t Hkv = kv->num_kv_heads;
   const uint32_t group = num_heads / Hkv;
   const uint32_t tiles_per_page = kv->page_size / 16;
-  uint32_t split_tiles = split_pages ? split_pages * tiles_per_page : 32;
+  const uint32_t max_tiles = kv->max_pages_per_seq * tiles_per_page;
+  uint32_t split_tiles;
+  if (split_pages) {
+    split_tiles = split_pages * tiles_per_page;
+  } else {
+    // Long splits amortise each CTA's pipeline fill and stitch (64 tiles for
+    // f16, 128 for int8 measured best on config 3 / 4), but a small batch
+    // still needs about four waves of 3 CTAs per SM on 148 SMs.
+    const uint64_t want = ((uint64_t)max_tiles * num_seqs * Hkv + 1775) / 1776;
+    const uint32_t cap = kv->kv_dtype == DOE_KV_INT8 ? 128u : 64u;
+    split_tiles = (uint32_t)(want < 4 ? 4 : (want > cap ? cap : want));
+  }
   if (split_tiles == 0) split_tiles = 1;
   if (split_tiles > 4 * 32) split_tiles = 4 * 32;  // 4 warps x 32 prefetched page ids
-  const uint32_t max_tiles = kv->max_pages_per_seq * tiles_per_page;
   const uint32_t max_splits = max_tiles == 0 ? 1 : ceil_div(max_tiles, split_tiles);
   const uint64_t rows = (uint64_t)num_seqs * Hkv * max_splits * group;
   const uint64_t part_bytes = rows * (kD + 2) * sizeof(float);
@@ -634,7 +663,12 @@ int launch_combine_natural(const float* part_o, const float* part_ml, float* out
   ca.num_kv_heads = rows;
   ca.group = 1;
   ca.head_dim = head_dim;
-  const int threads = head_dim >= 256 ? 256 : ((head_dim + 31) / 32) * 32;
+  int threads = head_dim >= 256 ? 256 : ((head_dim + 31) / 32) * 32;
+  if (threads < max_splits) threads = ((max_splits + 31) / 32) * 32;  // one thread per split
+  if (threads > 1024) {
+    set_op_error("combine: %d splits exceed one block", max_splits);
+    return DOE_UNSUPPORTED;
+  }
   combine_splits_kernel<false><<<dim3(rows, 1), threads, 0, st>>>(ca);
   return cuda_status(cudaGetLastError(), "combine_splits_kernel");
 }

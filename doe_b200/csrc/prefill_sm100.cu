@@ -40,14 +40,14 @@ constexpr uint32_t kTile = 2 * kSub;      // 128 x 128 f16 tile (32 KB)
 constexpr uint32_t OFF_Q = 0;
 constexpr uint32_t OFF_K = OFF_Q + kTile;           // 2 stages
 constexpr uint32_t OFF_V = OFF_K + 2 * kTile;       // 2 stages
-constexpr uint32_t OFF_P = OFF_V + 2 * kTile;
-constexpr uint32_t OFF_BAR = OFF_P + kTile;          // barriers + TMEM slot
+constexpr uint32_t OFF_P = OFF_V + 2 * kTile;       // 2 buffers
+constexpr uint32_t OFF_BAR = OFF_P + 2 * kTile;      // barriers + TMEM slot
 constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;                  // S0 [0,128) S1 [128,256) O [256,384)
 constexpr long long kWaitCycles = 4000000000LL;      // ~2 s at 1.9 GHz
 
 enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1, S_FULL0, S_FULL1,
-           P_FULL, O_FULL, MMA_DONE, NUM_BARS };
+           P_FULL, P_FREE0, P_FREE1, O_FULL, MMA_DONE, NUM_BARS };
 
 struct Args {
   float* out;               // [S, H, D] f32
@@ -97,6 +97,13 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       return false;
     }
   }
+}
+
+// 2^x with the SFU's approximate exp2 (max relative error ~2^-22); -inf -> +0.
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
@@ -313,11 +320,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // A = P (K-major over keys), B = V (MN-major: head dims contiguous)
-          const uint32_t pa = sbase + OFF_P + (kk >> 2) * kSub + (kk & 3) * 32;
+          const uint32_t pa = sbase + OFF_P + (j & 1) * kTile + (kk >> 2) * kSub + (kk & 3) * 32;
           umma(tmem + 256, sdesc(pa, 16, 1024), sdesc(vb + kk * 16 * 128, kSub, 1024), idp,
                (j > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(bar(O_FULL));
+        umma_commit(bar(P_FREE0 + (j & 1)));
         umma_commit(bar(KV_EMPTY0 + (j & 1)));
       }
       // every MMA this thread issued has finished once MMA_DONE flips
@@ -332,70 +340,97 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
-    uint8_t* prow = smem + OFF_P + row * 128;
     for (int j = 0; j < n_kv; ++j) {
       ok = ok && mbar_wait(bar(S_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
       // warp-collective TMEM traffic: a timed-out lane keeps its warp in step
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      float x[BN];
+      const int k0 = j * BN;
+      const uint32_t s_base = lane_base + (j & 1) * 128;
+      // only the diagonal tile (causal) and a ragged last tile need masks
+      const bool masked = (a.causal && j == n_kv - 1) || k0 + BN > a.seq_len;
+      const int key_lim = min(a.seq_len, a.causal ? q_idx + 1 : a.seq_len) - k0;  // keys [0, key_lim) live
+      // pass 1: row max over 8 independent chains (raw scores; the scale is positive)
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        tmem_ld32(lane_base + (j & 1) * 128 + c * 32, r);
+        tmem_ld32(s_base + c * 32, r);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(r[i]);
+          if (masked && c * 32 + i >= key_lim) v = -INFINITY;
+          mx[i & 7] = fmaxf(mx[i & 7], v);
+        }
       }
-      const int k0 = j * BN;
-      float m_t = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN; ++c) {
-        const int key = k0 + c;
-        const bool valid = key < a.seq_len && (!a.causal || key <= q_idx);
-        x[c] = valid ? x[c] * a.scale_log2 : -INFINITY;
-        m_t = fmaxf(m_t, x[c]);
-      }
+      const float m_raw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      const float m_t = m_raw == -INFINITY ? -INFINITY : m_raw * a.scale_log2;
       const bool grow = m_t > m_used + 8.0f;
       const float m_new = grow ? m_t : m_used;
-      const float corr = (grow && m_used != -INFINITY) ? exp2f(m_used - m_new) : 1.0f;
-      float sum = 0.0f;
-      uint32_t ph[BN / 2];
-#pragma unroll
-      for (int c = 0; c < BN; c += 2) {
-        const float p0 = m_new == -INFINITY ? 0.0f : exp2f(x[c] - m_new);
-        const float p1 = m_new == -INFINITY ? 0.0f : exp2f(x[c + 1] - m_new);
-        sum += p0 + p1;
-        ph[c / 2] = pack_half2(p0, p1);
+      const float corr = (grow && m_used != -INFINITY) ? ex2(m_used - m_new) : 1.0f;
+      const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
+      // P buffer j&1 was last read by PV(j-2)
+      if (j >= 2) {
+        ok = mbar_wait(bar(P_FREE0 + (j & 1)), ((j >> 1) - 1) & 1, abort_flag, a.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
       }
+      uint8_t* prow = smem + OFF_P + (j & 1) * kTile + row * 128;
+      float sums[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sums[i] = 0.0f;
+      // pass 2: p = 2^(s * scale * log2e - m), one FFMA + one MUFU.EX2 per score;
+      // each 8-key chunk is a 16-byte piece landing at ch ^ (row & 7) of its
+      // 128-byte swizzled line
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(s_base + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int i0 = q4 * 8 + 2 * e;
+            float v0 = __uint_as_float(r[i0]), v1 = __uint_as_float(r[i0 + 1]);
+            if (masked && c * 32 + i0 >= key_lim) v0 = -INFINITY;
+            if (masked && c * 32 + i0 + 1 >= key_lim) v1 = -INFINITY;
+            const float p0 = ex2(fmaf(v0, a.scale_log2, neg_m));
+            const float p1 = ex2(fmaf(v1, a.scale_log2, neg_m));
+            sums[(q4 * 4 + e) & 7] += p0 + p1;
+            w[e] = pack_half2(p0, p1);
+          }
+          const int ch = c * 4 + q4;
+          const int sub = ch >> 3, cc = ch & 7;
+          *reinterpret_cast<uint4*>(prow + sub * kSub + ((cc ^ (row & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
       l = l * corr + sum;
       m_used = m_new;
-      if (j > 0) {
-        // PV(j-1) must be done: it reads the P buffer and owns O
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // the running max rose: O must be rescaled once PV(j-1) has finished
         ok = mbar_wait(bar(O_FULL), (j - 1) & 1, abort_flag, a.status);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, grow)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(lane_base + 256 + c * 32, r);
-            tmem_wait_ld();
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(lane_base + 256 + c * 32, r);
+          tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-            tmem_st32(lane_base + 256 + c * 32, r);
-          }
-          tmem_wait_st();
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
+          tmem_st32(lane_base + 256 + c * 32, r);
         }
-      }
-      // P row -> two swizzled 128-byte lines (16-byte chunk ch lands at ch ^ (row & 7))
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const int sub = ch >> 3, cc = ch & 7;
-        uint4 v = make_uint4(ph[ch * 4], ph[ch * 4 + 1], ph[ch * 4 + 2], ph[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(prow + sub * kSub + ((cc ^ (row & 7)) << 4)) = v;
+        tmem_wait_st();
       }
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
       tc_fence_before();

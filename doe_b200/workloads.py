@@ -146,6 +146,39 @@ def paged_int8(seed: int = 3, num_seqs: int = 32, chunk: int = 512) -> PagedWork
     return _paged("paged_gqa_decode_int8", seed, num_seqs, 8192, 32768, "int8", extra_tokens=chunk)
 
 
+def concat(parts: list[PagedWorkload], name: str | None = None) -> PagedWorkload:
+    """One batch holding every sequence of `parts`, pages renumbered disjointly."""
+    base = parts[0]
+    tables, off = [], 0
+    width = max(p.block_table.shape[1] for p in parts)
+    for p in parts:
+        t = np.full((p.num_seqs, width), -1, np.int32)
+        live = p.block_table >= 0
+        t[:, :p.block_table.shape[1]][live] = p.block_table[live] + off
+        tables.append(t)
+        off += p.num_pages
+    return PagedWorkload(name or base.name, base.seed, sum(p.num_seqs for p in parts), base.num_heads,
+                         base.num_kv_heads, base.head_dim, base.page_size,
+                         np.concatenate([p.ctx for p in parts]), np.concatenate(tables), off,
+                         np.concatenate([p.q for p in parts]), np.concatenate([p.new_k for p in parts]),
+                         np.concatenate([p.new_v for p in parts]), base.kv_dtype, base.scale,
+                         base.extra_tokens)
+
+
+def subset(w: PagedWorkload, idx) -> PagedWorkload:
+    """The sequences `idx` of `w` with their pages renumbered 0..n-1 (one GPU's shard)."""
+    idx = np.asarray(idx, dtype=np.int64)
+    rows = w.block_table[idx]
+    used = np.unique(rows[rows >= 0])
+    remap = np.full(w.num_pages, -1, np.int32)
+    remap[used] = np.arange(len(used), dtype=np.int32)
+    table = np.where(rows >= 0, remap[np.maximum(rows, 0)], -1).astype(np.int32)
+    return PagedWorkload(w.name, w.seed, len(idx), w.num_heads, w.num_kv_heads, w.head_dim,
+                         w.page_size, w.ctx[idx].copy(), table, int(len(used)), w.q[idx].copy(),
+                         w.new_k[idx].copy(), w.new_v[idx].copy(), w.kv_dtype, w.scale,
+                         w.extra_tokens, {"global_index": idx})
+
+
 def small_paged(seed: int, lens, num_heads=32, num_kv_heads=8, head_dim=128, page_size=16,
                 kv_dtype="f16", extra_tokens=0, spare_pages=0) -> PagedWorkload:
     """A small paged workload with explicit context lengths (tests)."""

@@ -99,11 +99,12 @@ def test_workspace_queries_are_host_side():
     fake = C.c_void_p(0x1000)
     kv = abi.PagedKV(fake, fake, None, None, abi.DOE_KV_F16, 19369, 16, 8, 128, 513, fake)
     ws = lib.doe_paged_decode_workspace_bytes(C.byref(kv), 64, 32, 0)
-    # 64 seqs x 8 kv heads x 17 splits (513 pages / 32-tile splits) x 4 heads x (128 + 2)
+    # 64 seqs x 8 kv heads x 9 splits (513 pages / 64-tile splits) x 4 heads x (128 + 2)
     # floats of partials, then one arrival counter per (sequence, kv head)
-    parts = 64 * 8 * 17 * 4 * 130 * 4
+    parts = 64 * 8 * 9 * 4 * 130 * 4
     assert ws == (parts + 255) // 256 * 256 + 64 * 8 * 4
-    assert lib.doe_attention_decode_f32_workspace_bytes(8, 64, 512) == 8 * 8 * 66 * 4
+    # 8 heads x 16 splits (32-token steps: 4 warps x 8 tokens) x (64 + 2) floats
+    assert lib.doe_attention_decode_f32_workspace_bytes(8, 64, 512) == 8 * 16 * 66 * 4
 
 
 def test_kv_pool_allocation_and_block_table():
