@@ -9,22 +9,27 @@
 // h / (H / Hkv).  The cache write is kv_write generalised to the paged pool
 // (runtime/zig/src/tsir/emit_kernel_body.zig:620-690).
 //
-// One CTA owns 128 query rows of one head and walks the 128-key tiles up to
-// the diagonal (heaviest tiles are launched first):
-//   warp 5     TMA producer: Q once, K/V tiles into a 2-stage ring; on the
-//              diagonal tile it also TMA-stores K/V into the paged cache
-//   warp 4     TMEM owner + MMA issuer (one thread): S = Q K^T into one of two
-//              TMEM S buffers, then O += P V into the TMEM O accumulator
-//   warps 0-3  softmax: thread r owns query row r (TMEM lane r): reads S
-//              (tcgen05.ld), keeps the running max in the log2 domain with a
-//              lazy rescale (O is rescaled in TMEM only when the max grows by
-//              more than 2^8), writes P as f16 into swizzled shared memory;
-//              finally reads O, divides by l and stores f32 rows.
-// Operands are K-major SWIZZLE_128B tiles (Q, K, P) and an MN-major tile (V)
-// described by tcgen05 shared-memory descriptors.  No cluster multicast.
-// Every mbarrier wait is bounded (about one second of clock cycles); on
-// timeout the kernel records DOE_DEVICE_ERR_TIMEOUT, the roles stop, all
-// issued MMAs are waited for (bounded) and TMEM is freed before returning.
+// One CTA owns two 128-row query tiles (A = 2m, B = 2m+1) of one head and
+// walks the 128-key tiles up to B's diagonal (heaviest pairs launch first).
+// The two tiles share every K/V tile:
+//   warp 9     TMA producer: Q_A, Q_B once, K/V tiles into a 2-stage ring; it
+//              also TMA-stores the diagonal K/V tiles into the paged cache
+//   warp 8     TMEM owner + MMA issuer (one thread): S_A = Q_A K^T, S_B =
+//              Q_B K^T, then O_A += P_A V and O_B += P_B V, ping-ponging so the
+//              tensor core works on one tile while the other tile's softmax runs
+//   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread r owns
+//              query row r (TMEM lane r); two passes over S in TMEM (row max,
+//              then 2^(s*scale - max)); P is written back as f16 into the S
+//              columns it came from and feeds the PV MMA straight from TMEM;
+//              the running max grows lazily (O is rescaled in TMEM only when
+//              it rises by more than 2^8); finally O / l -> f32 rows.
+// TMEM: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_x aliases
+// the first 64 columns of S_x.  A commit on S_x(j+1) covers PV_x(j), so when
+// a softmax warp sees S_x(j+1) its P buffer is free and O_x is quiescent.
+// Operands: Q, K K-major SWIZZLE_128B smem tiles; V an MN-major smem tile;
+// P from TMEM.  No cluster multicast.  Every mbarrier wait is bounded (~2 s
+// of clock cycles); on timeout the kernel records DOE_DEVICE_ERR_TIMEOUT, the
+// roles stop, all issued MMAs are waited for (bounded) and TMEM is freed.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -34,26 +39,25 @@ namespace doe {
 namespace pf {
 
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr uint32_t kSub = 128 * 128;      // one 128-row x 64-half swizzled sub-tile (16 KB)
 constexpr uint32_t kTile = 2 * kSub;      // 128 x 128 f16 tile (32 KB)
-constexpr uint32_t OFF_Q = 0;
-constexpr uint32_t OFF_K = OFF_Q + kTile;           // 2 stages
-constexpr uint32_t OFF_V = OFF_K + 2 * kTile;       // 2 stages
-constexpr uint32_t OFF_P = OFF_V + 2 * kTile;       // 2 buffers
-constexpr uint32_t OFF_BAR = OFF_P + 2 * kTile;      // barriers + TMEM slot
+constexpr uint32_t OFF_Q = 0;                        // Q_A, Q_B
+constexpr uint32_t OFF_K = OFF_Q + 2 * kTile;        // 2 stages
+constexpr uint32_t OFF_V = OFF_K + 2 * kTile;        // 2 stages
+constexpr uint32_t OFF_BAR = OFF_V + 2 * kTile;      // barriers + TMEM slot
 constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;  // + alignment slack
-constexpr uint32_t kTmemCols = 512;                  // S0 [0,128) S1 [128,256) O [256,384)
+constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 4000000000LL;      // ~2 s at 1.9 GHz
 
-enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1, S_FULL0, S_FULL1,
-           P_FULL, P_FREE0, P_FREE1, O_FULL, MMA_DONE, NUM_BARS };
+enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1, S_FULL_A, S_FULL_B,
+           P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, MMA_DONE, NUM_BARS };
 
 struct Args {
   float* out;               // [S, H, D] f32
   int32_t* status;
   const int32_t* table;     // block-table row of the cache sequence (or null)
-  int seq_len, num_heads, num_kv_heads, n_qtiles, causal;
+  int seq_len, num_heads, num_kv_heads, n_qtiles, n_pairs, causal;
   int cache_page_size, cache_num_pages, cache_max_pages, cache_start;
   float scale_log2;
 };
@@ -149,6 +153,16 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, ui
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]: A (M x 16, f16 pairs packed per 32-bit
+// column, row m in lane m) read from tensor memory.
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
                : "memory");
@@ -189,6 +203,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       DOE_W32(r)
       : "memory");
 }
+// 16 consecutive TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+      "%13,%14,%15,%16};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -210,19 +233,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int H = a.num_heads;
-  const int t_order = blockIdx.x / H;
-  const int h = blockIdx.x - t_order * H;
-  const int qtile = a.n_qtiles - 1 - t_order;  // heaviest (longest) rows first
+  const int order = blockIdx.x / H;
+  const int h = blockIdx.x - order * H;
+  const int pair = a.n_pairs - 1 - order;  // heaviest (longest) rows first
   const int hk = h / (H / a.num_kv_heads);
-  const int q0 = qtile * BM;
-  const int n_kv = a.causal ? qtile + 1 : (a.seq_len + BN - 1) / BN;
+  const int n_kv_all = (a.seq_len + BN - 1) / BN;
+  // tile t = 2*pair + x (x = 0: A, 1: B); n[x] = key tiles it attends
+  const int tA = 2 * pair, tB = 2 * pair + 1;
+  const bool hasB = tB < a.n_qtiles;
+  const int nA = a.causal ? tA + 1 : n_kv_all;
+  const int nB = hasB ? (a.causal ? tB + 1 : n_kv_all) : 0;
+  const int n_kv = nA > nB ? nA : nB;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), i == P_FULL ? 4u : 1u);
+    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i == P_FULL_A || i == P_FULL_B) ? 4u : 1u);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (warp == 4) {
+  if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols));
@@ -233,12 +261,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 5) {
+  if (warp == 9) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      mbar_expect_tx(bar(Q_FULL), kTile);
-      tma_load_3d(sbase + OFF_Q, &tm_q, bar(Q_FULL), 0, h, q0);
-      tma_load_3d(sbase + OFF_Q + kSub, &tm_q, bar(Q_FULL), 64, h, q0);
+      mbar_expect_tx(bar(Q_FULL), (hasB ? 2 : 1) * kTile);
+      tma_load_3d(sbase + OFF_Q, &tm_q, bar(Q_FULL), 0, h, tA * BM);
+      tma_load_3d(sbase + OFF_Q + kSub, &tm_q, bar(Q_FULL), 64, h, tA * BM);
+      if (hasB) {
+        tma_load_3d(sbase + OFF_Q + kTile, &tm_q, bar(Q_FULL), 0, h, tB * BM);
+        tma_load_3d(sbase + OFF_Q + kTile + kSub, &tm_q, bar(Q_FULL), 64, h, tB * BM);
+      }
       bool ok = true;
       for (int j = 0; j < n_kv && ok; ++j) {
         const int st = j & 1;
@@ -252,14 +284,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(vd, &tm_v, bar(V_FULL0 + st), 0, hk, j * BN);
         tma_load_3d(vd + kSub, &tm_v, bar(V_FULL0 + st), 64, hk, j * BN);
       }
-      // the diagonal CTA of the first head of each kv group writes this
-      // tile's K/V rows into the paged cache (16-row boxes: one page slice each)
-      const int j = n_kv - 1;
+      // causal: the key tiles tA and tB are this CTA's diagonals; the first head
+      // of each kv group writes their K/V rows into the paged cache (16-row
+      // boxes: one page slice each).  Both are the last two tiles loaded, so
+      // they still sit in the ring.
       if (ok && a.table != nullptr && a.causal && (h % (H / a.num_kv_heads)) == 0) {
-        const int st = j & 1;
-        ok = mbar_wait(bar(K_FULL0 + st), (j >> 1) & 1, abort_flag, a.status) &&
-             mbar_wait(bar(V_FULL0 + st), (j >> 1) & 1, abort_flag, a.status);
-        if (ok) {
+        for (int j = (n_kv >= 2 ? n_kv - 2 : 0); j < n_kv && ok; ++j) {
+          if (j != tA && j != tB) continue;
+          const int st = j & 1;
+          ok = mbar_wait(bar(K_FULL0 + st), (j >> 1) & 1, abort_flag, a.status) &&
+               mbar_wait(bar(V_FULL0 + st), (j >> 1) & 1, abort_flag, a.status);
+          if (!ok) break;
           asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
           for (int m = 0; m < BN / 16; ++m) {
             const int tok = j * BN + m * 16;
@@ -278,54 +313,58 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_store_3d(&tm_cv, sbase + OFF_V + off, sub * 64, hk, row);
             }
           }
-          asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
-          asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
         }
+        asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idq = idesc_f16(false), idp = idesc_f16(true);
-      auto issue_s = [&](int j) {
-        const int st = j & 1;
-        const uint32_t kb = sbase + OFF_K + st * kTile;
-        const uint32_t d = tmem + st * 128;
+      // S_x(j) = Q_x K_j^T into TMEM columns [128x, 128x + 128)
+      auto issue_s = [&](int x, int j) {
+        const uint32_t kb = sbase + OFF_K + (j & 1) * kTile;
+        const uint32_t qb = sbase + OFF_Q + x * kTile;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
-          umma(d, sdesc(sbase + OFF_Q + off, 16, 1024), sdesc(kb + off, 16, 1024), idq, kk > 0);
+          umma(tmem + x * 128, sdesc(qb + off, 16, 1024), sdesc(kb + off, 16, 1024), idq, kk > 0);
         }
-        umma_commit(bar(S_FULL0 + st));
+        umma_commit(bar(S_FULL_A + x));
       };
+      // O_x += P_x V_j with P_x (f16) in TMEM columns [128x, 128x + 64)
+      auto issue_pv = [&](int x, int j) {
+        const uint32_t vb = sbase + OFF_V + (j & 1) * kTile;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, sdesc(vb + kk * 16 * 128, kSub, 1024),
+                  idp, (j > 0 || kk > 0) ? 1u : 0u);
+      };
+      const int nx[2] = {nA, nB};
       bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag, a.status) &&
                 mbar_wait(bar(K_FULL0), 0, abort_flag, a.status);
       if (ok) {
         tc_fence_after();
-        issue_s(0);
+        for (int x = 0; x < 2; ++x)
+          if (nx[x] > 0) issue_s(x, 0);
       }
       for (int j = 0; j < n_kv && ok; ++j) {
-        if (j + 1 < n_kv) {
-          const int st = (j + 1) & 1;
-          ok = mbar_wait(bar(K_FULL0 + st), ((j + 1) >> 1) & 1, abort_flag, a.status);
+        ok = mbar_wait(bar(V_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
+        for (int x = 0; x < 2 && ok; ++x) {
+          if (j >= nx[x]) continue;
+          ok = mbar_wait(bar(P_FULL_A + x), j & 1, abort_flag, a.status);
           if (!ok) break;
           tc_fence_after();
-          issue_s(j + 1);
+          issue_pv(x, j);
+          if (j == nx[x] - 1) umma_commit(bar(O_FULL_A + x));
+          if (j + 1 < nx[x]) {
+            ok = mbar_wait(bar(K_FULL0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag, a.status);
+            if (!ok) break;
+            tc_fence_after();
+            issue_s(x, j + 1);
+          }
         }
-        ok = mbar_wait(bar(P_FULL), j & 1, abort_flag, a.status) &&
-             mbar_wait(bar(V_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
-        if (!ok) break;
-        tc_fence_after();
-        const uint32_t vb = sbase + OFF_V + (j & 1) * kTile;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          // A = P (K-major over keys), B = V (MN-major: head dims contiguous)
-          const uint32_t pa = sbase + OFF_P + (j & 1) * kTile + (kk >> 2) * kSub + (kk & 3) * 32;
-          umma(tmem + 256, sdesc(pa, 16, 1024), sdesc(vb + kk * 16 * 128, kSub, 1024), idp,
-               (j > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(bar(O_FULL));
-        umma_commit(bar(P_FREE0 + (j & 1)));
         umma_commit(bar(KV_EMPTY0 + (j & 1)));
       }
       // every MMA this thread issued has finished once MMA_DONE flips
@@ -335,22 +374,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
-    const int row = warp * 32 + lane;
-    const int q_idx = q0 + row;
-    const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    const int x = warp >> 2, wl = warp & 3;      // tile A (x = 0) or B (x = 1)
+    const int nt = x == 0 ? nA : nB;
+    const int row = wl * 32 + lane;
+    const int q_idx = (x == 0 ? tA : tB) * BM + row;
+    const uint32_t lane_base = tmem + ((uint32_t)(wl * 32) << 16);
+    const uint32_t s_col = x * 128, o_col = 256 + x * 128;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      ok = ok && mbar_wait(bar(S_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
-      // warp-collective TMEM traffic: a timed-out lane keeps its warp in step
-      ok = __all_sync(0xffffffffu, ok);
+    for (int j = 0; j < nt; ++j) {
+      // S_x(j) is ready; its commit also covers PV_x(j-1): P buffer free, O quiescent
+      ok = ok && mbar_wait(bar(S_FULL_A + x), j & 1, abort_flag, a.status);
+      ok = __all_sync(0xffffffffu, ok);  // TMEM ops are warp-collective
       if (!ok) break;
       tc_fence_after();
       const int k0 = j * BN;
-      const uint32_t s_base = lane_base + (j & 1) * 128;
-      // only the diagonal tile (causal) and a ragged last tile need masks
-      const bool masked = (a.causal && j == n_kv - 1) || k0 + BN > a.seq_len;
-      const int key_lim = min(a.seq_len, a.causal ? q_idx + 1 : a.seq_len) - k0;  // keys [0, key_lim) live
+      const bool masked = (a.causal && j == nt - 1) || k0 + BN > a.seq_len;
+      const int key_lim = min(a.seq_len, a.causal ? q_idx + 1 : a.seq_len) - k0;  // live keys [0, key_lim)
       // pass 1: row max over 8 independent chains (raw scores; the scale is positive)
       float mx[8];
 #pragma unroll
@@ -358,13 +398,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        tmem_ld32(s_base + c * 32, r);
+        tmem_ld32(lane_base + s_col + c * 32, r);
         tmem_wait_ld();
+        if (masked) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float v = __uint_as_float(r[i]);
-          if (masked && c * 32 + i >= key_lim) v = -INFINITY;
-          mx[i & 7] = fmaxf(mx[i & 7], v);
+          for (int i = 0; i < 32; ++i)
+            mx[i & 7] = fmaxf(mx[i & 7], c * 32 + i < key_lim ? __uint_as_float(r[i]) : -INFINITY);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
         }
       }
       const float m_raw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
@@ -374,87 +416,71 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float m_new = grow ? m_t : m_used;
       const float corr = (grow && m_used != -INFINITY) ? ex2(m_used - m_new) : 1.0f;
       const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
-      // P buffer j&1 was last read by PV(j-2)
-      if (j >= 2) {
-        ok = mbar_wait(bar(P_FREE0 + (j & 1)), ((j >> 1) - 1) & 1, abort_flag, a.status);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-      }
-      uint8_t* prow = smem + OFF_P + (j & 1) * kTile + row * 128;
-      float sums[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sums[i] = 0.0f;
-      // pass 2: p = 2^(s * scale * log2e - m), one FFMA + one MUFU.EX2 per score;
-      // each 8-key chunk is a 16-byte piece landing at ch ^ (row & 7) of its
-      // 128-byte swizzled line
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(s_base + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int i0 = q4 * 8 + 2 * e;
-            float v0 = __uint_as_float(r[i0]), v1 = __uint_as_float(r[i0 + 1]);
-            if (masked && c * 32 + i0 >= key_lim) v0 = -INFINITY;
-            if (masked && c * 32 + i0 + 1 >= key_lim) v1 = -INFINITY;
-            const float p0 = ex2(fmaf(v0, a.scale_log2, neg_m));
-            const float p1 = ex2(fmaf(v1, a.scale_log2, neg_m));
-            sums[(q4 * 4 + e) & 7] += p0 + p1;
-            w[e] = pack_half2(p0, p1);
-          }
-          const int ch = c * 4 + q4;
-          const int sub = ch >> 3, cc = ch & 7;
-          *reinterpret_cast<uint4*>(prow + sub * kSub + ((cc ^ (row & 7)) << 4)) =
-              make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
-      l = l * corr + sum;
-      m_used = m_new;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // the running max rose: O must be rescaled once PV(j-1) has finished
-        ok = mbar_wait(bar(O_FULL), (j - 1) & 1, abort_flag, a.status);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
+        // the running max rose by more than 2^8: rescale this row of O
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
-          tmem_ld32(lane_base + 256 + c * 32, r);
+          tmem_ld32(lane_base + o_col + c * 32, r);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-          tmem_st32(lane_base + 256 + c * 32, r);
+          tmem_st32(lane_base + o_col + c * 32, r);
         }
-        tmem_wait_st();
       }
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar(P_FULL));
-    }
-    // ---- epilogue: O / l -> out
-    if (ok) ok = mbar_wait(bar(O_FULL), (n_kv - 1) & 1, abort_flag, a.status);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      tc_fence_after();
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      float* orow = a.out + ((size_t)q_idx * H + h) * HD;
+      // pass 2: p = 2^(s * scale * log2e - m) (one FFMA + one MUFU.EX2 per score),
+      // packed to f16 pairs and stored over the S columns already read
+      float sums[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sums[i] = 0.0f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        tmem_ld32(lane_base + 256 + c * 32, r);
+        tmem_ld32(lane_base + s_col + c * 32, r);
         tmem_wait_ld();
-        if (q_idx < a.seq_len) {
+        uint32_t w[16];
 #pragma unroll
-          for (int i = 0; i < 32; i += 4) {
-            float4 o = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                   __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
-            *reinterpret_cast<float4*>(orow + c * 32 + i) = o;
+        for (int e = 0; e < 16; ++e) {
+          float v0 = __uint_as_float(r[2 * e]), v1 = __uint_as_float(r[2 * e + 1]);
+          if (masked) {
+            if (c * 32 + 2 * e >= key_lim) v0 = -INFINITY;
+            if (c * 32 + 2 * e + 1 >= key_lim) v1 = -INFINITY;
+          }
+          const float p0 = ex2(fmaf(v0, a.scale_log2, neg_m));
+          const float p1 = ex2(fmaf(v1, a.scale_log2, neg_m));
+          sums[e & 7] += p0 + p1;
+          w[e] = pack_half2(p0, p1);
+        }
+        tmem_st16(lane_base + s_col + c * 16, w);
+      }
+      tmem_wait_st();
+      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+      l = l * corr + sum;
+      m_used = m_new;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(P_FULL_A + x));
+    }
+    // ---- epilogue: O / l -> out
+    if (nt > 0) {
+      if (ok) ok = mbar_wait(bar(O_FULL_A + x), 0, abort_flag, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok) {
+        tc_fence_after();
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        float* orow = a.out + ((size_t)q_idx * H + h) * HD;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(lane_base + o_col + c * 32, r);
+          tmem_wait_ld();
+          if (q_idx < a.seq_len) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              float4 o = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
+                                     __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
+              *reinterpret_cast<float4*>(orow + c * 32 + i) = o;
+            }
           }
         }
       }
@@ -463,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 8) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }
@@ -532,6 +558,7 @@ int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, 
   a.num_heads = (int)num_heads;
   a.num_kv_heads = (int)num_kv_heads;
   a.n_qtiles = (int)((seq_len + 127) / 128);
+  a.n_pairs = (a.n_qtiles + 1) / 2;
   a.causal = causal ? 1 : 0;
   a.cache_page_size = a.cache_num_pages = a.cache_max_pages = a.cache_start = 0;
   a.scale_log2 = scale * kLog2e;
@@ -557,7 +584,7 @@ int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, 
     if (rc != DOE_OK) return rc;
     attr_set = true;
   }
-  const uint64_t ctas = (uint64_t)a.n_qtiles * num_heads;
+  const uint64_t ctas = (uint64_t)a.n_pairs * num_heads;
   pf::prefill_kernel<<<(unsigned)ctas, pf::kThreads, pf::kSmemBytes,
                        static_cast<cudaStream_t>(launch->stream)>>>(mq, mk, mv, mck, mcv, a);
   return cuda_status(cudaGetLastError(), "prefill_kernel");
