@@ -12,17 +12,19 @@
 // One CTA owns two 128-row query tiles (A = 2m, B = 2m+1) of one head and
 // walks the 128-key tiles up to B's diagonal (heaviest pairs launch first).
 // The two tiles share every K/V tile:
-//   warp 9     TMA producer: Q_A, Q_B once, K/V tiles into a 2-stage ring; it
+//   warp 17    TMA producer: Q_A, Q_B once, K/V tiles into a 2-stage ring; it
 //              also TMA-stores the diagonal K/V tiles into the paged cache
-//   warp 8     TMEM owner + MMA issuer (one thread): S_A = Q_A K^T, S_B =
+//   warp 16    TMEM owner + MMA issuer (one thread): S_A = Q_A K^T, S_B =
 //              Q_B K^T, then O_A += P_A V and O_B += P_B V, ping-ponging so the
 //              tensor core works on one tile while the other tile's softmax runs
-//   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: thread r owns
-//              query row r (TMEM lane r); two passes over S in TMEM (row max,
-//              then 2^(s*scale - max)); P is written back as f16 into the S
-//              columns it came from and feeds the PV MMA straight from TMEM;
-//              the running max grows lazily (O is rescaled in TMEM only when
-//              it rises by more than 2^8); finally O / l -> f32 rows.
+//   warps 0-7  softmax of tile A, warps 8-15 softmax of tile B: row r (TMEM
+//              lane r) is shared by two threads, one per half of the 128 keys
+//              (warps w and w + 4 of a tile); each reads its 64 scores from TMEM
+//              once, the pair agrees on the row max through shared memory, and
+//              each writes its half of P as f16 over S columns the pair has
+//              already read; P feeds the PV MMA straight from TMEM.  The running
+//              max grows lazily (O is rescaled in TMEM only when it rises by
+//              more than 2^8); finally O / l -> f32 rows.
 // TMEM: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_x aliases
 // the first 64 columns of S_x.  A commit on S_x(j+1) covers PV_x(j), so when
 // a softmax warp sees S_x(j+1) its P buffer is free and O_x is quiescent.
@@ -39,19 +41,20 @@ namespace doe {
 namespace pf {
 
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int kThreads = 320;
+constexpr int kThreads = 576;  // 16 softmax warps + MMA warp + TMA warp
 constexpr uint32_t kSub = 128 * 128;      // one 128-row x 64-half swizzled sub-tile (16 KB)
 constexpr uint32_t kTile = 2 * kSub;      // 128 x 128 f16 tile (32 KB)
 constexpr uint32_t OFF_Q = 0;                        // Q_A, Q_B
 constexpr uint32_t OFF_K = OFF_Q + 2 * kTile;        // 2 stages
 constexpr uint32_t OFF_V = OFF_K + 2 * kTile;        // 2 stages
 constexpr uint32_t OFF_BAR = OFF_V + 2 * kTile;      // barriers + TMEM slot
-constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;  // + alignment slack
+constexpr uint32_t OFF_XCHG = OFF_BAR + 256;         // row max / sum exchange: [parity][tile][half][128]
+constexpr uint32_t kSmemBytes = OFF_XCHG + 2 * 2 * 2 * 128 * 4 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 4000000000LL;      // ~2 s at 1.9 GHz
 
-enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, KV_EMPTY0, KV_EMPTY1, S_FULL_A, S_FULL_B,
-           P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, MMA_DONE, NUM_BARS };
+enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, K_EMPTY0, K_EMPTY1, V_EMPTY0, V_EMPTY1,
+           S_FULL_A, S_FULL_B, P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, MMA_DONE, NUM_BARS };
 
 struct Args {
   float* out;               // [S, H, D] f32
@@ -212,6 +215,14 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
       : "memory");
 }
+// 16 consecutive TMEM columns of this thread's lane (warp-collective).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 }
@@ -246,11 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kv = nA > nB ? nA : nB;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i == P_FULL_A || i == P_FULL_B) ? 4u : 1u);
+    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i == P_FULL_A || i == P_FULL_B) ? 8u : 1u);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (warp == 8) {
+  if (warp == 16) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols));
@@ -261,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 9) {
+  if (warp == 17) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       mbar_expect_tx(bar(Q_FULL), (hasB ? 2 : 1) * kTile);
@@ -271,18 +282,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_3d(sbase + OFF_Q + kTile, &tm_q, bar(Q_FULL), 0, h, tB * BM);
         tma_load_3d(sbase + OFF_Q + kTile + kSub, &tm_q, bar(Q_FULL), 64, h, tB * BM);
       }
-      bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
+      // K runs one tile ahead of V: the MMA issuer is done with K(j) an
+      // iteration before it is done with V(j) (S_x(j) is issued while PV_x(j-1)
+      // is), so each ring slot is refilled as soon as its own tile is released.
+      // Tile i of a ring is released by the (i/2)-th arrival on its EMPTY barrier.
+      auto load = [&](int ring, int j) -> bool {
         const int st = j & 1;
-        if (j >= 2) ok = mbar_wait(bar(KV_EMPTY0 + st), ((j >> 1) - 1) & 1, abort_flag, a.status);
-        if (!ok) break;
-        const uint32_t kd = sbase + OFF_K + st * kTile, vd = sbase + OFF_V + st * kTile;
-        mbar_expect_tx(bar(K_FULL0 + st), kTile);
-        tma_load_3d(kd, &tm_k, bar(K_FULL0 + st), 0, hk, j * BN);
-        tma_load_3d(kd + kSub, &tm_k, bar(K_FULL0 + st), 64, hk, j * BN);
-        mbar_expect_tx(bar(V_FULL0 + st), kTile);
-        tma_load_3d(vd, &tm_v, bar(V_FULL0 + st), 0, hk, j * BN);
-        tma_load_3d(vd + kSub, &tm_v, bar(V_FULL0 + st), 64, hk, j * BN);
+        if (j >= 2 &&
+            !mbar_wait(bar((ring == 0 ? K_EMPTY0 : V_EMPTY0) + st), ((j >> 1) - 1) & 1, abort_flag, a.status))
+          return false;
+        const uint32_t full = bar((ring == 0 ? K_FULL0 : V_FULL0) + st);
+        const uint32_t dst = sbase + (ring == 0 ? OFF_K : OFF_V) + st * kTile;
+        const CUtensorMap* map = ring == 0 ? &tm_k : &tm_v;
+        mbar_expect_tx(full, kTile);
+        tma_load_3d(dst, map, full, 0, hk, j * BN);
+        tma_load_3d(dst + kSub, map, full, 64, hk, j * BN);
+        return true;
+      };
+      bool ok = load(0, 0);
+      for (int j = 0; j < n_kv && ok; ++j) {
+        if (j + 1 < n_kv) ok = load(0, j + 1);
+        if (ok) ok = load(1, j);
       }
       // causal: the key tiles tA and tB are this CTA's diagonals; the first head
       // of each kv group writes their K/V rows into the paged cache (16-row
@@ -318,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
       }
     }
-  } else if (warp == 8) {
+  } else if (warp == 16) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idq = idesc_f16(false), idp = idesc_f16(true);
@@ -348,24 +368,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         for (int x = 0; x < 2; ++x)
           if (nx[x] > 0) issue_s(x, 0);
+        umma_commit(bar(K_EMPTY0));  // K(0) released once S_x(0) are done
       }
       for (int j = 0; j < n_kv && ok; ++j) {
         ok = mbar_wait(bar(V_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
+        bool k_ready = false;  // K(j+1) seen complete
         for (int x = 0; x < 2 && ok; ++x) {
           if (j >= nx[x]) continue;
+          // every mbarrier wait here stalls the issue stream (~100 cycles even
+          // when the phase is complete), so each is taken only once per step
           ok = mbar_wait(bar(P_FULL_A + x), j & 1, abort_flag, a.status);
           if (!ok) break;
           tc_fence_after();
           issue_pv(x, j);
           if (j == nx[x] - 1) umma_commit(bar(O_FULL_A + x));
           if (j + 1 < nx[x]) {
-            ok = mbar_wait(bar(K_FULL0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag, a.status);
-            if (!ok) break;
+            if (!k_ready) {
+              ok = mbar_wait(bar(K_FULL0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag, a.status);
+              if (!ok) break;
+              k_ready = true;
+            }
             tc_fence_after();
             issue_s(x, j + 1);
           }
         }
-        umma_commit(bar(KV_EMPTY0 + (j & 1)));
+        if (!ok) break;
+        if (j + 1 < n_kv) umma_commit(bar(K_EMPTY0 + ((j + 1) & 1)));  // K(j+1): S_x(j+1) issued
+        umma_commit(bar(V_EMPTY0 + (j & 1)));                          // V(j): PV_x(j) issued
       }
       // every MMA this thread issued has finished once MMA_DONE flips
       umma_commit(bar(MMA_DONE));
@@ -374,112 +403,129 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
-    const int x = warp >> 2, wl = warp & 3;      // tile A (x = 0) or B (x = 1)
+    const int x = warp >> 3;                 // tile A (x = 0) or B (x = 1)
+    const int half = (warp >> 2) & 1;        // keys [64 half, 64 half + 64)
+    const int wl = warp & 3;                 // TMEM lane group
     const int nt = x == 0 ? nA : nB;
     const int row = wl * 32 + lane;
     const int q_idx = (x == 0 ? tA : tB) * BM + row;
     const uint32_t lane_base = tmem + ((uint32_t)(wl * 32) << 16);
-    const uint32_t s_col = x * 128, o_col = 256 + x * 128;
+    const uint32_t s_col = x * 128 + half * 64, o_col = 256 + x * 128 + half * 64;
+    const uint32_t p_col = x * 128 + half * 32;  // P keys 2c, 2c+1 live in column c
+    // [parity][tile][half][row]: iteration j uses parity j & 1, so one pair
+    // barrier per iteration suffices (a warp cannot reuse a parity before its
+    // partner has passed the next iteration's barrier)
+    float* xchg = reinterpret_cast<float*>(smem + OFF_XCHG) + x * 256;
+    const int pair_bar = 1 + x * 4 + wl;     // named barrier of the warp pair (w, w + 4)
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
+    // Both warps of a pair run every iteration and every pair barrier: after a
+    // timed-out wait a warp skips its TMEM work and arrivals but keeps step,
+    // so the named barriers (which have no timeout) always match.
     for (int j = 0; j < nt; ++j) {
       // S_x(j) is ready; its commit also covers PV_x(j-1): P buffer free, O quiescent
-      ok = ok && mbar_wait(bar(S_FULL_A + x), j & 1, abort_flag, a.status);
+      if (ok) ok = mbar_wait(bar(S_FULL_A + x), j & 1, abort_flag, a.status);
       ok = __all_sync(0xffffffffu, ok);  // TMEM ops are warp-collective
-      if (!ok) break;
-      tc_fence_after();
-      const int k0 = j * BN;
-      const bool masked = (a.causal && j == nt - 1) || k0 + BN > a.seq_len;
+      uint32_t r[64];
+      if (ok) {
+        tc_fence_after();
+        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+        tmem_ld32(lane_base + s_col, r0);
+        tmem_ld32(lane_base + s_col + 32, r1);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) r[i] = 0u;
+      }
+      const int k0 = j * BN + half * 64;
+      const bool masked = (a.causal && j == nt - 1) || j * BN + BN > a.seq_len;
       const int key_lim = min(a.seq_len, a.causal ? q_idx + 1 : a.seq_len) - k0;  // live keys [0, key_lim)
-      // pass 1: row max over 8 independent chains (raw scores; the scale is positive)
+      if (masked) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i >= key_lim) r[i] = __float_as_uint(-INFINITY);
+      }
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(r[i]);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + s_col + c * 32, r);
-        tmem_wait_ld();
-        if (masked) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            mx[i & 7] = fmaxf(mx[i & 7], c * 32 + i < key_lim ? __uint_as_float(r[i]) : -INFINITY);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
-        }
-      }
-      const float m_raw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
+      float m_raw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                          fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      // the pair's agreed row max; the barrier also proves both halves have
+      // read their S columns before either overwrites S with P
+      float* xb = xchg + (j & 1) * 512;
+      xb[half * 128 + row] = m_raw;
+      asm volatile("bar.sync %0, 64;\n" ::"r"(pair_bar) : "memory");
+      m_raw = fmaxf(m_raw, xb[(half ^ 1) * 128 + row]);
       const float m_t = m_raw == -INFINITY ? -INFINITY : m_raw * a.scale_log2;
       const bool grow = m_t > m_used + 8.0f;
       const float m_new = grow ? m_t : m_used;
       const float corr = (grow && m_used != -INFINITY) ? ex2(m_used - m_new) : 1.0f;
       const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // the running max rose by more than 2^8: rescale this row of O
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(lane_base + o_col + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * corr);
-          tmem_st32(lane_base + o_col + c * 32, r);
-        }
-      }
-      // pass 2: p = 2^(s * scale * log2e - m) (one FFMA + one MUFU.EX2 per score),
-      // packed to f16 pairs and stored over the S columns already read
+      if (!ok) continue;  // barriers above were kept in step; nothing else to do
+      // p = 2^(s * scale * log2e - m): one FFMA + one MUFU.EX2 per score
       float sums[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) sums[i] = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_base + s_col + c * 32, r);
-        tmem_wait_ld();
+      for (int c = 0; c < 2; ++c) {
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          float v0 = __uint_as_float(r[2 * e]), v1 = __uint_as_float(r[2 * e + 1]);
-          if (masked) {
-            if (c * 32 + 2 * e >= key_lim) v0 = -INFINITY;
-            if (c * 32 + 2 * e + 1 >= key_lim) v1 = -INFINITY;
-          }
-          const float p0 = ex2(fmaf(v0, a.scale_log2, neg_m));
-          const float p1 = ex2(fmaf(v1, a.scale_log2, neg_m));
+          const float p0 = ex2(fmaf(__uint_as_float(r[c * 32 + 2 * e]), a.scale_log2, neg_m));
+          const float p1 = ex2(fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), a.scale_log2, neg_m));
           sums[e & 7] += p0 + p1;
           w[e] = pack_half2(p0, p1);
         }
-        tmem_st16(lane_base + s_col + c * 16, w);
+        tmem_st16(lane_base + p_col + c * 16, w);
       }
-      tmem_wait_st();
-      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
-      l = l * corr + sum;
-      m_used = m_new;
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        // the running max rose by more than 2^8: rescale this half-row of O
+        // (quiescent: S_x(j)'s commit covered PV_x(j-1), and PV_x(j) waits for
+        // this warp's P_FULL arrival below)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // 16 columns at a time
+          uint32_t o[16];
+          tmem_ld16(lane_base + o_col + c * 16, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * corr);
+          tmem_st16(lane_base + o_col + c * 16, o);
+        }
+      }
+      tmem_wait_st();  // P (and any O rescale) has landed
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(P_FULL_A + x));
+      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
+      l = l * corr + sum;  // this half's share of the row sum
+      m_used = m_new;
     }
-    // ---- epilogue: O / l -> out
+    // ---- epilogue: O / l -> out (l = both halves' shares)
     if (nt > 0) {
       if (ok) ok = mbar_wait(bar(O_FULL_A + x), 0, abort_flag, a.status);
       ok = __all_sync(0xffffffffu, ok);
+      float* xb = xchg + (nt & 1) * 512;  // the parity iteration nt would use
+      xb[half * 128 + row] = l;
+      asm volatile("bar.sync %0, 64;\n" ::"r"(pair_bar) : "memory");
+      const float l_row = l + xb[(half ^ 1) * 128 + row];
       if (ok) {
         tc_fence_after();
-        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-        float* orow = a.out + ((size_t)q_idx * H + h) * HD;
+        const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
+        float* orow = a.out + ((size_t)q_idx * H + h) * HD + half * 64;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tmem_ld32(lane_base + o_col + c * 32, r);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tmem_ld32(lane_base + o_col + c * 32, o);
           tmem_wait_ld();
           if (q_idx < a.seq_len) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4) {
-              float4 o = make_float4(__uint_as_float(r[i]) * inv, __uint_as_float(r[i + 1]) * inv,
-                                     __uint_as_float(r[i + 2]) * inv, __uint_as_float(r[i + 3]) * inv);
-              *reinterpret_cast<float4*>(orow + c * 32 + i) = o;
+              float4 v = make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                     __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+              *reinterpret_cast<float4*>(orow + c * 32 + i) = v;
             }
           }
         }
@@ -489,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == 16) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }
