@@ -12,11 +12,14 @@
 // One CTA owns two 128-row query tiles (A = 2m, B = 2m+1) of one head and
 // walks the 128-key tiles up to B's diagonal (heaviest pairs launch first).
 // The two tiles share every K/V tile:
-//   warp 17    TMA producer: Q_A, Q_B once, K/V tiles into a 2-stage ring; it
-//              also TMA-stores the diagonal K/V tiles into the paged cache
-//   warp 16    TMEM owner + MMA issuer (one thread): S_A = Q_A K^T, S_B =
-//              Q_B K^T, then O_A += P_A V and O_B += P_B V, ping-ponging so the
-//              tensor core works on one tile while the other tile's softmax runs
+//   warp 17    TMA producer: Q_A, Q_B once, K and V tiles into two 2-slot
+//              rings (K runs a tile ahead of V: each slot is refilled as soon
+//              as its own tile is released); it also TMA-stores the diagonal
+//              K/V tiles into the paged cache
+//   warp 16    TMEM owner + MMA issuer (whole warp, one elected lane issues):
+//              S_A = Q_A K^T, S_B = Q_B K^T, then O_A += P_A V and O_B += P_B V,
+//              ping-ponging so the tensor core works on one tile while the
+//              other tile's softmax runs
 //   warps 0-7  softmax of tile A, warps 8-15 softmax of tile B: row r (TMEM
 //              lane r) is shared by two threads, one per half of the 128 keys
 //              (warps w and w + 4 of a tile); each reads its 64 scores from TMEM
@@ -52,6 +55,7 @@ constexpr uint32_t OFF_XCHG = OFF_BAR + 256;         // row max / sum exchange: 
 constexpr uint32_t kSmemBytes = OFF_XCHG + 2 * 2 * 2 * 128 * 4 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 4000000000LL;      // ~2 s at 1.9 GHz
+constexpr uint32_t kSuspendNs = 20000;                // try_wait sleep hint (the 2 s bound is checked between)
 
 enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, K_EMPTY0, K_EMPTY1, V_EMPTY0, V_EMPTY1,
            S_FULL_A, S_FULL_B, P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, MMA_DONE, NUM_BARS };
@@ -90,13 +94,27 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps in hardware until it completes (or kSuspendNs pass) instead of
+// re-polling; polling warps take shared-memory bandwidth from the SS MMAs.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.b32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: false (and an error bit, and the CTA abort flag) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int32_t* status) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
+    if (mbar_try_sleep(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitCycles) {
       *abort_flag = 1;
@@ -148,27 +166,31 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool b_mn_major) {
          ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 }
 
-__device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
-                                     uint32_t accumulate) {
+// Elected-lane forms: called by a whole converged warp; elect.sync picks the
+// one lane that issues, so the operands can stay warp-uniform.
+__device__ __forceinline__ void umma_elect(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                           uint32_t accumulate) {
   asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "{\n.reg .pred e, p;\nelect.sync _|e, 0xffffffff;\nsetp.ne.b32 p, %4, 0;\n"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
       "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // D[tmem] (+)= A[tmem] * B[smem]: A (M x 16, f16 pairs packed per 32-bit
 // column, row m in lane m) read from tensor memory.
-__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                        uint32_t accumulate) {
+__device__ __forceinline__ void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                              uint32_t accumulate) {
   asm volatile(
-      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "{\n.reg .pred e, p;\nelect.sync _|e, 0xffffffff;\nsetp.ne.b32 p, %4, 0;\n"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b), "r"(idesc), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
-               : "memory");
+__device__ __forceinline__ void commit_elect(uint32_t bar) {
+  asm volatile(
+      "{\n.reg .pred e;\nelect.sync _|e, 0xffffffff;\n"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n}\n" ::"r"(bar)
+      : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
@@ -340,67 +362,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 16) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const uint32_t idq = idesc_f16(false), idp = idesc_f16(true);
-      // S_x(j) = Q_x K_j^T into TMEM columns [128x, 128x + 128)
-      auto issue_s = [&](int x, int j) {
-        const uint32_t kb = sbase + OFF_K + (j & 1) * kTile;
-        const uint32_t qb = sbase + OFF_Q + x * kTile;
+    // The whole warp runs the (warp-uniform) control flow and one elected lane
+    // issues each tcgen05 instruction: the descriptors stay in uniform
+    // registers and each MMA costs an add and the issue itself.  This warp
+    // shares its scheduler with four softmax warps, so every instruction it
+    // saves is issue bandwidth the tensor pipe would otherwise wait for.
+    const uint32_t idq = idesc_f16(false), idp = idesc_f16(true);
+    const uint64_t dq = sdesc(sbase + OFF_Q, 16, 1024);      // Q_A; Q_B is kTile further
+    const uint64_t dk = sdesc(sbase + OFF_K, 16, 1024);      // K ring slot 0
+    const uint64_t dv = sdesc(sbase + OFF_V, kSub, 1024);    // V ring slot 0
+    // S_x(j) = Q_x K_j^T into TMEM columns [128x, 128x + 128)
+    auto issue_s = [&](int x, int j) {
+      const uint64_t q = dq + ((x * kTile) >> 4), k = dk + (((j & 1) * kTile) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kSub + (kk & 3) * 32;
-          umma(tmem + x * 128, sdesc(qb + off, 16, 1024), sdesc(kb + off, 16, 1024), idq, kk > 0);
-        }
-        umma_commit(bar(S_FULL_A + x));
-      };
-      // O_x += P_x V_j with P_x (f16) in TMEM columns [128x, 128x + 64)
-      auto issue_pv = [&](int x, int j) {
-        const uint32_t vb = sbase + OFF_V + (j & 1) * kTile;
+      for (int kk = 0; kk < HD / 16; ++kk) {
+        const uint32_t off = ((kk >> 2) * kSub + (kk & 3) * 32) >> 4;  // start-address field units
+        umma_elect(tmem + x * 128, q + off, k + off, idq, kk > 0);
+      }
+      commit_elect(bar(S_FULL_A + x));
+    };
+    // O_x += P_x V_j with P_x (f16) in TMEM columns [128x, 128x + 64)
+    auto issue_pv = [&](int x, int j) {
+      const uint64_t v = dv + (((j & 1) * kTile) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)
-          umma_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, sdesc(vb + kk * 16 * 128, kSub, 1024),
-                  idp, (j > 0 || kk > 0) ? 1u : 0u);
-      };
-      const int nx[2] = {nA, nB};
-      bool ok = mbar_wait(bar(Q_FULL), 0, abort_flag, a.status) &&
-                mbar_wait(bar(K_FULL0), 0, abort_flag, a.status);
-      if (ok) {
-        tc_fence_after();
-        for (int x = 0; x < 2; ++x)
-          if (nx[x] > 0) issue_s(x, 0);
-        umma_commit(bar(K_EMPTY0));  // K(0) released once S_x(0) are done
-      }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        ok = mbar_wait(bar(V_FULL0 + (j & 1)), (j >> 1) & 1, abort_flag, a.status);
-        bool k_ready = false;  // K(j+1) seen complete
-        for (int x = 0; x < 2 && ok; ++x) {
-          if (j >= nx[x]) continue;
-          // every mbarrier wait here stalls the issue stream (~100 cycles even
-          // when the phase is complete), so each is taken only once per step
-          ok = mbar_wait(bar(P_FULL_A + x), j & 1, abort_flag, a.status);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(x, j);
-          if (j == nx[x] - 1) umma_commit(bar(O_FULL_A + x));
-          if (j + 1 < nx[x]) {
-            if (!k_ready) {
-              ok = mbar_wait(bar(K_FULL0 + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag, a.status);
-              if (!ok) break;
-              k_ready = true;
-            }
-            tc_fence_after();
-            issue_s(x, j + 1);
-          }
-        }
-        if (!ok) break;
-        if (j + 1 < n_kv) umma_commit(bar(K_EMPTY0 + ((j + 1) & 1)));  // K(j+1): S_x(j+1) issued
-        umma_commit(bar(V_EMPTY0 + (j & 1)));                          // V(j): PV_x(j) issued
-      }
-      // every MMA this thread issued has finished once MMA_DONE flips
-      umma_commit(bar(MMA_DONE));
-      mbar_wait(bar(MMA_DONE), 0, abort_flag, a.status);
+      for (int kk = 0; kk < BN / 16; ++kk)
+        umma_ts_elect(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, v + ((kk * 16 * 128) >> 4), idp,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+    };
+    // bounded wait by every lane, agreed across the warp so it stays converged
+    auto wait = [&](int b, uint32_t parity) {
+      return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, abort_flag, a.status));
+    };
+    bool ok = wait(Q_FULL, 0) && wait(K_FULL0, 0);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0, 0);
+      if (nB > 0) issue_s(1, 0);
+      commit_elect(bar(K_EMPTY0));  // K(0) released once S_x(0) are done
     }
-    __syncwarp();
+    for (int j = 0; j < n_kv && ok; ++j) {
+      ok = wait(V_FULL0 + (j & 1), (j >> 1) & 1);
+      bool k_ready = false;  // K(j+1) seen complete
+      for (int x = 0; x < 2 && ok; ++x) {
+        const int nt = x == 0 ? nA : nB;
+        if (j >= nt) continue;
+        // every mbarrier wait here costs the issue stream ~100 cycles even when
+        // the phase is complete, so each is taken only once per step
+        ok = wait(P_FULL_A + x, j & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(x, j);
+        if (j == nt - 1) commit_elect(bar(O_FULL_A + x));
+        if (j + 1 < nt) {
+          if (!k_ready) {
+            ok = wait(K_FULL0 + ((j + 1) & 1), ((j + 1) >> 1) & 1);
+            if (!ok) break;
+            k_ready = true;
+          }
+          tc_fence_after();
+          issue_s(x, j + 1);
+        }
+      }
+      if (!ok) break;
+      if (j + 1 < n_kv) commit_elect(bar(K_EMPTY0 + ((j + 1) & 1)));  // K(j+1): S_x(j+1) issued
+      commit_elect(bar(V_EMPTY0 + (j & 1)));                          // V(j): PV_x(j) issued
+    }
+    // every MMA this warp issued has finished once MMA_DONE flips
+    commit_elect(bar(MMA_DONE));
+    wait(MMA_DONE, 0);
   } else {
     // ------------------------------------------------------------ softmax
     const int x = warp >> 3;                 // tile A (x = 0) or B (x = 1)
@@ -474,8 +503,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float p0 = ex2(fmaf(__uint_as_float(r[c * 32 + 2 * e]), a.scale_log2, neg_m));
-          const float p1 = ex2(fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), a.scale_log2, neg_m));
+          const float x0 = fmaf(__uint_as_float(r[c * 32 + 2 * e]), a.scale_log2, neg_m);
+          const float x1 = fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), a.scale_log2, neg_m);
+          const float p0 = ex2(x0);
+          const float p1 = ex2(x1);
           sums[e & 7] += p0 + p1;
           w[e] = pack_half2(p0, p1);
         }
