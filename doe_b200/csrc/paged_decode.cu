@@ -9,16 +9,18 @@
 //
 // Design (B200): the work is HBM-bound (2 flop/byte), so the kernel is built
 // around the loads.  One warp consumes one 16-token tile (a page, or a
-// 16-token slice of a larger page) per step with 128-bit loads taken straight
-// into mma.sync fragments -- no shared-memory staging, no barriers in the
-// loop.  A dimension permutation, applied identically to Q, makes every lane's
-// K/V bytes contiguous: each load instruction reads whole 32-byte sectors.
+// 16-token slice of a larger page) per step.  Each warp has its own ring of
+// tiles filled by TMA (one elected lane issues the boxes, an mbarrier per
+// slot): the copies bypass the load/store pipe, which is left to the
+// fragment reads.  Boxes land with the 128-byte swizzle, so the 16-byte
+// fragment reads of a warp are conflict-free.  A dimension permutation,
+// applied identically to Q, makes each lane's fragment bytes contiguous.
 //   S  = Q K^T   : m16n8k16, rows = the GROUP query heads of one kv head
 //   O^T = V^T P^T: m16n8k16, rows = 16 head dims, cols = the GROUP heads
 // so P moves from the S accumulator into the PV B operand without shuffles.
 // int8 tiles convert exactly to f16 in registers; the K scale multiplies S
 // and the V scale folds into P.  Scores run in the log2 domain (exp2f).
-#include "common.cuh"
+#include "tma.cuh"
 
 namespace doe {
 
@@ -114,31 +116,23 @@ __device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
   }
 }
 
-// Per-warp shared-memory ring.  Lane l copies exactly the 16-byte pieces it
-// will later feed to its own mma fragments into slot [piece][l]: the copy and
-// the read-back are private to the lane (no barrier, no bank conflicts), and
-// cp.async keeps several tiles of HBM traffic in flight per warp.
+// Per-warp ring of TMA-filled tiles.  A slot holds one 16-token tile, each
+// 16-row x 128-byte box on a 1024-byte boundary (chunk x of row R at x ^ R%8):
+//   f16:  K dims 0-63 | K dims 64-127 | V dims 0-63 | V dims 64-127   (8 KB)
+//   int8: K (128 dims) | V (128 dims)                                  (4 KB)
+// int8 slots also take the tile's 16 K scales and 16 V scales (64 B, kept
+// after the tiles).  Slot reuse is ordered by the warp itself: it issues the
+// refill of a slot only after it has read the slot's previous tile.
 template <bool INT8>
-struct StageLayout {
-  static constexpr int kK = INT8 ? 4 : 8;     // K pieces (16 B) per lane per tile
-  static constexpr int kV = INT8 ? 4 : 8;     // V pieces
-  static constexpr int kPieces = kK + kV;
-  static constexpr int kScaleOff = kPieces * 512;           // int8: 4 x u32 scales per lane
-  static constexpr int kBytes = kPieces * 512 + (INT8 ? 4 * 128 : 0);
+struct Ring {
   static constexpr int kStages = INT8 ? 4 : 2;
+  static constexpr int kTile = INT8 ? 4096 : 8192;
+  static constexpr int kScale = INT8 ? 64 : 0;
+  static constexpr int kTx = kTile + kScale;                       // bytes per filled slot
+  static constexpr int kWarpBytes = (kStages * (kTile + kScale) + 1023) / 1024 * 1024;
+  static constexpr int kSmem = kWarps * kWarpBytes + 1024;         // + base alignment
 };
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"
@@ -154,10 +148,13 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
 
 template <bool INT8, int GROUP>
 __global__ void __launch_bounds__(kWarps * 32)
-    paged_decode_kernel(const PagedDecodeArgs a) {
-  using SL = StageLayout<INT8>;
-  constexpr int P = SL::kStages;
-  extern __shared__ __align__(128) uint8_t dsmem[];
+    paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                        const PagedDecodeArgs a) {
+  using R = Ring<INT8>;
+  constexpr int P = R::kStages;
+  extern __shared__ __align__(1024) uint8_t dsmem_raw[];
+  // the swizzled boxes need 1024-byte alignment
+  uint8_t* dsmem = dsmem_raw + ((1024 - (smem_addr(dsmem_raw) & 1023)) & 1023);
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
@@ -178,10 +175,22 @@ __global__ void __launch_bounds__(kWarps * 32)
   __shared__ float sm_m[kWarps][8];
   __shared__ float sm_l[kWarps][8];
   __shared__ int sm_last;
+  __shared__ __align__(8) uint64_t ring_bar[kWarps][P];
+
+  if (lane == 0) {
+#pragma unroll
+    for (int st = 0; st < P; ++st) mbar_init(smem_addr(&ring_bar[warp][st]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncwarp();
 
   if (a.new_k != nullptr && split == nsplits - 1 && seq_len > 0) {
-    if (warp == 0) append_row<INT8>(a, b, g, seq_len - 1, table, lane);
-    __syncthreads();  // the appended row is read back below (through L2)
+    if (warp == 0) {
+      append_row<INT8>(a, b, g, seq_len - 1, table, lane);
+      // the row is read back below by TMA (the async proxy)
+      asm volatile("fence.proxy.async.global;\n" ::: "memory");
+    }
+    __syncthreads();
   }
 
   // ---- this warp's tiles: tile_begin + warp + 4k, k < nt; page ids up front
@@ -222,38 +231,40 @@ __global__ void __launch_bounds__(kWarps * 32)
   constexpr int ROWB = INT8 ? kD : 2 * kD;  // bytes per (token, kv head) row
   const size_t head_stride = (size_t)Hkv * ROWB;
   const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-  const uint32_t wbase = static_cast<uint32_t>(__cvta_generic_to_shared(dsmem)) + warp * P * SL::kBytes;
+  const uint32_t wbase = smem_addr(dsmem) + warp * R::kWarpBytes;
+  auto slot = [&](int k) { return wbase + (k % P) * R::kTile; };
+  auto scales = [&](int k) { return wbase + P * R::kTile + (k % P) * R::kScale; };
 
-  // Copies tile k's pieces for this lane into stage k % P.
+  // Fills slot k % P with tile k (whole warp calls, one lane issues).  A tile
+  // whose page id is out of range gets a plain arrival instead, so the slot's
+  // barrier phase still advances; the consumer reports the bad page.
   auto issue = [&](int k) {
     const int page = __shfl_sync(0xffffffffu, pg, k & 31);
-    if ((unsigned)page >= (unsigned)a.num_pages) return;
+    if (lane != 0) return;
+    const uint32_t bar = smem_addr(&ring_bar[warp][k % P]);
+    if ((unsigned)page >= (unsigned)a.num_pages) {
+      mbar_arrive(bar);
+      return;
+    }
     const int pos0 = (tile_begin + warp + kWarps * k) << 4;
     const int pidx = pos0 / a.page_size;
     const int in0 = pos0 - pidx * a.page_size;
-    const size_t row0 = (size_t)page * a.page_size + in0;
-    const uint8_t* kbase = a.k_pool + row0 * head_stride + (size_t)g * ROWB;
-    const uint8_t* vbase = a.v_pool + row0 * head_stride + (size_t)g * ROWB;
-    const uint32_t sb = wbase + (k % P) * SL::kBytes + lane * 16;
-#pragma unroll
-    for (int nb = 0; nb < 2; ++nb)
-#pragma unroll
-      for (int i = 0; i < (INT8 ? 2 : 4); ++i)
-        cp_async16(sb + (nb * (INT8 ? 2 : 4) + i) * 512,
-                   kbase + (size_t)(nb * 8 + r) * head_stride + 64 * i + 16 * c);
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-#pragma unroll
-      for (int h = 0; h < (INT8 ? 1 : 2); ++h)
-        cp_async16(sb + (SL::kK + j * (INT8 ? 1 : 2) + h) * 512,
-                   vbase + (size_t)vt[j] * head_stride + (INT8 ? 16 * r : 128 * h + 16 * r));
-    if (INT8) {
+    const int row0 = page * a.page_size + in0;
+    const uint32_t dst = slot(k);
+    // this warp read the slot's previous tile through the generic proxy
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    mbar_expect_tx(bar, R::kTx);
+    if (!INT8) {
+      tma_load_3d(dst, &tm_k, bar, 0, g, row0);
+      tma_load_3d(dst + 2048, &tm_k, bar, 64, g, row0);
+      tma_load_3d(dst + 4096, &tm_v, bar, 0, g, row0);
+      tma_load_3d(dst + 6144, &tm_v, bar, 64, g, row0);
+    } else {
+      tma_load_3d(dst, &tm_k, bar, 0, g, row0);
+      tma_load_3d(dst + 2048, &tm_v, bar, 0, g, row0);
       const size_t sidx = ((size_t)page * Hkv + g) * a.page_size + in0;
-      const uint32_t ss = wbase + (k % P) * SL::kBytes + SL::kScaleOff + lane * 4;
-      cp_async4(ss + 0 * 128, a.k_scale + sidx + 2 * c);
-      cp_async4(ss + 1 * 128, a.k_scale + sidx + 8 + 2 * c);
-      cp_async4(ss + 2 * 128, a.v_scale + sidx + 2 * c);
-      cp_async4(ss + 3 * 128, a.v_scale + sidx + 8 + 2 * c);
+      bulk_load(scales(k), a.k_scale + sidx, 32, bar);
+      bulk_load(scales(k) + 32, a.v_scale + sidx, 32, bar);
     }
   };
 
@@ -263,39 +274,49 @@ __global__ void __launch_bounds__(kWarps * 32)
   for (int mb = 0; mb < 8; ++mb) acc[mb][0] = acc[mb][1] = acc[mb][2] = acc[mb][3] = 0.0f;
 
 #pragma unroll
-  for (int s0 = 0; s0 < P - 1; ++s0) {
+  for (int s0 = 0; s0 < P - 1; ++s0)
     if (s0 < nt) issue(s0);
-    cp_async_commit();
-  }
+  bool ring_ok = true;
   for (int k = 0; k < nt; ++k) {
     if (k + P - 1 < nt) issue(k + P - 1);
-    cp_async_commit();
-    cp_async_wait<P - 1>();  // tile k's pieces have landed
+    // tile k has landed (bounded: a timeout ends this warp's walk)
+    ring_ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_addr(&ring_bar[warp][k % P]), (k / P) & 1));
+    if (!ring_ok) {
+      if (lane == 0) report(a.status, DOE_DEVICE_ERR_TIMEOUT);
+      break;
+    }
     const int page = __shfl_sync(0xffffffffu, pg, k & 31);
     if ((unsigned)page >= (unsigned)a.num_pages) {
       if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
       continue;
     }
     const int pos0 = (tile_begin + warp + kWarps * k) << 4;
-    const uint32_t sb = wbase + (k % P) * SL::kBytes + lane * 16;
+    const uint32_t sb = slot(k);
 
+    // Fragment reads (swizzled chunk positions; see Ring).  K: lane (r, c)
+    // takes row nb*8 + r, 16-byte chunk 4*(i&1) + c of box i>>1 (f16) or
+    // chunk 4i + c (int8).  V: row vt[j], chunk r of box h.
     uint4 kraw[2][INT8 ? 2 : 4];
     uint4 vraw[4][INT8 ? 1 : 2];
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
-      for (int i = 0; i < (INT8 ? 2 : 4); ++i) kraw[nb][i] = lds128(sb + (nb * (INT8 ? 2 : 4) + i) * 512);
+      for (int i = 0; i < (INT8 ? 2 : 4); ++i) {
+        const int box = INT8 ? 0 : (i >> 1), chunk = INT8 ? (4 * i + c) : (4 * (i & 1) + c);
+        kraw[nb][i] = lds128(sb + box * 2048 + (nb * 8 + r) * 128 + ((chunk ^ r) << 4));
+      }
 #pragma unroll
     for (int j = 0; j < 4; ++j)
 #pragma unroll
-      for (int h = 0; h < (INT8 ? 1 : 2); ++h) vraw[j][h] = lds128(sb + (SL::kK + j * (INT8 ? 1 : 2) + h) * 512);
+      for (int h = 0; h < (INT8 ? 1 : 2); ++h)
+        vraw[j][h] = lds128(sb + (INT8 ? 2048 : 4096 + h * 2048) + vt[j] * 128 + ((r ^ (vt[j] & 7)) << 4));
     uint32_t ksc[2] = {0, 0}, vsc[2] = {0, 0};
     if (INT8) {
-      const uint32_t ss = wbase + (k % P) * SL::kBytes + SL::kScaleOff + lane * 4;
-      ksc[0] = lds32(ss);
-      ksc[1] = lds32(ss + 128);
-      vsc[0] = lds32(ss + 256);
-      vsc[1] = lds32(ss + 384);
+      const uint32_t ss = scales(k);
+      ksc[0] = lds32(ss + 4 * c);        // tokens 2c, 2c+1
+      ksc[1] = lds32(ss + 16 + 4 * c);   // tokens 8+2c, 9+2c
+      vsc[0] = lds32(ss + 32 + 4 * c);
+      vsc[1] = lds32(ss + 48 + 4 * c);
     }
 
     // ---- S = Q K^T ----------------------------------------------------------
@@ -401,7 +422,6 @@ __global__ void __launch_bounds__(kWarps * 32)
       mma_16816(acc[mb], a0, a1, a2, a3, pb0, pb1);
     }
   }
-  cp_async_wait<0>();
 
   // ---- merge the warps of this split (O staged in this warp's own ring) ----
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
@@ -410,7 +430,7 @@ __global__ void __launch_bounds__(kWarps * 32)
     sm_m[warp][r] = m_run;
     sm_l[warp][r] = l_run;
   }
-  float* my_o = reinterpret_cast<float*>(dsmem + warp * P * SL::kBytes);  // [GROUP][kD]
+  float* my_o = reinterpret_cast<float*>(dsmem + warp * R::kWarpBytes);  // [GROUP][kD]
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) {
     const int d0 = INT8 ? (16 * r + 4 * (mb >> 1) + 2 * (mb & 1))
@@ -439,7 +459,7 @@ __global__ void __launch_bounds__(kWarps * 32)
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
         const float f = exp2f(sm_m[w][hh] - M[hh]);  // -inf -> 0
-        O[hh] += f * reinterpret_cast<const float*>(dsmem + w * P * SL::kBytes)[hh * kD + dim];
+        O[hh] += f * reinterpret_cast<const float*>(dsmem + w * R::kWarpBytes)[hh * kD + dim];
         L[hh] += f * sm_l[w][hh];
       }
     }
@@ -553,9 +573,9 @@ template __global__ void combine_splits_kernel<false>(const CombineArgs);
 
 // ---------------------------------------------------------------------------
 template <bool INT8, int GROUP>
-static int launch_one(const PagedDecodeArgs& a, dim3 grid, cudaStream_t st) {
-  using SL = StageLayout<INT8>;
-  constexpr int smem = kWarps * SL::kStages * SL::kBytes;
+static int launch_one(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const PagedDecodeArgs& a, dim3 grid,
+                      cudaStream_t st) {
+  constexpr int smem = Ring<INT8>::kSmem;
   static bool attr = false;  // per instantiation
   if (!attr) {
     int rc = cuda_status(cudaFuncSetAttribute(paged_decode_kernel<INT8, GROUP>,
@@ -564,7 +584,7 @@ static int launch_one(const PagedDecodeArgs& a, dim3 grid, cudaStream_t st) {
     if (rc != DOE_OK) return rc;
     attr = true;
   }
-  paged_decode_kernel<INT8, GROUP><<<grid, kWarps * 32, smem, st>>>(a);
+  paged_decode_kernel<INT8, GROUP><<<grid, kWarps * 32, smem, st>>>(tm_k, tm_v, a);
   return cuda_status(cudaGetLastError(), "paged_decode_kernel");
 }
 
@@ -633,11 +653,27 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   if (rc != DOE_OK) return rc;
   dim3 grid(max_splits, Hkv, num_seqs);
   const bool int8 = kv->kv_dtype == DOE_KV_INT8;
+  // K/V pools as {128 elements, Hkv, rows} tensor maps; one box = 16 rows of
+  // one kv head: 64 f16 (two boxes per row) or 128 int8.
+  for (const void* p : {(const void*)kv->k_pool, (const void*)kv->v_pool, (const void*)kv->k_scale,
+                        (const void*)kv->v_scale})
+    if (reinterpret_cast<uintptr_t>(p) % 16 != 0) {
+      set_op_error("doe_paged_decode: pools and scales must be 16-byte aligned");
+      return DOE_INVALID_ARGUMENT;
+    }
+  const uint64_t pool_rows = (uint64_t)kv->num_pages * kv->page_size;
+  CUtensorMap mk, mv;
+  const CUtensorMapDataType dt = int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint32_t eb = int8 ? 1 : 2, box_inner = int8 ? 128 : 64;
+  rc = encode_rows_map(&mk, kv->k_pool, dt, eb, kD, Hkv, pool_rows, box_inner, 16, "doe_paged_decode");
+  if (rc == DOE_OK)
+    rc = encode_rows_map(&mv, kv->v_pool, dt, eb, kD, Hkv, pool_rows, box_inner, 16, "doe_paged_decode");
+  if (rc != DOE_OK) return rc;
   switch (group) {
-    case 1: return int8 ? launch_one<true, 1>(a, grid, st) : launch_one<false, 1>(a, grid, st);
-    case 2: return int8 ? launch_one<true, 2>(a, grid, st) : launch_one<false, 2>(a, grid, st);
-    case 4: return int8 ? launch_one<true, 4>(a, grid, st) : launch_one<false, 4>(a, grid, st);
-    case 8: return int8 ? launch_one<true, 8>(a, grid, st) : launch_one<false, 8>(a, grid, st);
+    case 1: return int8 ? launch_one<true, 1>(mk, mv, a, grid, st) : launch_one<false, 1>(mk, mv, a, grid, st);
+    case 2: return int8 ? launch_one<true, 2>(mk, mv, a, grid, st) : launch_one<false, 2>(mk, mv, a, grid, st);
+    case 4: return int8 ? launch_one<true, 4>(mk, mv, a, grid, st) : launch_one<false, 4>(mk, mv, a, grid, st);
+    case 8: return int8 ? launch_one<true, 8>(mk, mv, a, grid, st) : launch_one<false, 8>(mk, mv, a, grid, st);
     default:
       set_op_error("doe_paged_decode: heads per kv head must be 1, 2, 4 or 8 (got %u)", group);
       return DOE_UNSUPPORTED;

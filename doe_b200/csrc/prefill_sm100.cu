@@ -38,7 +38,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
-#include "common.cuh"
+#include "tma.cuh"
 
 namespace doe {
 namespace pf {
@@ -577,37 +577,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---- host -----------------------------------------------------------------
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-
-int get_encoder() {
-  if (g_encode) return DOE_OK;
-  void* fn = nullptr;
-  cudaDriverEntryPointQueryResult q;
-  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
-    cudaGetLastError();
-    set_op_error("prefill: cuTensorMapEncodeTiled is not available from the driver");
-    return DOE_CUDA_ERROR;
-  }
-  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-  return DOE_OK;
-}
-
 // [rows, heads, 128] f16 viewed as a 3-D tensor {128, heads, rows}; boxes of
 // 64 x 1 x box_rows elements with the 128-byte swizzle.
 int make_map(CUtensorMap* m, const void* base, uint64_t rows, uint64_t heads, uint32_t box_rows) {
-  const cuuint64_t dims[3] = {128, heads, rows};
-  const cuuint64_t strides[2] = {128 * 2, heads * 128 * 2};
-  const cuuint32_t box[3] = {64, 1, box_rows};
-  const cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
-                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) {
-    set_op_error("prefill: cuTensorMapEncodeTiled failed (%d)", (int)r);
-    return DOE_CUDA_ERROR;
-  }
-  return DOE_OK;
+  return encode_rows_map(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, 128, heads, rows, 64, box_rows,
+                         "prefill");
 }
 
 }  // namespace
@@ -616,8 +590,7 @@ int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, 
                        uint32_t num_heads, uint32_t num_kv_heads, float scale, uint32_t causal,
                        const doe_paged_kv* cache, uint32_t cache_seq, uint32_t cache_start,
                        const doe_launch* launch) {
-  int rc = get_encoder();
-  if (rc != DOE_OK) return rc;
+  int rc = DOE_OK;
   for (const void* p : {q, k, v, (const void*)out})
     if (reinterpret_cast<uintptr_t>(p) % 16 != 0) {
       set_op_error("prefill: q, k, v and out must be 16-byte aligned");
