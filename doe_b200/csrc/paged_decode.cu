@@ -125,7 +125,7 @@ __device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
 // refill of a slot only after it has read the slot's previous tile.
 template <bool INT8>
 struct Ring {
-  static constexpr int kStages = INT8 ? 4 : 2;
+  static constexpr int kStages = 2;
   static constexpr int kTile = INT8 ? 4096 : 8192;
   static constexpr int kScale = INT8 ? 64 : 0;
   static constexpr int kTx = kTile + kScale;                       // bytes per filled slot
