@@ -167,6 +167,9 @@ def time_steps(step, steps: int, warmup: int, world: int):
     stream = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     per = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    # keep the GPU busy (~1 ms per 10 steps) while the host enqueues the timed
+    # steps, so host launch gaps never enter the device-timed region
+    torch.cuda._sleep(2_000_000 * max(1, (steps + 9) // 10))
     ev0.record(stream)
     for a, b in per:
         a.record(stream)

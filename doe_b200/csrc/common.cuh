@@ -53,6 +53,27 @@ __device__ __forceinline__ uint32_t prmt(uint32_t x, uint32_t y, uint32_t sel) {
   return __byte_perm(x, y, sel);
 }
 
+// int8 KV quantisation of one element: clamp(rint(x / s), -127, 127) for an
+// f16 value x and the row's f16 scale s = f16(absmax / 127) > 0, equal to the
+// CPU definition's rint of the f32 IEEE quotient.  The quotient is formed from
+// the correctly rounded reciprocal rs and one residual correction (Markstein's
+// method): y0 = x rs, y = y0 + (x - y0 s) rs, the residual exact in an FMA.
+// For f16 operands x / s is either exactly k + 1/2 or at least 2^-14 from
+// every half-integer (2x - (2k+1)s is a multiple of the finer of the two
+// operands' ulps), far beyond y's error; y lands on the same side of every
+// rounding boundary and is exactly k + 1/2 in the tie case, where rint takes
+// the even neighbour as the CPU does.
+__device__ __forceinline__ int quantize_s8(float x, float s, float rs) {
+  const float y0 = x * rs;
+  const float y = fmaf(fmaf(-y0, s, x), rs, y0);
+  const int q = __float2int_rn(y);
+  return q > 127 ? 127 : (q < -127 ? -127 : q);
+}
+// Low bytes of four ints (two's complement int8 values) packed into a word.
+__device__ __forceinline__ uint32_t pack_s8x4(int q0, int q1, int q2, int q3) {
+  return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

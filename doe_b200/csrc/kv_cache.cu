@@ -68,17 +68,13 @@ __global__ void __launch_bounds__(256) paged_append_kernel(const PagedAppendArgs
         amax = warp_max(amax);
         const __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
         const float sf = __half2float(sh);
+        const float rs = sf != 0.0f ? __frcp_rn(sf) : 0.0f;
         int8_t* dst = reinterpret_cast<int8_t*>(kv ? a.v_pool : a.k_pool) + (row * Hkv + h) * D +
                       (size_t)lane * EPL;
 #pragma unroll
         for (int i = 0; i < EPL; ++i) {
           const float xv = (i & 1) ? __high2float(x2[i / 2]) : __low2float(x2[i / 2]);
-          int qv = 0;
-          if (sf != 0.0f) {
-            qv = __float2int_rn(__fdiv_rn(xv, sf));
-            qv = qv > 127 ? 127 : (qv < -127 ? -127 : qv);
-          }
-          dst[i] = (int8_t)qv;
+          dst[i] = (int8_t)(sf != 0.0f ? quantize_s8(xv, sf, rs) : 0);
         }
         if (lane == 0) (kv ? a.v_scale : a.k_scale)[((size_t)page * Hkv + h) * a.page_size + in_page] = sh;
       }
@@ -131,30 +127,25 @@ __global__ void __launch_bounds__(128) paged_append_d128_kernel(const PagedAppen
       continue;
     }
     const __half2* hx = reinterpret_cast<const __half2*>(&x[i]);
-    float v[8];
-    float amax = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      v[2 * e] = __low2float(hx[e]);
-      v[2 * e + 1] = __high2float(hx[e]);
-      amax = fmaxf(amax, fmaxf(fabsf(v[2 * e]), fabsf(v[2 * e + 1])));
-    }
+    // |x| max in f16x2 (exact), then across the half-warp
+    __half2 m2 = __hmax2(__habs2(hx[0]), __habs2(hx[1]));
+    m2 = __hmax2(m2, __hmax2(__habs2(hx[2]), __habs2(hx[3])));
+    float amax = fmaxf(__low2float(m2), __high2float(m2));
     // both half-warps run this together (ROWS is even); offsets <= 8 stay in a half
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
     const float sf = __half2float(sh);
-    uint32_t lo = 0, hi = 0;
+    int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (sf != 0.0f) {
+      const float rs = __frcp_rn(sf);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      int qv = 0;
-      if (sf != 0.0f) {
-        qv = __float2int_rn(__fdiv_rn(v[e], sf));
-        qv = qv > 127 ? 127 : (qv < -127 ? -127 : qv);
+      for (int e = 0; e < 4; ++e) {
+        q[2 * e] = quantize_s8(__low2float(hx[e]), sf, rs);
+        q[2 * e + 1] = quantize_s8(__high2float(hx[e]), sf, rs);
       }
-      if (e < 4) lo |= (uint32_t)(qv & 0xff) << (8 * e);
-      else hi |= (uint32_t)(qv & 0xff) << (8 * (e - 4));
     }
+    const uint32_t lo = pack_s8x4(q[0], q[1], q[2], q[3]), hi = pack_s8x4(q[4], q[5], q[6], q[7]);
     *reinterpret_cast<uint2*>(pool + (row * HKV + h) * D + 8 * l16) = make_uint2(lo, hi);
     if (l16 == 0) (rr < HKV ? a.k_scale : a.v_scale)[((size_t)page * HKV + h) * a.page_size + in_page] = sh;
   }

@@ -96,16 +96,13 @@ __device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
       amax = warp_max(amax);
       __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
       float sf = __half2float(sh);
-      uint32_t packed = 0;
+      int qv[4] = {0, 0, 0, 0};
+      if (sf != 0.0f) {
+        const float rs = __frcp_rn(sf);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        int qv = 0;
-        if (sf != 0.0f) {
-          qv = __float2int_rn(__fdiv_rn(x[e], sf));
-          qv = qv > 127 ? 127 : (qv < -127 ? -127 : qv);
-        }
-        packed |= (uint32_t)(qv & 0xff) << (8 * e);
+        for (int e = 0; e < 4; ++e) qv[e] = quantize_s8(x[e], sf, rs);
       }
+      const uint32_t packed = pack_s8x4(qv[0], qv[1], qv[2], qv[3]);
       uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * kD + 4 * lane;
       *reinterpret_cast<uint32_t*>(dst) = packed;
       if (lane == 0) {
