@@ -113,6 +113,9 @@ SIGNATURES = {
     "doe_paged_decode_workspace_bytes": (_U64, [C.POINTER(PagedKV), _U32, _U32, _U32]),
     "doe_paged_decode": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _P, _F, _P, _U32, _LP]),
     "doe_paged_append": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _LP]),
+    "doe_paged_append_rope": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _P, _U32, _LP]),
+    "doe_paged_decode_rope": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _P, _F, _P, _U32, _P, _U32,
+                                   _LP]),
     "doe_paged_gather": (_I, [C.POINTER(PagedKV), _U32, _U32, _U32, _P, _P, _P, _P, _LP]),
     "doe_kv_write_dense": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _LP]),
     "doe_kv_read_dense": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _LP]),

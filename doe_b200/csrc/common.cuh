@@ -74,6 +74,50 @@ __device__ __forceinline__ uint32_t pack_s8x4(int q0, int q1, int q2, int q3) {
   return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
 }
 
+// RoPE on 2W f16 elements of a row (rope.wgsl:12-35): each pair (d, d + D/2)
+// becomes x0' = x0 cos - x1 sin, x1' = x0 sin + x1 cos in f32, every product
+// and sum rounded separately, and the results are rounded back to f16.
+// `mine` holds 2W consecutive dims, `partner` the dims D/2 away; `first` is
+// true when mine holds the first halves (x0).  c/sn: the pairs' table entries.
+template <int W>
+__device__ __forceinline__ void rope_rotate(const uint32_t* mine, const uint32_t* partner, bool first,
+                                            const float (&c)[2 * W], const float (&sn)[2 * W],
+                                            uint32_t* out) {
+#pragma unroll
+  for (int e = 0; e < W; ++e) {
+    const __half2 m2 = *reinterpret_cast<const __half2*>(&mine[e]);
+    const __half2 p2 = *reinterpret_cast<const __half2*>(&partner[e]);
+    float r[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const float xm = k ? __high2float(m2) : __low2float(m2);
+      const float xp = k ? __high2float(p2) : __low2float(p2);
+      const float x0 = first ? xm : xp, x1 = first ? xp : xm;
+      const int j = 2 * e + k;
+      r[k] = first ? __fsub_rn(__fmul_rn(x0, c[j]), __fmul_rn(x1, sn[j]))
+                   : __fadd_rn(__fmul_rn(x0, sn[j]), __fmul_rn(x1, c[j]));
+    }
+    out[e] = pack_half2(r[0], r[1]);
+  }
+}
+// Loads the RoPE table entries of 2W consecutive pairs starting at `pair` for
+// position `pos` (freq_cis [positions, half, {cos, sin}]); positions beyond
+// the table get the identity and report DOE_DEVICE_ERR_POSITION.
+template <int W>
+__device__ __forceinline__ void rope_table(const float* freq_cis, int positions, int half, long long pos,
+                                           int pair, int32_t* status, bool reporter, float (&c)[2 * W],
+                                           float (&sn)[2 * W]) {
+  const bool in_table = pos >= 0 && pos < positions;
+  if (!in_table && reporter) report(status, DOE_DEVICE_ERR_POSITION);
+  const float4* tab = reinterpret_cast<const float4*>(freq_cis + ((size_t)(in_table ? pos : 0) * half + pair) * 2);
+#pragma unroll
+  for (int q = 0; q < W; ++q) {
+    const float4 t4 = in_table ? tab[q] : make_float4(1.0f, 0.0f, 1.0f, 0.0f);
+    c[2 * q] = t4.x; sn[2 * q] = t4.y;
+    c[2 * q + 1] = t4.z; sn[2 * q + 1] = t4.w;
+  }
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

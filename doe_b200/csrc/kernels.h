@@ -40,10 +40,11 @@ int launch_combine_natural(const float* part_o, const float* part_ml, float* out
 int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
                         const void* q, const int32_t* seq_lens, const void* new_k,
                         const void* new_v, float scale, float* out, uint32_t split_pages,
+                        const float* freq_cis, uint32_t rope_positions,
                         const doe_launch* launch, uint64_t* ws_needed_out);
 int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
                         const void* new_k, const void* new_v, const int32_t* positions,
-                        const doe_launch* launch);
+                        const float* freq_cis, uint32_t rope_positions, const doe_launch* launch);
 int launch_paged_gather(const doe_paged_kv* kv, uint32_t seq, uint32_t start, uint32_t len,
                         void* k_out, void* v_out, void* ks_out, void* vs_out,
                         const doe_launch* launch);

@@ -26,7 +26,9 @@ struct PagedAppendArgs {
   const int32_t* block_table;
   const int32_t* positions;
   int32_t* status;
+  const float* freq_cis;  // RoPE table [rope_positions, D/2, {cos, sin}] or null
   int n_tokens, num_kv_heads, head_dim, page_size, num_pages, max_pages;
+  int rope_positions;
 };
 
 // One warp per (sequence, token, kv head); lane owns head_dim/32 elements
@@ -107,6 +109,13 @@ __global__ void __launch_bounds__(128) paged_append_d128_kernel(const PagedAppen
   const int in_page = (int)(pos - pidx * a.page_size);
   const size_t row = (size_t)page * a.page_size + in_page;
   const size_t src_tok = ((size_t)b * a.n_tokens + t) * HKV * D;
+  // RoPE (rope.wgsl:12-35): lane l16 holds dims [8 l16, 8 l16 + 8); dim d < 64
+  // pairs with d + 64, held by lane l16 ^ 8.  Both lanes of a pair need the
+  // table entries of pair index 8 (l16 & 7) + e at this token's position.
+  const bool rope = a.freq_cis != nullptr;
+  float rc[8], rsn[8];
+  if (rope)
+    rope_table<4>(a.freq_cis, a.rope_positions, D / 2, pos, 8 * (l16 & 7), a.status, lane == 0, rc, rsn);
   uint4 x[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
@@ -119,6 +128,17 @@ __global__ void __launch_bounds__(128) paged_append_d128_kernel(const PagedAppen
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int rr = 2 * i + hw;
+    if (rope) {
+      // every lane takes part in the exchange; only K rows are rotated
+      uint4 px;
+      px.x = __shfl_xor_sync(0xffffffffu, x[i].x, 8);
+      px.y = __shfl_xor_sync(0xffffffffu, x[i].y, 8);
+      px.z = __shfl_xor_sync(0xffffffffu, x[i].z, 8);
+      px.w = __shfl_xor_sync(0xffffffffu, x[i].w, 8);
+      if (rr < HKV) rope_rotate<4>(reinterpret_cast<const uint32_t*>(&x[i]),
+                                  reinterpret_cast<const uint32_t*>(&px), l16 < 8, rc, rsn,
+                                  reinterpret_cast<uint32_t*>(&x[i]));
+    }
     if (rr >= ROWS) continue;  // uniform per half-warp; shuffles below stay inside it
     const int h = rr % HKV;
     uint8_t* pool = rr < HKV ? a.k_pool : a.v_pool;
@@ -153,8 +173,15 @@ __global__ void __launch_bounds__(128) paged_append_d128_kernel(const PagedAppen
 
 int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
                         const void* new_k, const void* new_v, const int32_t* positions,
-                        const doe_launch* launch) {
+                        const float* freq_cis, uint32_t rope_positions, const doe_launch* launch) {
   if (num_seqs == 0 || n_tokens == 0) return DOE_OK;
+  const bool d128 = kv->head_dim == 128 && (kv->num_kv_heads == 8 || kv->num_kv_heads == 4 ||
+                                            kv->num_kv_heads == 2 || kv->num_kv_heads == 1);
+  if (freq_cis != nullptr && !d128) {
+    set_op_error("doe_paged_append_rope: built for head_dim 128 with 1, 2, 4 or 8 kv heads "
+                 "(got head_dim %u, %u kv heads)", kv->head_dim, kv->num_kv_heads);
+    return DOE_UNSUPPORTED;
+  }
   if (kv->head_dim % 64 != 0 || kv->head_dim > 512) {
     set_op_error("doe_paged_append: head_dim must be a multiple of 64 up to 512 (got %u)",
                  kv->head_dim);
@@ -176,10 +203,11 @@ int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_to
   a.page_size = (int)kv->page_size;
   a.num_pages = (int)kv->num_pages;
   a.max_pages = (int)kv->max_pages_per_seq;
+  a.freq_cis = freq_cis;
+  a.rope_positions = (int)rope_positions;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
   const bool int8 = kv->kv_dtype == DOE_KV_INT8;
-  if (kv->head_dim == 128 && (kv->num_kv_heads == 8 || kv->num_kv_heads == 4 ||
-                              kv->num_kv_heads == 2 || kv->num_kv_heads == 1)) {
+  if (d128) {
     dim3 g2((n_tokens + 3) / 4, num_seqs);
 #define DOE_PA2(H) \
   (int8 ? paged_append_d128_kernel<true, H><<<g2, 128, 0, st>>>(a) \

@@ -208,31 +208,57 @@ uint64_t doe_paged_decode_workspace_bytes(const doe_paged_kv* kv, uint32_t num_s
   if (num_heads % kv->num_kv_heads != 0) return 0;
   uint64_t ws = 0;
   launch_paged_decode(kv, num_seqs, num_heads, nullptr, nullptr, nullptr, nullptr, 0.0f, nullptr,
-                      split_pages, &kDefaultLaunch, &ws);
+                      split_pages, nullptr, 0, &kDefaultLaunch, &ws);
   return ws;
 }
+
+namespace {
+int paged_decode_common(const char* who, const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
+                        const void* q, const int32_t* seq_lens, const void* new_k, const void* new_v,
+                        float scale, float* out, uint32_t split_pages, const float* freq_cis,
+                        uint32_t rope_positions, const doe_launch* launch) {
+  int rc = check_paged_kv(kv, who);
+  if (rc != DOE_OK) return rc;
+  if (!q || !seq_lens || !out) return invalid("%s: q, seq_lens and out are required", who);
+  if ((new_k == nullptr) != (new_v == nullptr)) return invalid("%s: new_k and new_v go together", who);
+  if (num_heads == 0 || num_heads % kv->num_kv_heads != 0)
+    return invalid("%s: num_heads %u is not a multiple of num_kv_heads %u", who, num_heads,
+                   kv->num_kv_heads);
+  if (kv->head_dim != 128) {
+    set_op_error("%s: the tensor-core decode kernel is built for head_dim 128 (got %u)", who, kv->head_dim);
+    return DOE_UNSUPPORTED;
+  }
+  if (num_seqs == 0) return DOE_OK;
+  if (num_seqs > 65535) return invalid("%s: at most 65535 sequences per launch", who);
+  return launch_paged_decode(kv, num_seqs, num_heads, q, seq_lens, new_k, new_v, scale, out, split_pages,
+                             freq_cis, rope_positions, launch_or_default(launch), nullptr);
+}
+
+int check_rope_table(const char* who, const float* freq_cis, uint32_t rope_positions) {
+  if (!freq_cis || rope_positions == 0)
+    return invalid("%s: freq_cis and a positive rope_positions are required", who);
+  if (reinterpret_cast<uintptr_t>(freq_cis) % 16 != 0)
+    return invalid("%s: freq_cis must be 16-byte aligned", who);
+  return DOE_OK;
+}
+}  // namespace
 
 int doe_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
                      const void* q, const int32_t* seq_lens, const void* new_k,
                      const void* new_v, float scale, float* out, uint32_t split_pages,
                      const doe_launch* launch) {
-  int rc = check_paged_kv(kv, "doe_paged_decode");
+  return paged_decode_common("doe_paged_decode", kv, num_seqs, num_heads, q, seq_lens, new_k, new_v, scale,
+                             out, split_pages, nullptr, 0, launch);
+}
+
+int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
+                          const void* q, const int32_t* seq_lens, const void* new_k,
+                          const void* new_v, float scale, float* out, uint32_t split_pages,
+                          const float* freq_cis, uint32_t rope_positions, const doe_launch* launch) {
+  int rc = check_rope_table("doe_paged_decode_rope", freq_cis, rope_positions);
   if (rc != DOE_OK) return rc;
-  if (!q || !seq_lens || !out) return invalid("doe_paged_decode: q, seq_lens and out are required");
-  if ((new_k == nullptr) != (new_v == nullptr))
-    return invalid("doe_paged_decode: new_k and new_v go together");
-  if (num_heads == 0 || num_heads % kv->num_kv_heads != 0)
-    return invalid("doe_paged_decode: num_heads %u is not a multiple of num_kv_heads %u",
-                   num_heads, kv->num_kv_heads);
-  if (kv->head_dim != 128) {
-    set_op_error("doe_paged_decode: the tensor-core decode kernel is built for head_dim 128 (got %u)",
-                 kv->head_dim);
-    return DOE_UNSUPPORTED;
-  }
-  if (num_seqs == 0) return DOE_OK;
-  if (num_seqs > 65535) return invalid("doe_paged_decode: at most 65535 sequences per launch");
-  return launch_paged_decode(kv, num_seqs, num_heads, q, seq_lens, new_k, new_v, scale, out,
-                             split_pages, launch_or_default(launch), nullptr);
+  return paged_decode_common("doe_paged_decode_rope", kv, num_seqs, num_heads, q, seq_lens, new_k, new_v,
+                             scale, out, split_pages, freq_cis, rope_positions, launch);
 }
 
 int doe_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
@@ -243,7 +269,21 @@ int doe_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_token
   if (!new_k || !new_v || !positions)
     return invalid("doe_paged_append: new_k, new_v and positions are required");
   if (num_seqs > 65535) return invalid("doe_paged_append: at most 65535 sequences per launch");
-  return launch_paged_append(kv, num_seqs, n_tokens, new_k, new_v, positions,
+  return launch_paged_append(kv, num_seqs, n_tokens, new_k, new_v, positions, nullptr, 0,
+                             launch_or_default(launch));
+}
+
+int doe_paged_append_rope(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
+                          const void* new_k, const void* new_v, const int32_t* positions,
+                          const float* freq_cis, uint32_t rope_positions, const doe_launch* launch) {
+  int rc = check_paged_kv(kv, "doe_paged_append_rope");
+  if (rc != DOE_OK) return rc;
+  rc = check_rope_table("doe_paged_append_rope", freq_cis, rope_positions);
+  if (rc != DOE_OK) return rc;
+  if (!new_k || !new_v || !positions)
+    return invalid("doe_paged_append_rope: new_k, new_v and positions are required");
+  if (num_seqs > 65535) return invalid("doe_paged_append_rope: at most 65535 sequences per launch");
+  return launch_paged_append(kv, num_seqs, n_tokens, new_k, new_v, positions, freq_cis, rope_positions,
                              launch_or_default(launch));
 }
 

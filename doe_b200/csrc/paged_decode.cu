@@ -39,6 +39,8 @@ struct PagedDecodeArgs {
   float* part_ml;           // [B*Hkv*max_splits, GROUP, 2]
   unsigned* counters;       // [B*Hkv] arrivals per (b, g); zeroed before each launch
   int32_t* status;
+  const float* freq_cis;    // RoPE table [rope_positions, D/2, {cos, sin}] or null
+  int rope_positions;
   int num_heads, num_kv_heads, num_pages, page_size, max_pages;
   int split_tiles, max_splits;
   float scale_log2;
@@ -81,10 +83,20 @@ __device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
                            a.new_v + ((size_t)b * Hkv + g) * kD};
   const uint8_t* pools[2] = {a.k_pool, a.v_pool};
   const __half* scales[2] = {a.k_scale, a.v_scale};
+  // RoPE on the K row: dim d < 64 (lanes 0-15) pairs with d + 64 (lane ^ 16)
+  float rc[4], rsn[4];
+  if (a.freq_cis != nullptr)
+    rope_table<2>(a.freq_cis, a.rope_positions, kD / 2, pos, 4 * (lane & 15), a.status, lane == 0, rc, rsn);
 #pragma unroll
   for (int kv = 0; kv < 2; ++kv) {
     // lane owns elements [4*lane, 4*lane+4)
     uint2 raw = *reinterpret_cast<const uint2*>(srcs[kv] + 4 * lane);
+    if (kv == 0 && a.freq_cis != nullptr) {
+      const uint2 partner = make_uint2(__shfl_xor_sync(0xffffffffu, raw.x, 16),
+                                       __shfl_xor_sync(0xffffffffu, raw.y, 16));
+      rope_rotate<2>(reinterpret_cast<const uint32_t*>(&raw), reinterpret_cast<const uint32_t*>(&partner),
+                     lane < 16, rc, rsn, reinterpret_cast<uint32_t*>(&raw));
+    }
     if (!INT8) {
       uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * (kD * 2) + 8 * lane;
       *reinterpret_cast<uint2*>(dst) = raw;
@@ -206,12 +218,35 @@ __global__ void __launch_bounds__(kWarps * 32)
   {
     const __half* qrow = a.q + ((size_t)b * a.num_heads + (size_t)g * GROUP + r) * kD;
     const bool live = r < GROUP;
+    // the lane's four 8-dim runs: index 2i + part (int8) or i (f16); runs 0, 1
+    // lie in the first half of the head dims and runs 2, 3 hold their RoPE
+    // partners 64 dims on
+    uint4 qv[4];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int dim0 = INT8 ? (64 * (n >> 1) + 16 * c + 8 * (n & 1)) : (32 * n + 8 * c);
+      qv[n] = live ? *reinterpret_cast<const uint4*>(qrow + dim0) : make_uint4(0, 0, 0, 0);
+    }
+    if (a.freq_cis != nullptr && live && seq_len > 0) {
+      // the query sits at the new token's position, seq_len - 1
+#pragma unroll
+      for (int n = 0; n < 2; ++n) {
+        float rc[8], rsn[8];
+        const int pair0 = INT8 ? (16 * c + 8 * n) : (32 * n + 8 * c);
+        rope_table<4>(a.freq_cis, a.rope_positions, kD / 2, (long long)seq_len - 1, pair0, a.status,
+                      split == 0 && g == 0 && r == 0 && c == 0 && warp == 0, rc, rsn);
+        const uint4 lo = qv[n], hi = qv[n + 2];
+        rope_rotate<4>(reinterpret_cast<const uint32_t*>(&lo), reinterpret_cast<const uint32_t*>(&hi), true, rc,
+                       rsn, reinterpret_cast<uint32_t*>(&qv[n]));
+        rope_rotate<4>(reinterpret_cast<const uint32_t*>(&hi), reinterpret_cast<const uint32_t*>(&lo), false, rc,
+                       rsn, reinterpret_cast<uint32_t*>(&qv[n + 2]));
+      }
+    }
 #pragma unroll
     for (int i = 0; i < (INT8 ? 2 : 4); ++i) {
 #pragma unroll
       for (int part = 0; part < (INT8 ? 2 : 1); ++part) {
-        const int dim0 = INT8 ? (64 * i + 16 * c + 8 * part) : (32 * i + 8 * c);
-        uint4 v = live ? *reinterpret_cast<const uint4*>(qrow + dim0) : make_uint4(0, 0, 0, 0);
+        const uint4 v = qv[INT8 ? 2 * i + part : i];
         if (!INT8) {
           qa[2 * i][0] = v.x; qa[2 * i][1] = v.y;
           qa[2 * i + 1][0] = v.z; qa[2 * i + 1][1] = v.w;
@@ -225,8 +260,6 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
   }
 
-  constexpr int ROWB = INT8 ? kD : 2 * kD;  // bytes per (token, kv head) row
-  const size_t head_stride = (size_t)Hkv * ROWB;
   const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
   const uint32_t wbase = smem_addr(dsmem) + warp * R::kWarpBytes;
   auto slot = [&](int k) { return wbase + (k % P) * R::kTile; };
@@ -588,6 +621,7 @@ static int launch_one(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const Pa
 int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
                         const void* q, const int32_t* seq_lens, const void* new_k,
                         const void* new_v, float scale, float* out, uint32_t split_pages,
+                        const float* freq_cis, uint32_t rope_positions,
                         const doe_launch* launch, uint64_t* ws_needed_out) {
   const uint32_t Hkv = kv->num_kv_heads;
   const uint32_t group = num_heads / Hkv;
@@ -643,6 +677,8 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.split_tiles = (int)split_tiles;
   a.max_splits = (int)max_splits;
   a.scale_log2 = scale * kLog2e;
+  a.freq_cis = freq_cis;
+  a.rope_positions = (int)rope_positions;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
   // arrival counters of the split stitch start at zero on every launch
   int rc = cuda_status(cudaMemsetAsync(a.counters, 0, (size_t)num_seqs * Hkv * sizeof(unsigned), st),

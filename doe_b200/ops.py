@@ -100,11 +100,13 @@ def stitch(partials, out=None, stream=None):
 
 
 def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new_v=None, out=None,
-                 split_pages: int = 0, status=None, stream=None):
+                 split_pages: int = 0, status=None, stream=None, freq_cis=None):
     """Batched GQA decode: q [B,H,D] f16, seq_lens [B] int32 -> out [B,H,D] f32.
 
     With new_k/new_v ([B,Hkv,D] f16) the new token is first written at
-    position seq_lens[b] - 1 (quantised for int8 caches)."""
+    position seq_lens[b] - 1 (quantised for int8 caches).  With freq_cis
+    ([positions, D/2, 2] f32 RoPE table) the query and the new K row are
+    rotated at position seq_lens[b] - 1 first (doe_paged_decode_rope)."""
     _need(q, torch.float16, "q")
     _need(seq_lens, torch.int32, "seq_lens")
     B, H, D = q.shape
@@ -113,24 +115,39 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
     lib = abi.lib()
     ws = lib.doe_paged_decode_workspace_bytes(C.byref(kv), B, H, split_pages)
     l = _launch(ws, status, stream, q.device)
-    abi.check("doe_paged_decode", lib.doe_paged_decode(
-        C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(),
-        new_k.data_ptr() if new_k is not None else None,
-        new_v.data_ptr() if new_v is not None else None, float(scale), out.data_ptr(),
-        split_pages, C.byref(l)))
+    nk = new_k.data_ptr() if new_k is not None else None
+    nv = new_v.data_ptr() if new_v is not None else None
+    if freq_cis is None:
+        abi.check("doe_paged_decode", lib.doe_paged_decode(
+            C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(), nk, nv, float(scale), out.data_ptr(),
+            split_pages, C.byref(l)))
+    else:
+        _need(freq_cis, torch.float32, "freq_cis")
+        abi.check("doe_paged_decode_rope", lib.doe_paged_decode_rope(
+            C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(), nk, nv, float(scale), out.data_ptr(),
+            split_pages, freq_cis.data_ptr(), freq_cis.shape[0], C.byref(l)))
     return out
 
 
-def paged_append(cache: PagedKVCache, new_k, new_v, positions, status=None, stream=None):
-    """Write new_k/new_v [B,T,Hkv,D] f16 at positions[b] + t (quantising int8 caches)."""
+def paged_append(cache: PagedKVCache, new_k, new_v, positions, status=None, stream=None, freq_cis=None):
+    """Write new_k/new_v [B,T,Hkv,D] f16 at positions[b] + t (quantising int8 caches).
+
+    With freq_cis ([positions, D/2, 2] f32 RoPE table) each K row is first
+    rotated at its position (doe_paged_append_rope)."""
     _need(new_k, torch.float16, "new_k")
     _need(new_v, torch.float16, "new_v")
     _need(positions, torch.int32, "positions")
     B, T = new_k.shape[:2]
     kv = cache.struct()
     l = _launch(0, status, stream, new_k.device)
-    abi.check("doe_paged_append", abi.lib().doe_paged_append(
-        C.byref(kv), B, T, new_k.data_ptr(), new_v.data_ptr(), positions.data_ptr(), C.byref(l)))
+    if freq_cis is None:
+        abi.check("doe_paged_append", abi.lib().doe_paged_append(
+            C.byref(kv), B, T, new_k.data_ptr(), new_v.data_ptr(), positions.data_ptr(), C.byref(l)))
+    else:
+        _need(freq_cis, torch.float32, "freq_cis")
+        abi.check("doe_paged_append_rope", abi.lib().doe_paged_append_rope(
+            C.byref(kv), B, T, new_k.data_ptr(), new_v.data_ptr(), positions.data_ptr(), freq_cis.data_ptr(),
+            freq_cis.shape[0], C.byref(l)))
 
 
 def paged_gather(cache: PagedKVCache, seq: int, start: int, length: int, status=None, stream=None):

@@ -270,6 +270,28 @@ int doe_paged_append(const doe_paged_kv* kv, uint32_t num_seqs,
                      uint32_t n_tokens, const void* new_k, const void* new_v,
                      const int32_t* positions, const doe_launch* launch);
 
+/* RoPE fused into the paged append and the paged decode (rope.wgsl:12-35,
+ * bench/inference-pipeline/kernels/): before K rows are written -- and, in the
+ * decode, before the query is used -- each is rotated at its absolute
+ * position pos (positions[b] + t for the append, seq_lens[b] - 1 for the
+ * decode's new token and query): pairs (i, i + D/2) become
+ * x0' = x0 cos - x1 sin, x1' = x0 sin + x1 cos in f32 (each product and sum
+ * rounded), with cos, sin = freq_cis[(pos * D/2 + i) * 2 + {0, 1}] (device
+ * f32, rope_positions rows, 16-byte aligned), then rounded to f16 (and
+ * quantised for int8 pools).  V rows are written as given.  A position
+ * >= rope_positions sets DOE_DEVICE_ERR_POSITION and leaves that row
+ * unrotated.  head_dim 128 (append: 1, 2, 4 or 8 kv heads).  The decode's
+ * workspace is doe_paged_decode_workspace_bytes.                           */
+int doe_paged_append_rope(const doe_paged_kv* kv, uint32_t num_seqs,
+                          uint32_t n_tokens, const void* new_k, const void* new_v,
+                          const int32_t* positions, const float* freq_cis,
+                          uint32_t rope_positions, const doe_launch* launch);
+int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs,
+                          uint32_t num_heads, const void* q, const int32_t* seq_lens,
+                          const void* new_k, const void* new_v, float scale,
+                          float* out, uint32_t split_pages, const float* freq_cis,
+                          uint32_t rope_positions, const doe_launch* launch);
+
 /* kv_read over the paged cache (runtime/zig/src/tsir/emit_kernel_body.zig:692-760):
  * copies tokens [start, start+len) of sequence `seq` into k_out/v_out
  * [len, Hkv, D] (element type of the pool); int8 pools also copy scales into
