@@ -73,6 +73,13 @@ class PagedKV(C.Structure):
                 ("max_pages_per_seq", C.c_uint32), ("block_table", C.c_void_p)]
 
 
+class DecodeOptions(C.Structure):
+    """doe_decode_options: RoPE table, sliding window, softcap of the paged decode."""
+
+    _fields_ = [("freq_cis", C.c_void_p), ("rope_positions", C.c_uint32), ("sliding_window", C.c_uint32),
+                ("attn_softcap", C.c_float), ("reserved", C.c_uint32)]
+
+
 _P = C.c_void_p
 _U32 = C.c_uint32
 _U64 = C.c_uint64
@@ -116,6 +123,8 @@ SIGNATURES = {
     "doe_paged_append_rope": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _P, _U32, _LP]),
     "doe_paged_decode_rope": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _P, _F, _P, _U32, _P, _U32,
                                    _LP]),
+    "doe_paged_decode_ex": (_I, [C.POINTER(PagedKV), _U32, _U32, _P, _P, _P, _P, _F, _P, _U32,
+                                 C.POINTER(DecodeOptions), _LP]),
     "doe_paged_gather": (_I, [C.POINTER(PagedKV), _U32, _U32, _U32, _P, _P, _P, _P, _LP]),
     "doe_kv_write_dense": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _LP]),
     "doe_kv_read_dense": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _LP]),

@@ -40,8 +40,8 @@ int launch_combine_natural(const float* part_o, const float* part_ml, float* out
 int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
                         const void* q, const int32_t* seq_lens, const void* new_k,
                         const void* new_v, float scale, float* out, uint32_t split_pages,
-                        const float* freq_cis, uint32_t rope_positions,
-                        const doe_launch* launch, uint64_t* ws_needed_out);
+                        const doe_decode_options* opts, const doe_launch* launch,
+                        uint64_t* ws_needed_out);
 int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
                         const void* new_k, const void* new_v, const int32_t* positions,
                         const float* freq_cis, uint32_t rope_positions, const doe_launch* launch);

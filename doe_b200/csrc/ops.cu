@@ -208,15 +208,22 @@ uint64_t doe_paged_decode_workspace_bytes(const doe_paged_kv* kv, uint32_t num_s
   if (num_heads % kv->num_kv_heads != 0) return 0;
   uint64_t ws = 0;
   launch_paged_decode(kv, num_seqs, num_heads, nullptr, nullptr, nullptr, nullptr, 0.0f, nullptr,
-                      split_pages, nullptr, 0, &kDefaultLaunch, &ws);
+                      split_pages, nullptr, &kDefaultLaunch, &ws);
   return ws;
 }
 
 namespace {
+int check_rope_table(const char* who, const float* freq_cis, uint32_t rope_positions) {
+  if (!freq_cis || rope_positions == 0)
+    return invalid("%s: freq_cis and a positive rope_positions are required", who);
+  if (reinterpret_cast<uintptr_t>(freq_cis) % 16 != 0)
+    return invalid("%s: freq_cis must be 16-byte aligned", who);
+  return DOE_OK;
+}
 int paged_decode_common(const char* who, const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
                         const void* q, const int32_t* seq_lens, const void* new_k, const void* new_v,
-                        float scale, float* out, uint32_t split_pages, const float* freq_cis,
-                        uint32_t rope_positions, const doe_launch* launch) {
+                        float scale, float* out, uint32_t split_pages, const doe_decode_options* opts,
+                        const doe_launch* launch) {
   int rc = check_paged_kv(kv, who);
   if (rc != DOE_OK) return rc;
   if (!q || !seq_lens || !out) return invalid("%s: q, seq_lens and out are required", who);
@@ -230,17 +237,18 @@ int paged_decode_common(const char* who, const doe_paged_kv* kv, uint32_t num_se
   }
   if (num_seqs == 0) return DOE_OK;
   if (num_seqs > 65535) return invalid("%s: at most 65535 sequences per launch", who);
+  if (opts != nullptr) {
+    if (opts->reserved != 0) return invalid("%s: options.reserved must be 0", who);
+    if (opts->freq_cis != nullptr) {
+      int rr = check_rope_table(who, opts->freq_cis, opts->rope_positions);
+      if (rr != DOE_OK) return rr;
+    }
+    if (!(opts->attn_softcap >= 0.0f)) return invalid("%s: attn_softcap must be >= 0", who);
+  }
   return launch_paged_decode(kv, num_seqs, num_heads, q, seq_lens, new_k, new_v, scale, out, split_pages,
-                             freq_cis, rope_positions, launch_or_default(launch), nullptr);
+                             opts, launch_or_default(launch), nullptr);
 }
 
-int check_rope_table(const char* who, const float* freq_cis, uint32_t rope_positions) {
-  if (!freq_cis || rope_positions == 0)
-    return invalid("%s: freq_cis and a positive rope_positions are required", who);
-  if (reinterpret_cast<uintptr_t>(freq_cis) % 16 != 0)
-    return invalid("%s: freq_cis must be 16-byte aligned", who);
-  return DOE_OK;
-}
 }  // namespace
 
 int doe_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
@@ -248,7 +256,15 @@ int doe_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_hea
                      const void* new_v, float scale, float* out, uint32_t split_pages,
                      const doe_launch* launch) {
   return paged_decode_common("doe_paged_decode", kv, num_seqs, num_heads, q, seq_lens, new_k, new_v, scale,
-                             out, split_pages, nullptr, 0, launch);
+                             out, split_pages, nullptr, launch);
+}
+
+int doe_paged_decode_ex(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
+                        const void* q, const int32_t* seq_lens, const void* new_k,
+                        const void* new_v, float scale, float* out, uint32_t split_pages,
+                        const doe_decode_options* options, const doe_launch* launch) {
+  return paged_decode_common("doe_paged_decode_ex", kv, num_seqs, num_heads, q, seq_lens, new_k, new_v,
+                             scale, out, split_pages, options, launch);
 }
 
 int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
@@ -257,8 +273,9 @@ int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t nu
                           const float* freq_cis, uint32_t rope_positions, const doe_launch* launch) {
   int rc = check_rope_table("doe_paged_decode_rope", freq_cis, rope_positions);
   if (rc != DOE_OK) return rc;
+  doe_decode_options o = {freq_cis, rope_positions, 0, 0.0f, 0};
   return paged_decode_common("doe_paged_decode_rope", kv, num_seqs, num_heads, q, seq_lens, new_k, new_v,
-                             scale, out, split_pages, freq_cis, rope_positions, launch);
+                             scale, out, split_pages, &o, launch);
 }
 
 int doe_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,

@@ -41,6 +41,9 @@ struct PagedDecodeArgs {
   int32_t* status;
   const float* freq_cis;    // RoPE table [rope_positions, D/2, {cos, sin}] or null
   int rope_positions;
+  int window;               // > 0: only the last `window` keys attend
+  float softcap;            // > 0: s = softcap * tanh(s / softcap) on the scaled score
+  float scale;              // the natural-domain scale (softcap path)
   int num_heads, num_kv_heads, num_pages, page_size, max_pages;
   int split_tiles, max_splits;
   float scale_log2;
@@ -174,10 +177,14 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int seq_len = clamp_len(raw_len, cap);
   if (raw_len != seq_len && split == 0 && g == 0 && threadIdx.x == 0)
     report(a.status, DOE_DEVICE_ERR_LENGTH);
-  const int ntiles = (seq_len + 15) >> 4;
+  // sliding window (attention_head256_f16kv.wgsl:129-135 at abs_q = seq_len - 1):
+  // keys [min_key, seq_len); the tiles start at the one holding min_key
+  const int min_key = (a.window > 0 && seq_len > a.window) ? seq_len - a.window : 0;
+  const int tile_origin = min_key >> 4;
+  const int ntiles = ((seq_len + 15) >> 4) - tile_origin;
   const int nsplits = max(1, (ntiles + a.split_tiles - 1) / a.split_tiles);
   if (split >= nsplits) return;
-  const int tile_begin = split * a.split_tiles;
+  const int tile_begin = split * a.split_tiles;  // relative to tile_origin
   const int tile_end = min(ntiles, tile_begin + a.split_tiles);
   const int32_t* table = a.block_table + (size_t)b * a.max_pages;
 
@@ -207,7 +214,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int nt = span > 0 ? (span + kWarps - 1) / kWarps : 0;
   int pg = -1;
   if (lane < nt) {
-    const int pos = (tile_begin + warp + kWarps * lane) << 4;
+    const int pos = (tile_origin + tile_begin + warp + kWarps * lane) << 4;
     pg = table[pos / a.page_size];
   }
 
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(kWarps * 32)
       mbar_arrive(bar);
       return;
     }
-    const int pos0 = (tile_begin + warp + kWarps * k) << 4;
+    const int pos0 = (tile_origin + tile_begin + warp + kWarps * k) << 4;
     const int pidx = pos0 / a.page_size;
     const int in0 = pos0 - pidx * a.page_size;
     const int row0 = page * a.page_size + in0;
@@ -320,7 +327,7 @@ __global__ void __launch_bounds__(kWarps * 32)
       if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
       continue;
     }
-    const int pos0 = (tile_begin + warp + kWarps * k) << 4;
+    const int pos0 = (tile_origin + tile_begin + warp + kWarps * k) << 4;
     const uint32_t sb = slot(k);
 
     // Fragment reads (swizzled chunk positions; see Ring).  K: lane (r, c)
@@ -377,13 +384,17 @@ __global__ void __launch_bounds__(kWarps * 32)
     for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        valid[nb][e] = pos0 + nb * 8 + 2 * c + e < seq_len;
+        const int key = pos0 + nb * 8 + 2 * c + e;
+        valid[nb][e] = key < seq_len && key >= min_key;
         float sv = s[nb][e];
         if (INT8) {
           __half2 k2 = *reinterpret_cast<__half2*>(&ksc[nb]);
           sv *= e ? __high2float(k2) : __low2float(k2);
         }
-        x[nb][e] = valid[nb][e] ? sv * a.scale_log2 : -INFINITY;
+        // softcap (…wgsl:197-199): cap * tanh((q.k * scale) / cap), then log2 domain
+        const float xs = a.softcap > 0.0f ? a.softcap * tanhf(sv * a.scale / a.softcap) * kLog2e
+                                          : sv * a.scale_log2;
+        x[nb][e] = valid[nb][e] ? xs : -INFINITY;
       }
     float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
     tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
@@ -621,8 +632,8 @@ static int launch_one(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const Pa
 int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
                         const void* q, const int32_t* seq_lens, const void* new_k,
                         const void* new_v, float scale, float* out, uint32_t split_pages,
-                        const float* freq_cis, uint32_t rope_positions,
-                        const doe_launch* launch, uint64_t* ws_needed_out) {
+                        const doe_decode_options* opts, const doe_launch* launch,
+                        uint64_t* ws_needed_out) {
   const uint32_t Hkv = kv->num_kv_heads;
   const uint32_t group = num_heads / Hkv;
   const uint32_t tiles_per_page = kv->page_size / 16;
@@ -677,8 +688,11 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.split_tiles = (int)split_tiles;
   a.max_splits = (int)max_splits;
   a.scale_log2 = scale * kLog2e;
-  a.freq_cis = freq_cis;
-  a.rope_positions = (int)rope_positions;
+  a.freq_cis = opts ? opts->freq_cis : nullptr;
+  a.rope_positions = opts ? (int)opts->rope_positions : 0;
+  a.window = opts ? (int)opts->sliding_window : 0;
+  a.softcap = opts ? opts->attn_softcap : 0.0f;
+  a.scale = scale;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
   // arrival counters of the split stitch start at zero on every launch
   int rc = cuda_status(cudaMemsetAsync(a.counters, 0, (size_t)num_seqs * Hkv * sizeof(unsigned), st),

@@ -100,13 +100,16 @@ def stitch(partials, out=None, stream=None):
 
 
 def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new_v=None, out=None,
-                 split_pages: int = 0, status=None, stream=None, freq_cis=None):
+                 split_pages: int = 0, status=None, stream=None, freq_cis=None, sliding_window: int = 0,
+                 softcap: float = 0.0):
     """Batched GQA decode: q [B,H,D] f16, seq_lens [B] int32 -> out [B,H,D] f32.
 
     With new_k/new_v ([B,Hkv,D] f16) the new token is first written at
     position seq_lens[b] - 1 (quantised for int8 caches).  With freq_cis
     ([positions, D/2, 2] f32 RoPE table) the query and the new K row are
-    rotated at position seq_lens[b] - 1 first (doe_paged_decode_rope)."""
+    rotated at position seq_lens[b] - 1 first (doe_paged_decode_rope).
+    sliding_window > 0 keeps the last sliding_window keys and softcap > 0
+    caps each scaled score as softcap * tanh(s / softcap) (doe_paged_decode_ex)."""
     _need(q, torch.float16, "q")
     _need(seq_lens, torch.int32, "seq_lens")
     B, H, D = q.shape
@@ -117,7 +120,16 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
     l = _launch(ws, status, stream, q.device)
     nk = new_k.data_ptr() if new_k is not None else None
     nv = new_v.data_ptr() if new_v is not None else None
-    if freq_cis is None:
+    if sliding_window or softcap:
+        if freq_cis is not None:
+            _need(freq_cis, torch.float32, "freq_cis")
+        opts = abi.DecodeOptions(freq_cis.data_ptr() if freq_cis is not None else None,
+                                 freq_cis.shape[0] if freq_cis is not None else 0, int(sliding_window),
+                                 float(softcap), 0)
+        abi.check("doe_paged_decode_ex", lib.doe_paged_decode_ex(
+            C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(), nk, nv, float(scale), out.data_ptr(),
+            split_pages, C.byref(opts), C.byref(l)))
+    elif freq_cis is None:
         abi.check("doe_paged_decode", lib.doe_paged_decode(
             C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(), nk, nv, float(scale), out.data_ptr(),
             split_pages, C.byref(l)))

@@ -292,6 +292,29 @@ int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs,
                           float* out, uint32_t split_pages, const float* freq_cis,
                           uint32_t rope_positions, const doe_launch* launch);
 
+/* Options of the batched paged decode (doe_paged_decode_ex), the head256
+ * kernel's remaining uniform words for query_len 1:
+ *   freq_cis / rope_positions  RoPE of the query and the new K row, exactly as
+ *                              doe_paged_decode_rope (null: none);
+ *   sliding_window             0: every key; w: only the last w keys, i.e.
+ *                              key positions >= seq_len - w
+ *                              (attention_head256_f16kv.wgsl:129-135);
+ *   attn_softcap               0: off; c: each scaled score s becomes
+ *                              c * tanh(s / c) (…wgsl:197-199);
+ *   reserved                   must be 0.                                  */
+typedef struct doe_decode_options {
+  const float* freq_cis;
+  uint32_t rope_positions;
+  uint32_t sliding_window;
+  float attn_softcap;
+  uint32_t reserved;
+} doe_decode_options;
+int doe_paged_decode_ex(const doe_paged_kv* kv, uint32_t num_seqs,
+                        uint32_t num_heads, const void* q, const int32_t* seq_lens,
+                        const void* new_k, const void* new_v, float scale,
+                        float* out, uint32_t split_pages,
+                        const doe_decode_options* options, const doe_launch* launch);
+
 /* kv_read over the paged cache (runtime/zig/src/tsir/emit_kernel_body.zig:692-760):
  * copies tokens [start, start+len) of sequence `seq` into k_out/v_out
  * [len, Hkv, D] (element type of the pool); int8 pools also copy scales into

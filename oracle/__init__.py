@@ -82,6 +82,8 @@ def _declare(l: C.CDLL) -> None:
         "doe_oracle_attention_online_f16kv": (_I, [C.POINTER(AttnUniforms), _P, _P, _P, _P, _P, _P, _I]),
         "doe_oracle_paged_decode": (_I, [_U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P,
                                          _U32, _P, _P, _F, _P, _I]),
+        "doe_oracle_paged_decode_ex": (_I, [_U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P,
+                                            _U32, _P, _P, _F, _U32, _F, _P, _I]),
         "doe_oracle_kv_write_dense": (_I, [_P, _P, _P, _P, _U32, _U32, _U32]),
         "doe_oracle_kv_read_dense": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32]),
         "doe_oracle_paged_append": (_I, [_U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P,
@@ -196,8 +198,12 @@ def attention_online_f16kv(u: dict, q, k_bits, v_bits, kv_len_buffer=None,
 
 
 def paged_decode(q_bits, k_pool, v_pool, block_table, kv_lens, scale, *, page_size: int,
-                 k_scale=None, v_scale=None, threads: int = 0) -> np.ndarray:
-    """Batched paged GQA decode; pools f16 bits (uint16) or int8 + f16 scales."""
+                 k_scale=None, v_scale=None, threads: int = 0, sliding_window: int = 0,
+                 softcap: float = 0.0) -> np.ndarray:
+    """Batched paged GQA decode; pools f16 bits (uint16) or int8 + f16 scales.
+
+    sliding_window > 0 keeps the last sliding_window keys; softcap > 0 caps
+    each scaled score as tanh(s / softcap) * softcap."""
     q = _c(q_bits, np.uint16)
     B, H, D = q.shape
     int8 = k_pool.dtype == np.int8
@@ -210,9 +216,10 @@ def paged_decode(q_bits, k_pool, v_pool, block_table, kv_lens, scale, *, page_si
     ks = None if k_scale is None else _c(k_scale, np.uint16)
     vs = None if v_scale is None else _c(v_scale, np.uint16)
     out = np.zeros((B, H, D), np.float32)
-    _check("paged_decode", lib().doe_oracle_paged_decode(
+    _check("paged_decode", lib().doe_oracle_paged_decode_ex(
         B, H, Hkv, D, page_size, num_pages, bt.shape[1], _ptr(q), _ptr(kp), _ptr(vp),
-        _ptr(ks), _ptr(vs), 1 if int8 else 0, _ptr(bt), _ptr(kl), float(scale), _ptr(out), threads))
+        _ptr(ks), _ptr(vs), 1 if int8 else 0, _ptr(bt), _ptr(kl), float(scale), int(sliding_window),
+        float(softcap), _ptr(out), threads))
     return out
 
 

@@ -559,15 +559,20 @@ static uint64_t phys_batched(const void* vctx, uint32_t key_pos) {
   return (uint64_t)page * c->page_size + (key_pos - page_idx * c->page_size);
 }
 
-int doe_oracle_paged_decode(uint32_t num_seqs, uint32_t num_heads,
-                            uint32_t num_kv_heads, uint32_t head_dim,
-                            uint32_t page_size, uint32_t num_pages,
-                            uint32_t max_pages_per_seq, const uint16_t* q,
-                            const void* k_pool, const void* v_pool,
-                            const uint16_t* k_scale, const uint16_t* v_scale,
-                            uint32_t kv_dtype, const int32_t* block_table,
-                            const int32_t* kv_lens, float scale, float* out,
-                            int threads) {
+/* With a sliding window (attention_head256_f16kv.wgsl:129-135 at abs_q =
+ * kv_len - 1, kv_start = 0) only the last `sliding_window` keys are active;
+ * with a softcap (…wgsl:197-199) each scaled score becomes
+ * tanh(s / softcap) * softcap.                                              */
+int doe_oracle_paged_decode_ex(uint32_t num_seqs, uint32_t num_heads,
+                               uint32_t num_kv_heads, uint32_t head_dim,
+                               uint32_t page_size, uint32_t num_pages,
+                               uint32_t max_pages_per_seq, const uint16_t* q,
+                               const void* k_pool, const void* v_pool,
+                               const uint16_t* k_scale, const uint16_t* v_scale,
+                               uint32_t kv_dtype, const int32_t* block_table,
+                               const int32_t* kv_lens, float scale,
+                               uint32_t sliding_window, float softcap, float* out,
+                               int threads) {
   if (!q || !k_pool || !v_pool || !block_table || !kv_lens || !out) return DOE_ORACLE_EINVAL;
   if (num_kv_heads == 0 || num_heads % num_kv_heads || head_dim == 0 || page_size == 0)
     return DOE_ORACLE_EINVAL;
@@ -590,7 +595,10 @@ int doe_oracle_paged_decode(uint32_t num_seqs, uint32_t num_heads,
       } else {
         batched_ctx pctx = {block_table + (uint64_t)b * max_pages_per_seq,
                             max_pages_per_seq, page_size, num_pages};
-        r = online_row(qrow, D, (uint32_t)len, 0, (uint32_t)len, scale, 0.0f,
+        uint32_t min_key = 0;
+        if (sliding_window > 0 && (uint32_t)len > sliding_window)
+          min_key = (uint32_t)len - sliding_window;  /* abs_q - window + 1 */
+        r = online_row(qrow, D, (uint32_t)len, min_key, (uint32_t)len, scale, softcap,
                        &ks, &vs, h / group, phys_batched, &pctx, out + off);
       }
       if (r != DOE_ORACLE_OK) {
@@ -600,6 +608,21 @@ int doe_oracle_paged_decode(uint32_t num_seqs, uint32_t num_heads,
     }
   }
   return rc;
+}
+
+int doe_oracle_paged_decode(uint32_t num_seqs, uint32_t num_heads,
+                            uint32_t num_kv_heads, uint32_t head_dim,
+                            uint32_t page_size, uint32_t num_pages,
+                            uint32_t max_pages_per_seq, const uint16_t* q,
+                            const void* k_pool, const void* v_pool,
+                            const uint16_t* k_scale, const uint16_t* v_scale,
+                            uint32_t kv_dtype, const int32_t* block_table,
+                            const int32_t* kv_lens, float scale, float* out,
+                            int threads) {
+  return doe_oracle_paged_decode_ex(num_seqs, num_heads, num_kv_heads, head_dim, page_size,
+                                    num_pages, max_pages_per_seq, q, k_pool, v_pool, k_scale,
+                                    v_scale, kv_dtype, block_table, kv_lens, scale, 0, 0.0f, out,
+                                    threads);
 }
 
 /* ------------------------------------------------------------------------ */

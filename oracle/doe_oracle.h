@@ -110,6 +110,18 @@ int doe_oracle_paged_decode(uint32_t num_seqs, uint32_t num_heads,
                             uint32_t kv_dtype, const int32_t* block_table,
                             const int32_t* kv_lens, float scale, float* out,
                             int threads);
+/* The same with a sliding window (last `sliding_window` keys; 0 = all) and a
+ * score softcap (s = tanh(s / softcap) * softcap; 0 = off).               */
+int doe_oracle_paged_decode_ex(uint32_t num_seqs, uint32_t num_heads,
+                               uint32_t num_kv_heads, uint32_t head_dim,
+                               uint32_t page_size, uint32_t num_pages,
+                               uint32_t max_pages_per_seq, const uint16_t* q,
+                               const void* k_pool, const void* v_pool,
+                               const uint16_t* k_scale, const uint16_t* v_scale,
+                               uint32_t kv_dtype, const int32_t* block_table,
+                               const int32_t* kv_lens, float scale,
+                               uint32_t sliding_window, float softcap, float* out,
+                               int threads);
 
 /* ---- KV append / read (kv_write, kv_read) ------------------------------ */
 /* Dense single-head form of emit_kernel_body.zig kv_write: cache[pos*D+d]. */

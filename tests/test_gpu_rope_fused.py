@@ -120,3 +120,49 @@ def test_rope_position_beyond_table_is_reported():
     ops.paged_decode(c, _dev(w.q), _dev(w.seq_lens), w.scale, status=status, freq_cis=_dev(table))
     torch.cuda.synchronize()
     assert int(status.item()) & DOE_DEVICE_ERR_POSITION
+
+
+# ---- sliding window and softcap (attention_head256_f16kv.wgsl:129-135, 197-199)
+@pytest.mark.parametrize("kv_dtype", ["f16", "int8"])
+@pytest.mark.parametrize("window,softcap", [(1, 0.0), (16, 0.0), (100, 0.0), (5000, 0.0), (0, 30.0),
+                                            (0, 5.0), (300, 50.0)])
+def test_paged_decode_window_softcap(kv_dtype, window, softcap):
+    w = workloads.small_paged(71, [0, 15, 16, 257, 1000, 2049], num_heads=32, num_kv_heads=8, kv_dtype=kv_dtype)
+    c = _cache(w)
+    kp, vp, ks, vs = _host(c)
+    oracle.paged_append(w.new_k[:, None].view(np.uint16), w.new_v[:, None].view(np.uint16), kp, vp,
+                        w.block_table, w.ctx.astype(np.int32), page_size=w.page_size, k_scale=ks, v_scale=vs)
+    ref = oracle.paged_decode(w.q.view(np.uint16), kp, vp, w.block_table, w.seq_lens, w.scale,
+                              page_size=w.page_size, k_scale=ks, v_scale=vs, sliding_window=window,
+                              softcap=softcap)
+    status = ops.status_word()
+    for split_pages in (0, 2):
+        out = ops.paged_decode(c, _dev(w.q), _dev(w.seq_lens), w.scale,
+                               new_k=_dev(w.new_k) if split_pages == 0 else None,
+                               new_v=_dev(w.new_v) if split_pages == 0 else None,
+                               status=status, split_pages=split_pages, sliding_window=window, softcap=softcap)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        within(out.cpu().numpy(), ref, F16_TOL)
+    gk, gv, _, _ = _host(c)
+    assert np.array_equal(gk, kp) and np.array_equal(gv, vp)
+
+
+def test_paged_decode_window_softcap_and_rope_together():
+    w = workloads.small_paged(73, [3, 400, 1500], num_heads=16, num_kv_heads=2)
+    c = _cache(w)
+    kp, vp, _, _ = _host(c)
+    table = rope_table(2048)
+    p = w.ctx.astype(np.int64)
+    rq = np.stack([rotate_f16(w.q[b][None], table, int(p[b]))[0] for b in range(w.num_seqs)])
+    rk = np.stack([rotate_f16(w.new_k[b][None], table, int(p[b]))[0] for b in range(w.num_seqs)])
+    oracle.paged_append(rk[:, None].view(np.uint16), w.new_v[:, None].view(np.uint16), kp, vp, w.block_table,
+                        w.ctx.astype(np.int32), page_size=w.page_size)
+    ref = oracle.paged_decode(rq.view(np.uint16), kp, vp, w.block_table, w.seq_lens, w.scale,
+                              page_size=w.page_size, sliding_window=512, softcap=20.0)
+    status = ops.status_word()
+    out = ops.paged_decode(c, _dev(w.q), _dev(w.seq_lens), w.scale, new_k=_dev(w.new_k), new_v=_dev(w.new_v),
+                           status=status, freq_cis=_dev(table), sliding_window=512, softcap=20.0)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    within(out.cpu().numpy(), ref, F16_TOL)

@@ -268,3 +268,35 @@ def test_rope_matches_definition():
     x0, x1 = x[..., :D // 2], x[..., D // 2:]
     np.testing.assert_allclose(out[..., :D // 2], x0 * c - x1 * s, rtol=1e-6, atol=1e-6)
     np.testing.assert_allclose(out[..., D // 2:], x0 * s + x1 * c, rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("window,softcap", [(0, 30.0), (7, 0.0), (16, 20.0), (100, 0.0)])
+def test_paged_decode_window_softcap_matches_head256_restatement(window, softcap):
+    """The batched paged decode with a sliding window / softcap equals the
+    head256 restatement (attention_head256_f16kv.wgsl) run causally at
+    abs_q = kv_len - 1 with the same window and softcap."""
+    rng = np.random.default_rng(17)
+    B, H, Hkv, D, page = 3, 8, 2, 64, 16
+    lens = np.array([5, 40, 33], np.int32)
+    table, num_pages = _paged_setup(rng, B, Hkv, D, page, lens)
+    kpool = np.zeros((num_pages * page, Hkv, D), np.uint16)
+    vpool = np.zeros_like(kpool)
+    dense_k, dense_v = [], []
+    for b in range(B):
+        L = int(lens[b])
+        kk = (rng.standard_normal((1, L, Hkv, D)) * 2).astype(np.float16).view(np.uint16)
+        vv = rng.standard_normal((1, L, Hkv, D)).astype(np.float16).view(np.uint16)
+        oracle.paged_append(kk, vv, kpool, vpool, table[b:b + 1], np.array([0], np.int32), page_size=page)
+        dense_k.append(kk[0])
+        dense_v.append(vv[0])
+    q = rng.standard_normal((B, H, D)).astype(np.float16).view(np.uint16)
+    scale = 1.0 / np.sqrt(D)
+    out = oracle.paged_decode(q, kpool, vpool, table, lens, scale, page_size=page, sliding_window=window,
+                              softcap=softcap)
+    for b in range(B):
+        L = int(lens[b])
+        u = dict(num_heads=H, num_kv_heads=Hkv, head_dim=D, seq_len=L, query_len=1, scale=scale,
+                 is_causal=1, start_pos=L - 1, attn_softcap=softcap, sliding_window=window, kv_len_source=0,
+                 kv_start=0, page_size=page, kv_layout=0)
+        ref = oracle.attention_online_f16kv(u, oracle.h2f(q[b])[None], dense_k[b], dense_v[b])[0]
+        np.testing.assert_array_equal(out[b], ref)
