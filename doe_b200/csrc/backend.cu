@@ -647,6 +647,18 @@ int doe_cuda_buffer_read(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset, vo
                 (unsigned long long)it->second.bytes);
   if (size == 0) return DOE_OK;
   DOE_TRY(bind_device(ctx));
+  // The read waits for the copy before returning, so a page-locked
+  // destination can take the DMA directly (no staging hop).
+  cudaPointerAttributes pa;
+  if (cudaPointerGetAttributes(&pa, dst) == cudaSuccess && pa.type == cudaMemoryTypeHost) {
+    DOE_TRY(cu(ctx, cudaMemcpyAsync(dst, static_cast<uint8_t*>(it->second.ptr) + offset, size,
+                                    cudaMemcpyDeviceToHost, ctx->stream),
+               "cudaMemcpyAsync(D2H)"));
+    DOE_TRY(cu(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize"));
+    ctx->staging_used = 0;
+    return DOE_OK;
+  }
+  cudaGetLastError();  // a pageable pointer is not an error
   DOE_TRY(ensure_staging(ctx, size));
   DOE_TRY(cu(ctx, cudaMemcpyAsync(ctx->staging + ctx->staging_used,
                                   static_cast<uint8_t*>(it->second.ptr) + offset, size,
