@@ -5,15 +5,21 @@
 // The WGSL kernel runs one 64-lane workgroup per head and holds every score
 // in workgroup memory (kv_len <= 2048).  Here the KV length is split across
 // CTAs (split-K) so all SMs stream K/V; each warp keeps an online softmax
-// over its tokens, the CTA merges its warps, and combine_splits_kernel
-// stitches the splits (the LSE recipe of
-// bench/tools/attention_kv_axis_sharded_stitch.py:46-90).
+// over its tokens and the CTA merges its warps.  The splits of one head form
+// a thread-block cluster (up to 16 CTAs): each writes its partial into the
+// first CTA's shared memory and, after one cluster barrier, that CTA
+// stitches them with the LSE recipe of
+// bench/tools/attention_kv_axis_sharded_stitch.py:46-90 -- one launch, no
+// workspace.  Heads needing more than 16 splits fall back to partials in the
+// workspace and combine_splits_kernel.
 //
 // Numerics: f32 throughout, natural-exp softmax.  The reference clamps
 // s - max to [-30, 30] before exp (…wgsl:90); only the lower bound can bind
 // (s - max <= 0), where it lifts a weight below e^-30 = 9.4e-14 up to
 // 9.4e-14.  This kernel uses the exact weight, so each such key differs by
 // less than 9.4e-14 * |v| in the numerator.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace doe {
@@ -32,9 +38,14 @@ struct DecodeF32Args {
 constexpr int kF32Warps = 4;
 constexpr int kF32MaxPerLane = 8;  // head_dim <= 256
 
+constexpr int kF32MaxCluster = 16;
+
+// One CTA's split of one head: online softmax over tokens
+// [split * split_tokens, ...) per warp, then the warps merged.  Leaves the
+// CTA's un-normalised O in o_sm[0..D) and returns its (max, sum).
 template <int PER_LANE>
-__global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const DecodeF32Args a) {
-  const int split = blockIdx.x, head = blockIdx.y;
+__device__ __forceinline__ void decode_f32_cta(const DecodeF32Args& a, int split, int head, float* o_sm,
+                                               float& M_out, float& L_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int D = a.head_dim;
   const int t_begin = split * a.split_tokens;
@@ -124,11 +135,28 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const 
     f[w] = M == -INFINITY ? 0.0f : expf(sm_m[w] - M);
     L += f[w] * sm_l[w];
   }
-  const int nsplits = (a.kv_len + a.split_tokens - 1) / a.split_tokens;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float O = 0.0f;
 #pragma unroll
     for (int w = 0; w < kF32Warps; ++w) O += f[w] * sm_o[w][d];
+    o_sm[d] = O;
+  }
+  M_out = M;
+  L_out = L;
+}
+
+// Splits as partials in the workspace (stitched by combine_splits_kernel).
+template <int PER_LANE>
+__global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const DecodeF32Args a) {
+  const int split = blockIdx.x, head = blockIdx.y;
+  const int D = a.head_dim;
+  __shared__ float o_sm[32 * kF32MaxPerLane];
+  float M, L;
+  decode_f32_cta<PER_LANE>(a, split, head, o_sm, M, L);
+  __syncthreads();
+  const int nsplits = (a.kv_len + a.split_tokens - 1) / a.split_tokens;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    const float O = o_sm[d];
     if (nsplits == 1) {
       a.out[(size_t)head * D + d] = L > 0.0f ? O / L : 0.0f;
     } else {
@@ -140,6 +168,83 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_split_kernel(const 
       }
     }
   }
+}
+
+// The splits of one head as one cluster (gridDim.x == cluster size): each
+// CTA stores (O, max, sum) into the first CTA's shared memory, which
+// stitches them after the cluster barrier.
+template <int PER_LANE>
+__global__ void __launch_bounds__(kF32Warps * 32) decode_f32_cluster_kernel(const DecodeF32Args a) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int split = blockIdx.x, head = blockIdx.y;
+  const int D = a.head_dim;
+  __shared__ float o_sm[32 * kF32MaxPerLane];
+  __shared__ float part_o[kF32MaxCluster][32 * kF32MaxPerLane];
+  __shared__ float part_ml[kF32MaxCluster][2];
+  float M, L;
+  decode_f32_cta<PER_LANE>(a, split, head, o_sm, M, L);
+  __syncthreads();
+  float* lead_o = cluster.map_shared_rank(&part_o[split][0], 0);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) lead_o[d] = o_sm[d];
+  if (threadIdx.x == 0) {
+    float* lead_ml = cluster.map_shared_rank(&part_ml[split][0], 0);
+    lead_ml[0] = M;
+    lead_ml[1] = L;
+  }
+  cluster.sync();  // every partial is in the first CTA's shared memory
+  if (split != 0) return;
+  const int n = (int)gridDim.x;
+  float MM = -INFINITY;
+  for (int sp = 0; sp < n; ++sp) MM = fmaxf(MM, part_ml[sp][0]);
+  float LL = 0.0f;
+  for (int sp = 0; sp < n; ++sp) LL += (MM == -INFINITY ? 0.0f : expf(part_ml[sp][0] - MM)) * part_ml[sp][1];
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float O = 0.0f;
+    for (int sp = 0; sp < n; ++sp) O += (MM == -INFINITY ? 0.0f : expf(part_ml[sp][0] - MM)) * part_o[sp][d];
+    a.out[(size_t)head * D + d] = LL > 0.0f ? O / LL : 0.0f;
+  }
+}
+
+// One cluster of `max_splits` CTAs per head; DOE_UNSUPPORTED when the device
+// will not run a cluster that large (the caller then uses the workspace path).
+template <int PER_LANE>
+static int launch_cluster_one(const DecodeF32Args& a, cudaStream_t s) {
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(decode_f32_cluster_kernel<PER_LANE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    cudaGetLastError();
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.max_splits, a.num_heads);
+  cfg.blockDim = dim3(kF32Warps * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = a.max_splits;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  // whether the device runs a cluster of this size, asked once per size
+  static int runs[kF32MaxCluster + 1] = {};  // 0 unknown, 1 yes, -1 no
+  int& known = runs[a.max_splits];
+  if (known == 0) {
+    int clusters = 0;
+    known = (cudaOccupancyMaxActiveClusters(&clusters, decode_f32_cluster_kernel<PER_LANE>, &cfg) ==
+                 cudaSuccess && clusters >= 1) ? 1 : -1;
+    cudaGetLastError();
+  }
+  if (known < 0) return DOE_UNSUPPORTED;
+  return cuda_status(cudaLaunchKernelEx(&cfg, decode_f32_cluster_kernel<PER_LANE>, a),
+                     "decode_f32_cluster_kernel");
+}
+
+static int launch_decode_f32_cluster(const DecodeF32Args& a, int per_lane, cudaStream_t s) {
+  if (per_lane <= 2) return launch_cluster_one<2>(a, s);
+  if (per_lane <= 4) return launch_cluster_one<4>(a, s);
+  return launch_cluster_one<8>(a, s);
 }
 
 static void decode_f32_plan(uint32_t num_heads, uint32_t head_dim, uint32_t kv_len,
@@ -188,6 +293,10 @@ int launch_decode_f32(const float* q, const float* k, const float* v, float* out
   cudaStream_t s = static_cast<cudaStream_t>(launch->stream);
   dim3 grid(ms, num_heads), block(kF32Warps * 32);
   const int per_lane = (int)((head_dim + 31) / 32);
+  if (ms > 1 && ms <= kF32MaxCluster && num_heads <= 65535) {
+    int rc = launch_decode_f32_cluster(a, per_lane, s);
+    if (rc != DOE_UNSUPPORTED) return rc;  // else: the workspace path below
+  }
   if (per_lane <= 2) decode_f32_split_kernel<2><<<grid, block, 0, s>>>(a);
   else if (per_lane <= 4) decode_f32_split_kernel<4><<<grid, block, 0, s>>>(a);
   else decode_f32_split_kernel<8><<<grid, block, 0, s>>>(a);
