@@ -399,8 +399,12 @@ __global__ void __launch_bounds__(kWarps * 32)
     float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
     tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
     tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
-    const float m_new = fmaxf(m_run, tmax);  // finite: the tile holds a valid key
-    const float corr = exp2f(m_run - m_new);
+    // lazy running max: it moves (and the accumulators are rescaled) only when
+    // a row's max rises by more than 2^8, so p <= 256 (exact in f16 P) and
+    // most tiles skip the rescale; the tile holds a valid key, so tmax is finite
+    const bool grow = tmax > m_run + 8.0f;
+    const float m_new = grow ? tmax : m_run;
+    const float corr = grow ? exp2f(m_run - m_new) : 1.0f;
     float p[2][2];
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb)
@@ -424,13 +428,15 @@ __global__ void __launch_bounds__(kWarps * 32)
     const uint32_t pb0 = pack_half2(pv[0][0], pv[0][1]);
     const uint32_t pb1 = pack_half2(pv[1][0], pv[1][1]);
 
-    // accumulator columns are heads 2c, 2c+1: fetch their row corrections
-    const float cA = __shfl_sync(0xffffffffu, corr, (2 * c) * 4);
-    const float cB = __shfl_sync(0xffffffffu, corr, (2 * c + 1) * 4);
+    if (__any_sync(0xffffffffu, grow)) {
+      // accumulator columns are heads 2c, 2c+1: fetch their row corrections
+      const float cA = __shfl_sync(0xffffffffu, corr, (2 * c) * 4);
+      const float cB = __shfl_sync(0xffffffffu, corr, (2 * c + 1) * 4);
 #pragma unroll
-    for (int mb = 0; mb < 8; ++mb) {
-      acc[mb][0] *= cA; acc[mb][2] *= cA;
-      acc[mb][1] *= cB; acc[mb][3] *= cB;
+      for (int mb = 0; mb < 8; ++mb) {
+        acc[mb][0] *= cA; acc[mb][2] *= cA;
+        acc[mb][1] *= cB; acc[mb][3] *= cB;
+      }
     }
 
     // f16 V rows past the sequence end may hold any bits: zero them
