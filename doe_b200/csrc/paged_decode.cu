@@ -18,8 +18,11 @@
 //   S  = Q K^T   : m16n8k16, rows = the GROUP query heads of one kv head
 //   O^T = V^T P^T: m16n8k16, rows = 16 head dims, cols = the GROUP heads
 // so P moves from the S accumulator into the PV B operand without shuffles.
-// int8 tiles convert exactly to f16 in registers; the K scale multiplies S
-// and the V scale folds into P.  Scores run in the log2 domain (exp2f).
+// int8 tiles convert exactly to f16 in registers as 1152 + b (the byte, sign
+// flipped, in the low half of 1024's f16 bits); the 1152 offsets are removed
+// once per row instead of per element: S -= 1152 * sum(q), O -= 1152 *
+// sum(f16 P).  The K scale multiplies S and the V scale folds into P.  Scores
+// run in the log2 domain (exp2f).
 #include "tma.cuh"
 
 namespace doe {
@@ -267,6 +270,24 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
   }
 
+  // int8: 1152 * sum of this row's query (its 32 dims per lane, then the 4
+  // lanes of the row), taken off every score
+  float q1152 = 0.0f;
+  if (INT8) {
+    float qs = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&qa[j][w]));
+        qs += f.x + f.y;
+      }
+    qs += __shfl_xor_sync(0xffffffffu, qs, 1);
+    qs += __shfl_xor_sync(0xffffffffu, qs, 2);
+    q1152 = 1152.0f * qs;
+  }
+  float p1152 = 0.0f;  // int8: running sum of this row's f16 P (times 1152 at the end)
+
   const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
   const uint32_t wbase = smem_addr(dsmem) + warp * R::kWarpBytes;
   auto slot = [&](int k) { return wbase + (k % P) * R::kTile; };
@@ -369,9 +390,10 @@ __global__ void __launch_bounds__(kWarps * 32)
           b0 = w4(v, 2 * (j & 1));
           b1 = w4(v, 2 * (j & 1) + 1);
         } else {
-          const uint32_t x = w4(kraw[nb][j >> 2], j & 3);
-          b0 = s8x2_to_f16x2(prmt(x, x, 0x0100));
-          b1 = s8x2_to_f16x2(prmt(x, x, 0x0302));
+          // bytes 0,1 / 2,3 -> f16 halves 1152 + k: sign-flipped byte under 0x64
+          const uint32_t x = w4(kraw[nb][j >> 2], j & 3) ^ 0x80808080u;
+          b0 = prmt(x, 0x64646464u, 0x4140);
+          b1 = prmt(x, 0x64646464u, 0x4342);
         }
         mma_16816(s[nb], qa[j][0], 0u, qa[j][1], 0u, b0, b1);
       }
@@ -389,7 +411,7 @@ __global__ void __launch_bounds__(kWarps * 32)
         float sv = s[nb][e];
         if (INT8) {
           __half2 k2 = *reinterpret_cast<__half2*>(&ksc[nb]);
-          sv *= e ? __high2float(k2) : __low2float(k2);
+          sv = (sv - q1152) * (e ? __high2float(k2) : __low2float(k2));
         }
         // softcap (…wgsl:197-199): cap * tanh((q.k * scale) / cap), then log2 domain
         const float xs = a.softcap > 0.0f ? a.softcap * tanhf(sv * a.scale / a.softcap) * kLog2e
@@ -427,6 +449,12 @@ __global__ void __launch_bounds__(kWarps * 32)
       }
     const uint32_t pb0 = pack_half2(pv[0][0], pv[0][1]);
     const uint32_t pb1 = pack_half2(pv[1][0], pv[1][1]);
+    if (INT8) {
+      // the f16 P the PV product uses, summed for the 1152 offset of V
+      const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&pb0));
+      const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&pb1));
+      p1152 = p1152 * corr + ((f0.x + f0.y) + (f1.x + f1.y));
+    }
 
     if (__any_sync(0xffffffffu, grow)) {
       // accumulator columns are heads 2c, 2c+1: fetch their row corrections
@@ -463,10 +491,25 @@ __global__ void __launch_bounds__(kWarps * 32)
         const uint32_t x0 = w4(vraw[0][0], w), x1 = w4(vraw[1][0], w);
         const uint32_t x2 = w4(vraw[2][0], w), x3 = w4(vraw[3][0], w);
         const uint32_t lo = e ? 0x0602u : 0x0400u, hi = e ? 0x0703u : 0x0501u;
-        a0 = s8x2_to_f16x2(prmt(x0, x1, lo)); a1 = s8x2_to_f16x2(prmt(x0, x1, hi));
-        a2 = s8x2_to_f16x2(prmt(x2, x3, lo)); a3 = s8x2_to_f16x2(prmt(x2, x3, hi));
+        // f16 halves 1152 + v: (byte pair & 0x00ff00ff) ^ 0x64806480, one LOP3
+        a0 = (prmt(x0, x1, lo) & 0x00ff00ffu) ^ 0x64806480u; a1 = (prmt(x0, x1, hi) & 0x00ff00ffu) ^ 0x64806480u;
+        a2 = (prmt(x2, x3, lo) & 0x00ff00ffu) ^ 0x64806480u; a3 = (prmt(x2, x3, hi) & 0x00ff00ffu) ^ 0x64806480u;
       }
       mma_16816(acc[mb], a0, a1, a2, a3, pb0, pb1);
+    }
+  }
+
+  if (INT8) {
+    // O -= 1152 * sum(f16 P) per head: accumulator columns are heads 2c, 2c+1
+    float ps = p1152;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 1);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 2);
+    const float oA = 1152.0f * __shfl_sync(0xffffffffu, ps, (2 * c) * 4);
+    const float oB = 1152.0f * __shfl_sync(0xffffffffu, ps, (2 * c + 1) * 4);
+#pragma unroll
+    for (int mb = 0; mb < 8; ++mb) {
+      acc[mb][0] -= oA; acc[mb][2] -= oA;
+      acc[mb][1] -= oB; acc[mb][3] -= oB;
     }
   }
 
