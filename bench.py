@@ -505,8 +505,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8"], default="all",
-                    help="time one workload only (no e2e or CPU leg): headline = config 3")
+    ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8", "append"], default="all",
+                    help="time one workload only (no e2e or CPU leg): headline = config 3, "
+                         "append = config 4b chunk quantise-append")
     ap.add_argument("--split-pages", type=int, default=0,
                     help="pages per split of the paged decode (0 = the library's choice)")
     ap.add_argument("--seqs", type=int, default=0,
@@ -523,11 +524,16 @@ def main():
     pk = peaks()
     from doe_b200 import workloads
 
-    if args.only in ("prefill", "f32", "int8"):
+    if args.only in ("prefill", "f32", "int8", "append"):
         if args.only == "prefill":
             r = measure_prefill(args.steps, args.warmup, world, pk)
         elif args.only == "f32":
             r = measure_f32(args.steps, args.warmup, world, pk)
+        elif args.only == "append":
+            w4, _ = sharded(lambda r: workloads.paged_int8(seed=3 + r, num_seqs=args.seqs or 32), world, rank)
+            cache4, _ = build_paged(w4, 3)
+            r = {"config": "config 4b: 32 x 512 tokens quantised into the paged cache",
+                 **measure_chunk_append(w4, cache4, args.steps, args.warmup, world, pk)}
         else:
             w4, g4 = sharded(lambda r: workloads.paged_int8(seed=3 + r, num_seqs=args.seqs or 32),
                              world, rank)
