@@ -338,6 +338,43 @@ def measure_prefill(steps, warmup, world, pk):
             "l2": "flushed (256 MB write) between steps"}
 
 
+def measure_decoder(steps, warmup, world, rank, pk):
+    """Config 5: the 4-layer bf16 decoder step (batch 32, ctx 4096), tensor
+    parallel by KV head over the `world` ranks, captured in a CUDA graph."""
+    import torch
+
+    from doe_b200 import decoder
+
+    cfg = decoder.DecoderConfig()
+    dec = decoder.Decoder(cfg, seed=4, rank=rank, world=world)
+    x0 = torch.from_numpy(np.random.default_rng(4).standard_normal((cfg.batch, cfg.hidden),
+                                                                   dtype=np.float32)).cuda()
+    x = x0.clone()
+    dec.step(x)  # eager warm-up: NCCL, workspaces, tensor maps
+    torch.cuda.synchronize()
+    x.copy_(x0)
+    dec.capture(x)
+    try:
+        total, each = time_steps(dec.replay, steps, warmup, world)
+        total = max_over_ranks(world, [total])[0]
+        status = int(dec.status.item())
+        finite = bool(torch.isfinite(x).all().item())
+    finally:
+        dec.release()
+    ms = total / steps
+    job_bytes = cfg.weight_bytes() + cfg.kv_read_bytes()
+    rank_bytes = job_bytes / world
+    return {"config": "config 5: 4-layer Llama-style decoder, hidden 4096, 32/8 heads, FFN 14336 SwiGLU, "
+                      "bf16 weights N(0,0.02) seed 4, batch 32 at ctx 4096, f16 paged KV",
+            "parallelism": f"tp{world} by KV head (NCCL all-reduce after o_proj and down_proj)"
+                           if world > 1 else "tp1",
+            "scaling": "strong", "ms_per_step": ms, "tokens_per_s": cfg.batch / (ms / 1e3),
+            "bytes_per_step": job_bytes, "gbs": job_bytes / (ms / 1e3) / 1e9,
+            "per_gpu_frac": rank_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
+            "gpu_launches_per_step": dec.launches_per_step(), "graph": "one CUDA graph per step",
+            "status": status, "output_finite": finite}
+
+
 def measure_e2e(w, cache, steps, warmup, world, gw=None):
     """Same decode step through doe_cuda_dispatch with host buffers."""
     gw = gw if gw is not None else w
@@ -505,9 +542,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8", "append"], default="all",
+    ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8", "append", "decoder"],
+                    default="all",
                     help="time one workload only (no e2e or CPU leg): headline = config 3, "
-                         "append = config 4b chunk quantise-append")
+                         "append = config 4b chunk quantise-append, decoder = config 5")
     ap.add_argument("--split-pages", type=int, default=0,
                     help="pages per split of the paged decode (0 = the library's choice)")
     ap.add_argument("--seqs", type=int, default=0,
@@ -524,8 +562,10 @@ def main():
     pk = peaks()
     from doe_b200 import workloads
 
-    if args.only in ("prefill", "f32", "int8", "append"):
-        if args.only == "prefill":
+    if args.only in ("prefill", "f32", "int8", "append", "decoder"):
+        if args.only == "decoder":
+            r = measure_decoder(args.steps, args.warmup, world, rank, pk)
+        elif args.only == "prefill":
             r = measure_prefill(args.steps, args.warmup, world, pk)
         elif args.only == "f32":
             r = measure_f32(args.steps, args.warmup, world, pk)
@@ -573,6 +613,9 @@ def main():
             extras["prefill"] = measure_prefill(10, 3, world, pk)
         except Exception as e:  # reported, never hidden
             extras["prefill"] = {"error": str(e)[:300]}
+        torch.cuda.empty_cache()
+        extras["decoder"] = measure_decoder(10, 3, world, rank, pk)
+        torch.cuda.empty_cache()
 
     e2e = None
     if args.only == "all":

@@ -77,7 +77,19 @@ class DecodeOptions(C.Structure):
     """doe_decode_options: RoPE table, sliding window, softcap of the paged decode."""
 
     _fields_ = [("freq_cis", C.c_void_p), ("rope_positions", C.c_uint32), ("sliding_window", C.c_uint32),
-                ("attn_softcap", C.c_float), ("reserved", C.c_uint32)]
+                ("attn_softcap", C.c_float), ("flags", C.c_uint32)]
+
+
+DECODE_OUT_BF16 = 0x1
+LINEAR_STORE, LINEAR_SWIGLU = 0, 1
+DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
+
+
+class LinearOut(C.Structure):
+    """doe_linear_out: output segments, dtype and epilogue of doe_linear_bf16."""
+
+    _fields_ = [("out", C.c_void_p * 3), ("width", C.c_uint32 * 3), ("dtype", C.c_uint32),
+                ("epilogue", C.c_uint32), ("residual", C.c_void_p)]
 
 
 _P = C.c_void_p
@@ -129,6 +141,9 @@ SIGNATURES = {
     "doe_kv_write_dense": (_I, [_P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _LP]),
     "doe_kv_read_dense": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _LP]),
     "doe_rope_f32": (_I, [_P, _P, _U32, _U32, _U32, _U32, _LP]),
+    "doe_rmsnorm_bf16": (_I, [_P, _P, _F, _P, _U32, _U32, _LP]),
+    "doe_linear_workspace_bytes": (_U64, [_U32, _U32]),
+    "doe_linear_bf16": (_I, [_P, _P, _U32, _U32, _U32, C.POINTER(LinearOut), _LP]),
     "doe_attention_decode_f32_noalloc": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _F, _P]),
     "doe_kv_pool_create": (_I, [_U32, _U32, _U32, _U32, C.POINTER(_P)]),
     "doe_kv_pool_destroy": (_I, [_P]),

@@ -43,7 +43,7 @@ def _compile(src: Path, verbose_ptxas: bool) -> tuple[Path, str]:
     obj = BUILD / (src.name + ".o")
     cmd = [nvcc(), *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cpp":
-        cmd = [nvcc(), *COMMON, "-x", "c++", "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc(), *COMMON, "-Wno-deprecated-gpu-targets", "-x", "c++", "-c", str(src), "-o", str(obj)]
     elif verbose_ptxas:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -1,6 +1,7 @@
 // common.cuh -- shared device helpers for the sm_100a attention / KV kernels.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -62,6 +62,11 @@ int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, 
                        uint32_t num_heads, uint32_t num_kv_heads, float scale, uint32_t causal,
                        const doe_paged_kv* cache, uint32_t cache_seq, uint32_t cache_start,
                        const doe_launch* launch);
+uint64_t linear_workspace(uint32_t n_out, uint32_t k);
+int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
+                  const doe_linear_out* out, const doe_launch* launch);
+int launch_rmsnorm(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
+                   const doe_launch* launch);
 int launch_rope(float* qk, const float* freq_cis, uint32_t seq_len, uint32_t num_heads,
                 uint32_t head_dim, uint32_t position_offset, const doe_launch* launch);
 

@@ -1,0 +1,439 @@
+// linear_sm100.cu -- the decoder block's matrix products and RMSNorm for
+// decode-sized batches on sm_100a.
+//
+// y[b, n] = sum_k x[b, k] w[n, k] with batch <= 32 is a weight stream: each
+// weight byte is read once and used for at most 32 products, so the product
+// is HBM-bound and the kernel's job is to keep every SM's share of the weight
+// bytes in flight.  The product is turned around so the weights are the MMA's
+// M side: D[128 weight rows, 32 batch] += W[128 x 16] * X^T[16 x 32] with
+// tcgen05.mma kind::f16 (bf16 operands, f32 accumulation in TMEM).
+//
+// Work split (stream-K): the (tile, 64-wide k block) iterations of the whole
+// product are divided evenly over a persistent grid of at most one CTA per
+// SM, so the grid is balanced for any (n_out, k); a CTA's range can start and
+// end inside a tile.  A CTA that covers a whole tile runs the epilogue from
+// TMEM; otherwise it writes its f32 partial tile to the workspace and the
+// last contributor to arrive sums all the tile's partials in contributor
+// order (the result does not depend on arrival order) and runs the epilogue.
+//
+//   warp 0     TMA producer: per k block one 128 x 64 weight box and one
+//              32 x 64 activation box (rows past `batch` read as zero) into
+//              an 8-stage ring, 128-byte swizzle
+//   warp 1     TMEM owner + MMA issuer (one elected lane): 4 MMAs of K = 16
+//              per stage into one of two 32-column accumulators, so the
+//              epilogue of one tile overlaps the MMAs of the next
+//   warps 2-5  epilogue: warp w reads TMEM lane quarter w % 4 (32 weight
+//              rows), 32 batch columns per thread
+//
+// Every mbarrier wait is bounded; on timeout the kernel sets
+// DOE_DEVICE_ERR_TIMEOUT, the roles stop, copies and MMAs still in flight are
+// waited for (bounded) and TMEM is freed.  No cluster multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "tma.cuh"
+#include "umma.cuh"
+
+namespace doe {
+namespace lin {
+
+constexpr int BM = 128, NB = 32;
+constexpr int kBoxes = 1;                 // 64-wide k boxes per stage
+constexpr int BK = 64 * kBoxes;           // k per stage
+constexpr int kStages = 8;
+constexpr int kMinIters = 1;              // fewest stages a CTA streams
+constexpr int kCtasPerSm = 1;
+constexpr uint32_t kWBox = BM * 64 * 2;   // 16 KB: 128 weight rows x 64 k
+constexpr uint32_t kXBox = NB * 64 * 2;   // 4 KB: 32 activation rows x 64 k
+constexpr uint32_t kWBytes = kBoxes * kWBox;
+constexpr uint32_t kXBytes = kBoxes * kXBox;
+constexpr uint32_t kStageBytes = kWBytes + kXBytes;  // a multiple of 1024
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 2 * NB;
+constexpr int kMaxCtas = 512;
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
+
+enum Bar { FULL0 = 0, EMPTY0 = FULL0 + kStages, ACC_FULL0 = EMPTY0 + kStages, ACC_EMPTY0 = ACC_FULL0 + 2,
+           MMA_DONE = ACC_EMPTY0 + 2, NUM_BARS };
+constexpr uint32_t OFF_BAR = kStages * kStageBytes;
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * NUM_BARS;  // TMEM slot, abort flag, last-arrival flag
+constexpr uint32_t OFF_XCHG = OFF_BAR + 512;            // SwiGLU up values [NB][64] f32
+constexpr uint32_t kSmemBytes = OFF_XCHG + NB * 64 * 4 + 1024;  // + alignment slack
+
+struct Args {
+  void* out[3];
+  int seg_end[3];          // exclusive end (output column) of each segment
+  const float* residual;   // [batch, n_out] f32 or null
+  float* part;             // [ctas][2][NB][BM] f32 partial tiles
+  unsigned* counters;      // [tiles], zero between launches
+  int32_t* status;
+  int batch, n_out, kb, tiles, ctas, epilogue, dtype;
+  long long iters;         // tiles * kb
+};
+
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                         int32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      *abort_flag = 1;
+      report(status, DOE_DEVICE_ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// The four epilogue warps (128 threads) on named barrier 1.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+__device__ __forceinline__ bool epi_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 p, %1, 0;\nbar.red.and.pred q, 1, 128, p;\nselp.u32 %0, 1, 0, q;\n}\n"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ long long it_begin(long long c, const Args& a) { return c * a.iters / a.ctas; }
+// The CTA whose iteration range holds iteration i.
+__device__ __forceinline__ int cta_of(long long i, const Args& a) {
+  return (int)(((i + 1) * a.ctas - 1) / a.iters);
+}
+
+__device__ __forceinline__ void store_elem(void* base, int dtype, size_t idx, float y) {
+  if (dtype == DOE_DTYPE_BF16)
+    static_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(y);
+  else if (dtype == DOE_DTYPE_F16)
+    static_cast<__half*>(base)[idx] = __float2half_rn(y);
+  else
+    static_cast<float*>(base)[idx] = y;
+}
+
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+    linear_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+                  const Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 16);
+  float* xchg = reinterpret_cast<float*>(smem + OFF_XCHG);
+  auto bar = [&](int i) { return smem_addr(&bars[i]); };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long it0 = it_begin(blockIdx.x, a), it1 = it_begin(blockIdx.x + 1, a);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i >= ACC_EMPTY0 && i < ACC_EMPTY0 + 2) ? 4u : 1u);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
+                     smem_addr(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      long long n = 0;
+      bool ok = true;
+      for (long long it = it0; it < it1; ++it, ++n) {
+        const int s = (int)(n % kStages);
+        if (n >= kStages && !(ok = wait_bar(bar(EMPTY0 + s), (uint32_t)((n / kStages) - 1) & 1, abort_flag,
+                                            a.status)))
+          break;
+        const int tile = (int)(it / a.kb), k = (int)(it - (long long)tile * a.kb);
+        const uint32_t dst = sbase + s * kStageBytes;
+        mbar_expect_tx(bar(FULL0 + s), kStageBytes);
+#pragma unroll
+        for (int b = 0; b < kBoxes; ++b) {
+          tma_load_3d(dst + b * kWBox, &tm_w, bar(FULL0 + s), k * BK + b * 64, 0, tile * BM);
+          tma_load_3d(dst + kWBytes + b * kXBox, &tm_x, bar(FULL0 + s), k * BK + b * 64, 0, 0);
+        }
+      }
+      if (!ok) {
+        // no copy may land after the CTA exits: wait for the last issued ones
+        for (long long j = n > kStages ? n - kStages : 0; j < n; ++j)
+          mbar_wait_bounded(bar(FULL0 + (int)(j % kStages)), (uint32_t)(j / kStages) & 1);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idesc = idesc_kind_f16(true, false, BM, NB);
+    const uint64_t d0 = sdesc(sbase, 16, 1024);  // stage 0's weight box; its activations kWBytes on
+    auto wait = [&](int b, uint32_t parity) {
+      return __all_sync(0xffffffffu, wait_bar(bar(b), parity, abort_flag, a.status));
+    };
+    long long n = 0;
+    int seg = 0;
+    bool ok = true;
+    for (long long it = it0; it < it1 && ok; ++seg) {
+      const long long tile = it / a.kb;
+      const long long end = min(it1, (tile + 1) * a.kb);
+      const int acc = seg & 1;
+      if (seg >= 2 && !(ok = wait(ACC_EMPTY0 + acc, (uint32_t)((seg >> 1) - 1) & 1))) break;
+      tc_fence_after();
+      const long long first = it;
+      for (; it < end; ++it, ++n) {
+        const int s = (int)(n % kStages);
+        if (!(ok = wait(FULL0 + s, (uint32_t)(n / kStages) & 1))) break;
+        tc_fence_after();
+        const uint64_t dw = d0 + ((s * kStageBytes) >> 4), dx = d0 + ((s * kStageBytes + kWBytes) >> 4);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          umma_elect(tmem + acc * NB, dw + (((kk >> 2) * kWBox + (kk & 3) * 32) >> 4),
+                     dx + (((kk >> 2) * kXBox + (kk & 3) * 32) >> 4), idesc, (it > first || kk > 0) ? 1u : 0u);
+        commit_elect(bar(EMPTY0 + s));  // the stage is free once these MMAs are done
+      }
+      if (ok) commit_elect(bar(ACC_FULL0 + acc));
+    }
+    // every MMA this warp issued has finished once MMA_DONE flips
+    commit_elect(bar(MMA_DONE));
+    __all_sync(0xffffffffu, mbar_wait_bounded(bar(MMA_DONE), 0));
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // weight row within the tile = TMEM lane
+    const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    const long long first_tile = it0 / a.kb;
+    int seg = 0;
+    for (long long it = it0; it < it1; ++seg) {
+      const long long tile = it / a.kb;
+      const long long end = min(it1, (tile + 1) * a.kb);
+      const bool whole = it == tile * a.kb && end == (tile + 1) * a.kb;
+      it = end;
+      const int acc = seg & 1;
+      const bool ok = epi_all(wait_bar(bar(ACC_FULL0 + acc), (uint32_t)(seg >> 1) & 1, abort_flag, a.status));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r[NB];
+      tmem_ld32(t_lane + acc * NB, r);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(ACC_EMPTY0 + acc));
+      float v[NB];
+#pragma unroll
+      for (int j = 0; j < NB; ++j) v[j] = __uint_as_float(r[j]);
+
+      if (!whole) {
+        const int slot = tile == first_tile ? 0 : 1;
+        float* p = a.part + ((size_t)blockIdx.x * 2 + slot) * NB * BM + row;
+#pragma unroll
+        for (int j = 0; j < NB; ++j) __stcg(p + j * BM, v[j]);
+        __threadfence();
+        epi_sync();
+        const int c0 = cta_of(tile * a.kb, a), c1 = cta_of((tile + 1) * a.kb - 1, a);
+        if (threadIdx.x == 64) {
+          const unsigned old = atomicAdd(&a.counters[tile], 1u);
+          const int last = old == (unsigned)(c1 - c0);
+          if (last) a.counters[tile] = 0u;  // ready for the next launch
+          *last_flag = last;
+        }
+        epi_sync();
+        if (!*last_flag) continue;
+        __threadfence();
+#pragma unroll
+        for (int j = 0; j < NB; ++j) v[j] = 0.0f;
+        for (int c = c0; c <= c1; ++c) {
+          const int sl = tile == it_begin(c, a) / a.kb ? 0 : 1;
+          const float* pc = a.part + ((size_t)c * 2 + sl) * NB * BM + row;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) v[j] += __ldcg(pc + j * BM);
+        }
+      }
+
+      if (a.epilogue == DOE_LINEAR_SWIGLU) {
+        // rows 0-63 of the tile are gate rows, 64-127 the matching up rows
+        if (row >= 64) {
+#pragma unroll
+          for (int j = 0; j < NB; ++j) xchg[j * 64 + row - 64] = v[j];
+        }
+        epi_sync();
+        if (row < 64) {
+          const size_t width = (size_t)a.n_out / 2, col = (size_t)tile * 64 + row;
+#pragma unroll
+          for (int j = 0; j < NB; ++j) {
+            if (j < a.batch) {
+              const float g = v[j], u = xchg[j * 64 + row];
+              store_elem(a.out[0], a.dtype, j * width + col, g / (1.0f + expf(-g)) * u);
+            }
+          }
+        }
+        // the next writes to xchg come after the next segment's epi_all
+      } else {
+        const int col0 = (int)tile * BM;
+        const int sg = col0 < a.seg_end[0] ? 0 : (col0 < a.seg_end[1] ? 1 : 2);
+        const int base = sg == 0 ? 0 : (sg == 1 ? a.seg_end[0] : a.seg_end[1]);
+        const size_t width = (size_t)((sg == 0 ? a.seg_end[0] : (sg == 1 ? a.seg_end[1] : a.seg_end[2])) - base);
+        void* dst = sg == 0 ? a.out[0] : (sg == 1 ? a.out[1] : a.out[2]);
+        const int col = col0 + row;
+#pragma unroll
+        for (int j = 0; j < NB; ++j) {
+          if (j < a.batch) {
+            float y = v[j];
+            if (a.residual) y += a.residual[(size_t)j * a.n_out + col];
+            store_elem(dst, a.dtype, j * width + (col - base), y);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// out[r, :] = bf16(x[r, :] * (1 / sqrt(mean(x[r, :]^2) + eps)) * gamma)
+constexpr int kNormThreads = 256;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __restrict__ x,
+                                                               const __nv_bfloat16* __restrict__ gamma,
+                                                               __nv_bfloat16* __restrict__ out, int cols,
+                                                               float eps) {
+  __shared__ float warp_sum[kNormThreads / 32];
+  const size_t row = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+  const int n4 = cols >> 2;
+  float ss = 0.0f;
+  for (int i = threadIdx.x; i < n4; i += kNormThreads) {
+    const float4 v = xr[i];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) warp_sum[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) total += warp_sum[w];
+  const float inv = 1.0f / sqrtf(total / (float)cols + eps);
+  const uint2* g2 = reinterpret_cast<const uint2*>(gamma);
+  uint2* o2 = reinterpret_cast<uint2*>(out + row * cols);
+  for (int i = threadIdx.x; i < n4; i += kNormThreads) {
+    const float4 v = xr[i];
+    const uint2 gw = g2[i];
+    const float2 g01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw.x));
+    const float2 g23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw.y));
+    __nv_bfloat162 y01 = __floats2bfloat162_rn(v.x * inv * g01.x, v.y * inv * g01.y);
+    __nv_bfloat162 y23 = __floats2bfloat162_rn(v.z * inv * g23.x, v.w * inv * g23.y);
+    uint2 ow;
+    ow.x = *reinterpret_cast<uint32_t*>(&y01);
+    ow.y = *reinterpret_cast<uint32_t*>(&y23);
+    o2[i] = ow;
+  }
+}
+
+}  // namespace lin
+
+// ---- host -----------------------------------------------------------------
+namespace {
+
+int num_sms() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148;
+    }
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+uint64_t counters_bytes(uint32_t n_out) { return ((uint64_t)(n_out / lin::BM) * 4 + 255) / 256 * 256; }
+
+}  // namespace
+
+uint64_t linear_workspace(uint32_t n_out, uint32_t k) {
+  (void)k;
+  return counters_bytes(n_out) + (uint64_t)lin::kMaxCtas * 2 * lin::NB * lin::BM * sizeof(float);
+}
+
+int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
+                  const doe_linear_out* o, const doe_launch* launch) {
+  const uint32_t tiles = n_out / lin::BM, kb = k / lin::BK;
+  if (k % lin::BK != 0) {
+    set_op_error("doe_linear_bf16: k %u must be a multiple of %d", k, lin::BK);
+    return DOE_UNSUPPORTED;
+  }
+  const long long iters = (long long)tiles * kb;
+  int ctas = num_sms() * lin::kCtasPerSm;
+  if (ctas > lin::kMaxCtas) ctas = lin::kMaxCtas;
+  const long long by_work = iters / lin::kMinIters > 0 ? iters / lin::kMinIters : 1;
+  if ((long long)ctas > by_work) ctas = (int)by_work;
+  const uint64_t need = linear_workspace(n_out, k);
+  if (launch->workspace == nullptr || launch->workspace_bytes < need) {
+    set_op_error("doe_linear_bf16: workspace of %llu bytes required, %llu given", (unsigned long long)need,
+                 (unsigned long long)launch->workspace_bytes);
+    return DOE_INVALID_ARGUMENT;
+  }
+  lin::Args a;
+  int end = 0;
+  for (int i = 0; i < 3; ++i) {
+    a.out[i] = o->out[i];
+    end += (int)o->width[i];
+    a.seg_end[i] = o->width[i] ? end : 0x7fffffff;
+  }
+  a.residual = o->residual;
+  a.counters = static_cast<unsigned*>(launch->workspace);
+  a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(launch->workspace) + counters_bytes(n_out));
+  a.status = launch->status;
+  a.batch = (int)batch;
+  a.n_out = (int)n_out;
+  a.kb = (int)kb;
+  a.tiles = (int)tiles;
+  a.ctas = ctas;
+  a.epilogue = (int)o->epilogue;
+  a.dtype = (int)o->dtype;
+  a.iters = iters;
+  CUtensorMap mw, mx;
+  int rc = encode_rows_map(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, 1, n_out, 64, lin::BM,
+                           "doe_linear_bf16");
+  if (rc == DOE_OK)
+    rc = encode_rows_map(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, 1, batch, 64, lin::NB,
+                         "doe_linear_bf16");
+  if (rc != DOE_OK) return rc;
+  static bool attr_set = false;
+  if (!attr_set) {
+    rc = cuda_status(cudaFuncSetAttribute(lin::linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          lin::kSmemBytes),
+                     "cudaFuncSetAttribute(linear)");
+    if (rc != DOE_OK) return rc;
+    attr_set = true;
+  }
+  lin::linear_kernel<<<ctas, lin::kThreads, lin::kSmemBytes, static_cast<cudaStream_t>(launch->stream)>>>(
+      mw, mx, a);
+  return cuda_status(cudaGetLastError(), "linear_kernel");
+}
+
+int launch_rmsnorm(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
+                   const doe_launch* launch) {
+  lin::rmsnorm_kernel<<<rows, lin::kNormThreads, 0, static_cast<cudaStream_t>(launch->stream)>>>(
+      x, static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(out), (int)cols, eps);
+  return cuda_status(cudaGetLastError(), "rmsnorm_kernel");
+}
+
+}  // namespace doe

@@ -238,7 +238,7 @@ int paged_decode_common(const char* who, const doe_paged_kv* kv, uint32_t num_se
   if (num_seqs == 0) return DOE_OK;
   if (num_seqs > 65535) return invalid("%s: at most 65535 sequences per launch", who);
   if (opts != nullptr) {
-    if (opts->reserved != 0) return invalid("%s: options.reserved must be 0", who);
+    if ((opts->flags & ~DOE_DECODE_OUT_BF16) != 0) return invalid("%s: unknown bits in options.flags", who);
     if (opts->freq_cis != nullptr) {
       int rr = check_rope_table(who, opts->freq_cis, opts->rope_positions);
       if (rr != DOE_OK) return rr;
@@ -350,6 +350,58 @@ int doe_rope_f32(float* qk, const float* freq_cis, uint32_t seq_len, uint32_t nu
   if (seq_len > 65535) return invalid("doe_rope_f32: at most 65535 positions per launch");
   return launch_rope(qk, freq_cis, seq_len, num_heads, head_dim, position_offset,
                      launch_or_default(launch));
+}
+
+int doe_rmsnorm_bf16(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
+                     const doe_launch* launch) {
+  if (!x || !gamma || !out) return invalid("doe_rmsnorm_bf16: null pointer");
+  if (cols == 0 || cols % 4 != 0) return invalid("doe_rmsnorm_bf16: cols must be a positive multiple of 4");
+  if (rows > 2147483647u) return invalid("doe_rmsnorm_bf16: too many rows");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(gamma) % 8 ||
+      reinterpret_cast<uintptr_t>(out) % 8)
+    return invalid("doe_rmsnorm_bf16: x must be 16-byte aligned, gamma and out 8-byte aligned");
+  if (!(eps >= 0.0f)) return invalid("doe_rmsnorm_bf16: eps must be >= 0");
+  if (rows == 0) return DOE_OK;
+  return launch_rmsnorm(x, gamma, eps, out, rows, cols, launch_or_default(launch));
+}
+
+uint64_t doe_linear_workspace_bytes(uint32_t n_out, uint32_t k) { return linear_workspace(n_out, k); }
+
+int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
+                    const doe_linear_out* out, const doe_launch* launch) {
+  const char* who = "doe_linear_bf16";
+  if (!x || !w || !out) return invalid("%s: x, w and out are required", who);
+  if (batch == 0) return DOE_OK;
+  if (batch > 32) {
+    set_op_error("%s: batch %u > 32 (the kernel's MMA N)", who, batch);
+    return DOE_UNSUPPORTED;
+  }
+  if (n_out == 0 || n_out % 128 != 0) return invalid("%s: n_out %u must be a positive multiple of 128", who, n_out);
+  if (k == 0 || k % 64 != 0) return invalid("%s: k %u must be a positive multiple of 64", who, k);
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16)
+    return invalid("%s: x and w must be 16-byte aligned", who);
+  if (out->dtype > DOE_DTYPE_F32) return invalid("%s: unknown dtype %u", who, out->dtype);
+  if (out->epilogue == DOE_LINEAR_SWIGLU) {
+    if (!out->out[0] || out->residual) return invalid("%s: SwiGLU writes out[0] only, without residual", who);
+  } else if (out->epilogue == DOE_LINEAR_STORE) {
+    uint32_t total = 0;
+    bool gap = false;
+    for (int i = 0; i < 3; ++i) {
+      if (out->width[i] == 0) {
+        gap = true;
+        continue;
+      }
+      if (gap || out->width[i] % 128 != 0 || !out->out[i])
+        return invalid("%s: segments must be leading, non-null, multiples of 128 wide", who);
+      total += out->width[i];
+    }
+    if (total != n_out) return invalid("%s: segment widths sum to %u, n_out is %u", who, total, n_out);
+    if (out->residual && (out->dtype != DOE_DTYPE_F32 || out->width[1] != 0))
+      return invalid("%s: a residual needs f32 output and a single segment", who);
+  } else {
+    return invalid("%s: unknown epilogue %u", who, out->epilogue);
+  }
+  return launch_linear(x, w, batch, n_out, k, out, launch_or_default(launch));
 }
 
 }  // extern "C"

@@ -37,7 +37,7 @@ struct PagedDecodeArgs {
   const int32_t* seq_lens;     // [B]
   const __half* new_k;      // [B, Hkv, D] or null
   const __half* new_v;
-  float* out;               // [B, H, D]
+  float* out;               // [B, H, D] f32, or bf16 storage when out_bf16
   float* part_o;            // [B*Hkv*max_splits, GROUP, D]
   float* part_ml;           // [B*Hkv*max_splits, GROUP, 2]
   unsigned* counters;       // [B*Hkv] arrivals per (b, g); zeroed before each launch
@@ -49,6 +49,7 @@ struct PagedDecodeArgs {
   float scale;              // the natural-domain scale (softcap path)
   int num_heads, num_kv_heads, num_pages, page_size, max_pages;
   int split_tiles, max_splits;
+  int out_bf16;
   float scale_log2;
 };
 
@@ -554,10 +555,16 @@ __global__ void __launch_bounds__(kWarps * 32)
       }
     }
   }
-  float* out_row = a.out + ((size_t)b * a.num_heads + (size_t)g * GROUP) * kD;
+  const size_t out_row = ((size_t)b * a.num_heads + (size_t)g * GROUP) * kD;
+  auto store = [&](int hh, float v) {
+    if (a.out_bf16)
+      reinterpret_cast<__nv_bfloat16*>(a.out)[out_row + hh * kD + dim] = __float2bfloat16_rn(v);
+    else
+      a.out[out_row + hh * kD + dim] = v;
+  };
   if (nsplits == 1) {
 #pragma unroll
-    for (int hh = 0; hh < GROUP; ++hh) out_row[hh * kD + dim] = L[hh] > 0.0f ? O[hh] * (1.0f / L[hh]) : 0.0f;
+    for (int hh = 0; hh < GROUP; ++hh) store(hh, L[hh] > 0.0f ? O[hh] * (1.0f / L[hh]) : 0.0f);
     return;
   }
   // ---- split partials; the last split of (b, g) to finish stitches them ---
@@ -595,7 +602,7 @@ __global__ void __launch_bounds__(kWarps * 32)
         LL += f * __ldcg(a.part_ml + prow * 2 + 1);
       }
     }
-    out_row[hh * kD + dim] = LL > 0.0f ? OO * (1.0f / LL) : 0.0f;
+    store(hh, LL > 0.0f ? OO * (1.0f / LL) : 0.0f);
   }
 }
 
@@ -742,6 +749,7 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.window = opts ? (int)opts->sliding_window : 0;
   a.softcap = opts ? opts->attn_softcap : 0.0f;
   a.scale = scale;
+  a.out_bf16 = (opts && (opts->flags & DOE_DECODE_OUT_BF16)) ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
   // arrival counters of the split stitch start at zero on every launch
   int rc = cuda_status(cudaMemsetAsync(a.counters, 0, (size_t)num_seqs * Hkv * sizeof(unsigned), st),

@@ -101,7 +101,7 @@ def stitch(partials, out=None, stream=None):
 
 def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new_v=None, out=None,
                  split_pages: int = 0, status=None, stream=None, freq_cis=None, sliding_window: int = 0,
-                 softcap: float = 0.0):
+                 softcap: float = 0.0, out_dtype=torch.float32):
     """Batched GQA decode: q [B,H,D] f16, seq_lens [B] int32 -> out [B,H,D] f32.
 
     With new_k/new_v ([B,Hkv,D] f16) the new token is first written at
@@ -109,23 +109,28 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
     ([positions, D/2, 2] f32 RoPE table) the query and the new K row are
     rotated at position seq_lens[b] - 1 first (doe_paged_decode_rope).
     sliding_window > 0 keeps the last sliding_window keys and softcap > 0
-    caps each scaled score as softcap * tanh(s / softcap) (doe_paged_decode_ex)."""
+    caps each scaled score as softcap * tanh(s / softcap) (doe_paged_decode_ex).
+    out_dtype torch.bfloat16 writes a bf16 output (DOE_DECODE_OUT_BF16)."""
     _need(q, torch.float16, "q")
     _need(seq_lens, torch.int32, "seq_lens")
+    if out_dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("out_dtype must be float32 or bfloat16")
     B, H, D = q.shape
-    out = torch.empty((B, H, D), dtype=torch.float32, device=q.device) if out is None else out
+    out = torch.empty((B, H, D), dtype=out_dtype, device=q.device) if out is None else out
+    _need(out, out_dtype, "out")
+    flags = abi.DECODE_OUT_BF16 if out_dtype == torch.bfloat16 else 0
     kv = cache.struct()
     lib = abi.lib()
     ws = lib.doe_paged_decode_workspace_bytes(C.byref(kv), B, H, split_pages)
     l = _launch(ws, status, stream, q.device)
     nk = new_k.data_ptr() if new_k is not None else None
     nv = new_v.data_ptr() if new_v is not None else None
-    if sliding_window or softcap:
+    if sliding_window or softcap or flags:
         if freq_cis is not None:
             _need(freq_cis, torch.float32, "freq_cis")
         opts = abi.DecodeOptions(freq_cis.data_ptr() if freq_cis is not None else None,
                                  freq_cis.shape[0] if freq_cis is not None else 0, int(sliding_window),
-                                 float(softcap), 0)
+                                 float(softcap), flags)
         abi.check("doe_paged_decode_ex", lib.doe_paged_decode_ex(
             C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(), nk, nv, float(scale), out.data_ptr(),
             split_pages, C.byref(opts), C.byref(l)))
@@ -228,3 +233,71 @@ def attention_prefill_f16(q, k, v, scale: float, causal: bool = True, cache: Pag
         1 if causal else 0, C.byref(kv) if kv is not None else None, cache_seq, cache_start,
         C.byref(l)))
     return out
+
+
+_LINEAR_WS: dict[int, torch.Tensor] = {}
+
+
+def linear_workspace(n_out: int, k: int, device=None) -> torch.Tensor:
+    """The zero-initialised workspace doe_linear_bf16 keeps its tile counters in.
+
+    Separate from `workspace()`: its counters must be zero before a call, and
+    every call that completes without a timeout leaves them zero again."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    need = int(abi.lib().doe_linear_workspace_bytes(n_out, k))
+    buf = _LINEAR_WS.get(key)
+    if buf is None or buf.numel() < need:
+        buf = torch.zeros(need, dtype=torch.uint8, device=dev)
+        _LINEAR_WS[key] = buf
+    return buf
+
+
+_DTYPES = {torch.bfloat16: abi.DTYPE_BF16, torch.float16: abi.DTYPE_F16, torch.float32: abi.DTYPE_F32}
+
+
+def rmsnorm(x, gamma, eps: float, out=None, status=None, stream=None):
+    """x [rows, cols] f32, gamma [cols] bf16 -> bf16 x / sqrt(mean(x^2) + eps) * gamma."""
+    _need(x, torch.float32, "x")
+    _need(gamma, torch.bfloat16, "gamma")
+    rows, cols = x.shape
+    out = torch.empty((rows, cols), dtype=torch.bfloat16, device=x.device) if out is None else out
+    _need(out, torch.bfloat16, "out")
+    l = _launch(0, status, stream, x.device)
+    abi.check("doe_rmsnorm_bf16", abi.lib().doe_rmsnorm_bf16(
+        x.data_ptr(), gamma.data_ptr(), float(eps), out.data_ptr(), rows, cols, C.byref(l)))
+    return out
+
+
+def linear(x, w, outs, *, swiglu: bool = False, residual=None, status=None, stream=None, ws=None):
+    """doe_linear_bf16: x [batch, k] bf16 times w [n_out, k] bf16 transposed.
+
+    `outs` is a list of 1-3 contiguous tensors of one dtype (bf16, f16 or f32),
+    each [batch, width]; with swiglu=True a single [batch, n_out/2] output of
+    silu(gate) * up (w packed in 128-row blocks: 64 gate rows, 64 up rows).
+    `residual` ([batch, n_out] f32, f32 output) is added to the product."""
+    _need(x, torch.bfloat16, "x")
+    _need(w, torch.bfloat16, "w")
+    batch, k = x.shape
+    n_out = w.shape[0]
+    if w.shape[1] != k:
+        raise ValueError(f"w is {tuple(w.shape)}, x is {tuple(x.shape)}")
+    if not 1 <= len(outs) <= 3:
+        raise ValueError("1 to 3 output segments")
+    dt = outs[0].dtype
+    lo = abi.LinearOut()
+    for i, o in enumerate(outs):
+        _need(o, dt, f"outs[{i}]")
+        lo.out[i] = o.data_ptr()
+        lo.width[i] = o.shape[-1] if not swiglu else 0
+    lo.dtype = _DTYPES[dt]
+    lo.epilogue = abi.LINEAR_SWIGLU if swiglu else abi.LINEAR_STORE
+    if residual is not None:
+        _need(residual, torch.float32, "residual")
+        lo.residual = residual.data_ptr()
+    ws = linear_workspace(n_out, k, x.device) if ws is None else ws
+    s = stream if stream is not None else torch.cuda.current_stream(x.device)
+    l = abi.Launch(s.cuda_stream, ws.data_ptr(), ws.numel(), status.data_ptr() if status is not None else None)
+    abi.check("doe_linear_bf16", abi.lib().doe_linear_bf16(
+        x.data_ptr(), w.data_ptr(), batch, n_out, k, C.byref(lo), C.byref(l)))
+    return outs

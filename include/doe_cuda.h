@@ -301,13 +301,17 @@ int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs,
  *                              (attention_head256_f16kv.wgsl:129-135);
  *   attn_softcap               0: off; c: each scaled score s becomes
  *                              c * tanh(s / c) (…wgsl:197-199);
- *   reserved                   must be 0.                                  */
+ *   flags                      DOE_DECODE_OUT_BF16: `out` is bf16 storage
+ *                              [B, H, D] (each f32 result rounded to
+ *                              nearest even), the input of a bf16 o_proj;
+ *                              other bits must be 0.                       */
+#define DOE_DECODE_OUT_BF16 0x1u
 typedef struct doe_decode_options {
   const float* freq_cis;
   uint32_t rope_positions;
   uint32_t sliding_window;
   float attn_softcap;
-  uint32_t reserved;
+  uint32_t flags;
 } doe_decode_options;
 int doe_paged_decode_ex(const doe_paged_kv* kv, uint32_t num_seqs,
                         uint32_t num_heads, const void* q, const int32_t* seq_lens,
@@ -345,6 +349,60 @@ int doe_kv_read_dense(const void* k_cache, const void* v_cache, void* k_out,
 int doe_rope_f32(float* qk, const float* freq_cis, uint32_t seq_len,
                  uint32_t num_heads, uint32_t head_dim,
                  uint32_t position_offset, const doe_launch* launch);
+
+/* ======================================================================== */
+/* Decoder-block operators (a Llama-style ONNX decoder through the ORT EP). */
+/* The EP's Compute for the f32 basic ops (MatMul, MatMul+Add, LayerNorm:  */
+/* runtime/bridge/onnxruntime-ep/src/doe_ort_ep.cc:2165, :2302, :2062)     */
+/* becomes, for bf16 decode graphs: SimplifiedLayerNormalization ->        */
+/* doe_rmsnorm_bf16; MatMul with its fused Split / SwiGLU / residual Add ->  */
+/* doe_linear_bf16; GroupQueryAttention with rotary -> doe_paged_decode_ex   */
+/* (DOE_DECODE_OUT_BF16); the tensor-parallel AllReduce -> NCCL.            */
+/* ======================================================================== */
+
+/* out[r, c] = bf16(x[r, c] * (1 / sqrt(mean_c(x[r, :]^2) + eps)) * gamma[c])
+ * x [rows, cols] f32 (the residual stream), gamma [cols] bf16, out [rows,
+ * cols] bf16; cols a multiple of 4; 16-byte aligned.                       */
+int doe_rmsnorm_bf16(const float* x, const void* gamma, float eps, void* out,
+                     uint32_t rows, uint32_t cols, const doe_launch* launch);
+
+/* Linear layer for decode-sized batches, y[b, n] = sum_k x[b, k] w[n, k]
+ * with f32 accumulation on the tensor cores; the weights stream from HBM
+ * once.  x [batch, k] bf16 with batch <= 32; w [n_out, k] bf16 (output
+ * features as rows: an ONNX MatMul initializer [k, n] is transposed once at
+ * load); n_out a multiple of 128, k a multiple of 64; 16-byte aligned.
+ * Epilogues (doe_linear_out.epilogue):
+ *   DOE_LINEAR_STORE   y split into up to 3 consecutive column segments of
+ *                      widths width[i] (multiples of 128, summing to n_out),
+ *                      segment i written to out[i] as [batch, width[i]] in
+ *                      `dtype` (a plain MatMul: one segment; the fused QKV
+ *                      projection: q | k | v).  With `residual` ([batch,
+ *                      n_out] f32; dtype f32; one segment) the result is
+ *                      residual + y: the Add after o_proj / down_proj
+ *                      (residual may alias out[0]).
+ *   DOE_LINEAR_SWIGLU  w rows come in 128-row blocks of 64 gate rows then the
+ *                      64 matching up rows; out[0] [batch, n_out / 2] =
+ *                      silu(gate) * up in `dtype` (silu(g) = g / (1 + e^-g)).
+ * Workspace: at least doe_linear_workspace_bytes(n_out, k) bytes.  It starts
+ * with per-tile arrival counters that must be zero before the first call on
+ * that workspace; every call that sets no DOE_DEVICE_ERR_TIMEOUT leaves them
+ * zero again, so one zeroed workspace serves any number of calls that run
+ * one after another on a stream.                                           */
+#define DOE_LINEAR_STORE 0u
+#define DOE_LINEAR_SWIGLU 1u
+#define DOE_DTYPE_BF16 0u
+#define DOE_DTYPE_F16 1u
+#define DOE_DTYPE_F32 2u
+typedef struct doe_linear_out {
+  void* out[3];
+  uint32_t width[3];       /* 0 = segment unused                           */
+  uint32_t dtype;          /* DOE_DTYPE_*                                   */
+  uint32_t epilogue;       /* DOE_LINEAR_*                                  */
+  const float* residual;   /* DOE_LINEAR_STORE with dtype f32, or null      */
+} doe_linear_out;
+uint64_t doe_linear_workspace_bytes(uint32_t n_out, uint32_t k);
+int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out,
+                    uint32_t k, const doe_linear_out* out, const doe_launch* launch);
 
 /* ======================================================================== */
 /* Allocation-free f32 decode.  This entry point has no counterpart in the   */

@@ -1,0 +1,118 @@
+"""GPU parity of the decoder block's linear layer and RMSNorm (doe_linear_bf16,
+doe_rmsnorm_bf16) against float64 products of the same bf16 inputs.
+
+f32 outputs: |y - ref| <= 2e-5 * max(|ref|, 1).  bf16 / f16 outputs are the
+f32 result rounded once, so they may differ from the rounded reference by one
+unit in the last place: |y - ref| <= 2^-7 * |ref| + 2e-5 for bf16, 2^-10 *
+|ref| + 2e-5 for f16.  Stream-K partial sums are added in a fixed order, so
+repeated calls give identical bits.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from doe_b200 import ops
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+def _bf16(g, shape, std):
+    return (torch.from_numpy(g.standard_normal(shape, dtype=np.float32)) * std).to(torch.bfloat16)
+
+
+def _ref(x, w):
+    return x.double() @ w.double().T
+
+
+def _close(got, ref, dtype):
+    got = got.double().cpu()
+    rel = {torch.float32: 0.0, torch.bfloat16: 2.0 ** -7, torch.float16: 2.0 ** -10}[dtype]
+    bound = rel * ref.abs() + 2e-5 * ref.abs().clamp(min=1.0)
+    bad = (got - ref).abs() > bound
+    assert not bad.any(), f"{int(bad.sum())} of {bad.numel()} out of tolerance; max err " \
+                          f"{float((got - ref).abs().max()):.3g}"
+
+
+@pytest.mark.parametrize("batch,n_out,k", [(32, 768, 4096), (32, 4096, 512), (5, 256, 128), (1, 128, 64),
+                                           (32, 128, 14336), (17, 1920, 1792)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_linear_store(batch, n_out, k, dtype):
+    g = np.random.default_rng(batch * 7 + n_out + k)
+    x, w = _bf16(g, (batch, k), 1.0), _bf16(g, (n_out, k), 0.02)
+    out = torch.full((batch, n_out), float("nan"), dtype=dtype, device="cuda")
+    status = ops.status_word()
+    ops.linear(x.cuda(), w.cuda(), [out], status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    _close(out, _ref(x, w), dtype)
+
+
+def test_linear_qkv_segments_f16():
+    g = np.random.default_rng(3)
+    batch, k = 32, 1024
+    widths = [1024, 256, 256]
+    x, w = _bf16(g, (batch, k), 1.0), _bf16(g, (sum(widths), k), 0.02)
+    outs = [torch.full((batch, wd), float("nan"), dtype=torch.float16, device="cuda") for wd in widths]
+    ops.linear(x.cuda(), w.cuda(), outs)
+    ref = _ref(x, w)
+    c = 0
+    for o, wd in zip(outs, widths):
+        _close(o, ref[:, c:c + wd], torch.float16)
+        c += wd
+
+
+@pytest.mark.parametrize("batch,feat,k", [(32, 512, 512), (9, 64, 4096), (32, 1792, 4096)])
+def test_linear_swiglu(batch, feat, k):
+    g = np.random.default_rng(feat + k)
+    x = _bf16(g, (batch, k), 1.0)
+    gate, up = _bf16(g, (feat, k), 0.02), _bf16(g, (feat, k), 0.02)
+    # pack: 128-row blocks of 64 gate rows then the matching 64 up rows
+    w = torch.cat([gate.view(-1, 64, k), up.view(-1, 64, k)], dim=1).reshape(2 * feat, k)
+    out = torch.empty((batch, feat), dtype=torch.bfloat16, device="cuda")
+    ops.linear(x.cuda(), w.cuda(), [out], swiglu=True)
+    gr, ur = _ref(x, gate), _ref(x, up)
+    # the kernel rounds its f32 gate/up sums; the reference is float64
+    ref = gr / (1.0 + torch.exp(-gr)) * ur
+    _close(out, ref, torch.bfloat16)
+
+
+def test_linear_residual_in_place_and_repeatable():
+    g = np.random.default_rng(9)
+    batch, n_out, k = 32, 1024, 3584
+    x, w = _bf16(g, (batch, k), 1.0), _bf16(g, (n_out, k), 0.02)
+    res = torch.from_numpy(g.standard_normal((batch, n_out), dtype=np.float32))
+    h = res.clone().cuda()
+    xd, wd = x.cuda(), w.cuda()
+    ops.linear(xd, wd, [h], residual=h)  # h = h + x w^T in place
+    _close(h, res.double() + _ref(x, w), torch.float32)
+    a = torch.empty((batch, n_out), dtype=torch.float32, device="cuda")
+    b = torch.empty_like(a)
+    ops.linear(xd, wd, [a])
+    ops.linear(xd, wd, [b])
+    assert torch.equal(a, b)
+    ws = ops.linear_workspace(n_out, k)
+    assert int(ws[: 4 * (n_out // 128)].sum().item()) == 0, "tile counters not left at zero"
+
+
+def test_linear_rejects_bad_shapes():
+    x = torch.zeros((33, 64), dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros((128, 64), dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros((33, 128), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ops.abi.DoeError):
+        ops.linear(x, w, [out])
+    w2 = torch.zeros((100, 64), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(ops.abi.DoeError):
+        ops.linear(x[:4].contiguous(), w2, [torch.zeros((4, 100), dtype=torch.bfloat16, device="cuda")])
+
+
+@pytest.mark.parametrize("rows,cols", [(32, 4096), (3, 512), (1, 4)])
+def test_rmsnorm(rows, cols):
+    g = np.random.default_rng(rows + cols)
+    x = torch.from_numpy(g.standard_normal((rows, cols), dtype=np.float32) * 3)
+    gamma = _bf16(g, (cols,), 1.0)
+    out = ops.rmsnorm(x.cuda(), gamma.cuda(), 1e-5)
+    xd = x.double()
+    ref = xd / torch.sqrt((xd * xd).mean(dim=1, keepdim=True) + 1e-5) * gamma.double()
+    _close(out, ref, torch.bfloat16)

@@ -166,3 +166,17 @@ def test_paged_decode_window_softcap_and_rope_together():
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     within(out.cpu().numpy(), ref, F16_TOL)
+
+
+@pytest.mark.parametrize("split_pages", [0, 2])
+def test_paged_decode_bf16_output_is_the_rounded_f32_output(split_pages):
+    w = workloads.small_paged(79, [0, 33, 700], num_heads=32, num_kv_heads=8)
+    c = _cache(w)
+    table = rope_table(1024)
+    args = dict(seq_lens=_dev(w.seq_lens), scale=w.scale, split_pages=split_pages, freq_cis=_dev(table))
+    f32 = ops.paged_decode(c, _dev(w.q), **args)
+    status = ops.status_word()
+    b16 = ops.paged_decode(c, _dev(w.q), **args, status=status, out_dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(b16, f32.to(torch.bfloat16))
