@@ -81,6 +81,7 @@ class DecodeOptions(C.Structure):
 
 
 DECODE_OUT_BF16 = 0x1
+DECODE_COUNTERS_ZEROED = 0x2
 LINEAR_STORE, LINEAR_SWIGLU = 0, 1
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 

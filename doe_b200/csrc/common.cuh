@@ -17,6 +17,14 @@ __device__ __forceinline__ void report(int32_t* status, int32_t bits) {
   if (status) atomicOr(status, bits);
 }
 
+// Programmatic dependent launch.  pdl_trigger lets the next kernel on the
+// stream (launched with launch_pdl) start its prologue while this one runs;
+// pdl_wait blocks until the previous kernel on the stream has completed and
+// its writes are visible.  A kernel launched with launch_pdl must call
+// pdl_wait before it touches memory the previous kernel writes or reads.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 // ---- warp mma: D = A(16x16 f16, row) * B(16x8 f16, col) + C (f32) -------
 // Fragment layout (PTX ISA, mma.m16n8k16 .f16): lane = 4*g + t.
 //   A regs: {(g, 2t..2t+1), (g+8, 2t..), (g, 2t+8..), (g+8, 2t+8..)}

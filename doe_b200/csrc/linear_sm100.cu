@@ -41,7 +41,8 @@ constexpr int BM = 128, NB = 32;
 constexpr int kBoxes = 1;                 // 64-wide k boxes per stage
 constexpr int BK = 64 * kBoxes;           // k per stage
 constexpr int kStages = 8;
-constexpr int kMinIters = 1;              // fewest stages a CTA streams
+constexpr int kMinIters = 2;              // fewest stages a CTA streams
+constexpr int kMaxSplit = 8;              // most CTAs sharing one tile
 constexpr int kCtasPerSm = 1;
 constexpr uint32_t kWBox = BM * 64 * 2;   // 16 KB: 128 weight rows x 64 k
 constexpr uint32_t kXBox = NB * 64 * 2;   // 4 KB: 32 activation rows x 64 k
@@ -144,13 +145,36 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      long long n = 0;
+      // The weights are never written by a kernel of the step: the first ring
+      // of weight boxes is issued before waiting for the previous kernel (the
+      // producer of x), whose tail it overlaps.
+      const long long npre = min((long long)kStages, it1 - it0);
+      for (long long j = 0; j < npre; ++j) {
+        const long long it = it0 + j;
+        const int tile = (int)(it / a.kb), k = (int)(it - (long long)tile * a.kb);
+        const uint32_t dst = sbase + (uint32_t)j * kStageBytes;
+        mbar_expect_tx(bar(FULL0 + (int)j), kStageBytes);
+#pragma unroll
+        for (int b = 0; b < kBoxes; ++b)
+          tma_load_3d(dst + b * kWBox, &tm_w, bar(FULL0 + (int)j), k * BK + b * 64, 0, tile * BM);
+      }
+      pdl_wait();
+      for (long long j = 0; j < npre; ++j) {
+        const long long it = it0 + j;
+        const int k = (int)(it - (it / a.kb) * a.kb);
+        const uint32_t dst = sbase + (uint32_t)j * kStageBytes;
+#pragma unroll
+        for (int b = 0; b < kBoxes; ++b)
+          tma_load_3d(dst + kWBytes + b * kXBox, &tm_x, bar(FULL0 + (int)j), k * BK + b * 64, 0, 0);
+      }
+      long long n = npre;
       bool ok = true;
-      for (long long it = it0; it < it1; ++it, ++n) {
+      for (long long it = it0 + npre; it < it1; ++it, ++n) {
         const int s = (int)(n % kStages);
         if (n >= kStages && !(ok = wait_bar(bar(EMPTY0 + s), (uint32_t)((n / kStages) - 1) & 1, abort_flag,
                                             a.status)))
@@ -205,6 +229,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     __all_sync(0xffffffffu, mbar_wait_bounded(bar(MMA_DONE), 0));
   } else {
     // ------------------------------------------------------------ epilogue
+    pdl_wait();  // residual, outputs and the workspace belong to earlier kernels until then
     const int q = warp & 3;
     const int row = q * 32 + lane;  // weight row within the tile = TMEM lane
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
@@ -248,11 +273,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         __threadfence();
 #pragma unroll
         for (int j = 0; j < NB; ++j) v[j] = 0.0f;
-        for (int c = c0; c <= c1; ++c) {
-          const int sl = tile == it_begin(c, a) / a.kb ? 0 : 1;
-          const float* pc = a.part + ((size_t)c * 2 + sl) * NB * BM + row;
+        // contributors in order, four partial tiles in flight at a time
+        for (int c = c0; c <= c1; c += 4) {
+          float t[4][NB];
 #pragma unroll
-          for (int j = 0; j < NB; ++j) v[j] += __ldcg(pc + j * BM);
+          for (int u = 0; u < 4; ++u) {
+            if (c + u <= c1) {
+              const int sl = tile == it_begin(c + u, a) / a.kb ? 0 : 1;
+              const float* pc = a.part + ((size_t)(c + u) * 2 + sl) * NB * BM + row;
+#pragma unroll
+              for (int j = 0; j < NB; ++j) t[u][j] = __ldcg(pc + j * BM);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (c + u <= c1) {
+#pragma unroll
+              for (int j = 0; j < NB; ++j) v[j] += t[u][j];
+            }
+          }
         }
       }
 
@@ -308,6 +347,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
                                                                __nv_bfloat16* __restrict__ out, int cols,
                                                                float eps) {
   __shared__ float warp_sum[kNormThreads / 32];
+  pdl_trigger();
+  pdl_wait();
   const size_t row = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
   const int n4 = cols >> 2;
@@ -382,8 +423,11 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
   const long long iters = (long long)tiles * kb;
   int ctas = num_sms() * lin::kCtasPerSm;
   if (ctas > lin::kMaxCtas) ctas = lin::kMaxCtas;
-  const long long by_work = iters / lin::kMinIters > 0 ? iters / lin::kMinIters : 1;
-  if ((long long)ctas > by_work) ctas = (int)by_work;
+  // enough stages per CTA to cover the load latency, few CTAs per tile so the
+  // partial-tile reduction stays short
+  long long cap = iters / lin::kMinIters > 0 ? iters / lin::kMinIters : 1;
+  if (cap > (long long)tiles * lin::kMaxSplit) cap = (long long)tiles * lin::kMaxSplit;
+  if ((long long)ctas > cap) ctas = (int)cap;
   const uint64_t need = linear_workspace(n_out, k);
   if (launch->workspace == nullptr || launch->workspace_bytes < need) {
     set_op_error("doe_linear_bf16: workspace of %llu bytes required, %llu given", (unsigned long long)need,
@@ -424,16 +468,18 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
     if (rc != DOE_OK) return rc;
     attr_set = true;
   }
-  lin::linear_kernel<<<ctas, lin::kThreads, lin::kSmemBytes, static_cast<cudaStream_t>(launch->stream)>>>(
-      mw, mx, a);
-  return cuda_status(cudaGetLastError(), "linear_kernel");
+  return cuda_status(launch_pdl(lin::linear_kernel, dim3(ctas), dim3(lin::kThreads), lin::kSmemBytes,
+                                static_cast<cudaStream_t>(launch->stream), mw, mx, a),
+                     "linear_kernel");
 }
 
 int launch_rmsnorm(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
                    const doe_launch* launch) {
-  lin::rmsnorm_kernel<<<rows, lin::kNormThreads, 0, static_cast<cudaStream_t>(launch->stream)>>>(
-      x, static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(out), (int)cols, eps);
-  return cuda_status(cudaGetLastError(), "rmsnorm_kernel");
+  return cuda_status(launch_pdl(lin::rmsnorm_kernel, dim3(rows), dim3(lin::kNormThreads), 0,
+                                static_cast<cudaStream_t>(launch->stream), x,
+                                static_cast<const __nv_bfloat16*>(gamma), static_cast<__nv_bfloat16*>(out),
+                                (int)cols, eps),
+                     "rmsnorm_kernel");
 }
 
 }  // namespace doe

@@ -171,6 +171,8 @@ __global__ void __launch_bounds__(kWarps * 32)
   extern __shared__ __align__(1024) uint8_t dsmem_raw[];
   // the swizzled boxes need 1024-byte alignment
   uint8_t* dsmem = dsmem_raw + ((1024 - (smem_addr(dsmem_raw) & 1023)) & 1023);
+  pdl_wait();  // launched with launch_pdl: q, new K/V and the pools come from earlier kernels
+  pdl_trigger();
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
@@ -681,8 +683,8 @@ static int launch_one(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const Pa
     if (rc != DOE_OK) return rc;
     attr = true;
   }
-  paged_decode_kernel<INT8, GROUP><<<grid, kWarps * 32, smem, st>>>(tm_k, tm_v, a);
-  return cuda_status(cudaGetLastError(), "paged_decode_kernel");
+  return cuda_status(launch_pdl(paged_decode_kernel<INT8, GROUP>, grid, dim3(kWarps * 32), smem, st, tm_k, tm_v, a),
+                     "paged_decode_kernel");
 }
 
 int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
@@ -751,10 +753,15 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.scale = scale;
   a.out_bf16 = (opts && (opts->flags & DOE_DECODE_OUT_BF16)) ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
-  // arrival counters of the split stitch start at zero on every launch
-  int rc = cuda_status(cudaMemsetAsync(a.counters, 0, (size_t)num_seqs * Hkv * sizeof(unsigned), st),
-                       "cudaMemsetAsync(split counters)");
-  if (rc != DOE_OK) return rc;
+  // arrival counters of the split stitch start at zero on every launch; the
+  // last split of each (sequence, kv head) puts its counter back to zero, so a
+  // caller that keeps a workspace for the decode alone may skip the clear
+  int rc = DOE_OK;
+  if (!(opts && (opts->flags & DOE_DECODE_COUNTERS_ZEROED))) {
+    rc = cuda_status(cudaMemsetAsync(a.counters, 0, (size_t)num_seqs * Hkv * sizeof(unsigned), st),
+                     "cudaMemsetAsync(split counters)");
+    if (rc != DOE_OK) return rc;
+  }
   dim3 grid(max_splits, Hkv, num_seqs);
   const bool int8 = kv->kv_dtype == DOE_KV_INT8;
   // K/V pools as {128 elements, Hkv, rows} tensor maps; one box = 16 rows of

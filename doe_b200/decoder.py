@@ -176,6 +176,8 @@ class Decoder:
         n_max = max(cfg.hidden, (self.qh + 2 * self.kvh) * D, 2 * self.f)
         self.lin_ws = torch.zeros(int(ops.abi.lib().doe_linear_workspace_bytes(n_max, 64)), dtype=torch.uint8,
                                   device=dev)
+        # the decode's own workspace: its split counters stay zero between calls
+        self.dec_ws = ops.decode_workspace(self.caches[0], B, self.qh)
         self.graph = None
 
     def _all_reduce(self, t: torch.Tensor) -> None:
@@ -191,7 +193,7 @@ class Decoder:
             ops.paged_decode(cache, self.q.view(B, self.qh, D), self.seq_lens, self.scale,
                              new_k=self.k.view(B, self.kvh, D), new_v=self.v.view(B, self.kvh, D),
                              out=self.attn.view(B, self.qh, D), status=self.status, freq_cis=self.freq_cis,
-                             out_dtype=torch.bfloat16)
+                             out_dtype=torch.bfloat16, ws=self.dec_ws)
             ops.linear(self.attn, L["wo"], [self.h], residual=x if first else None, status=self.status,
                        ws=self.lin_ws)
             self._all_reduce(self.h)

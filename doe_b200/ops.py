@@ -101,7 +101,7 @@ def stitch(partials, out=None, stream=None):
 
 def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new_v=None, out=None,
                  split_pages: int = 0, status=None, stream=None, freq_cis=None, sliding_window: int = 0,
-                 softcap: float = 0.0, out_dtype=torch.float32):
+                 softcap: float = 0.0, out_dtype=torch.float32, ws=None):
     """Batched GQA decode: q [B,H,D] f16, seq_lens [B] int32 -> out [B,H,D] f32.
 
     With new_k/new_v ([B,Hkv,D] f16) the new token is first written at
@@ -110,7 +110,10 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
     rotated at position seq_lens[b] - 1 first (doe_paged_decode_rope).
     sliding_window > 0 keeps the last sliding_window keys and softcap > 0
     caps each scaled score as softcap * tanh(s / softcap) (doe_paged_decode_ex).
-    out_dtype torch.bfloat16 writes a bf16 output (DOE_DECODE_OUT_BF16)."""
+    out_dtype torch.bfloat16 writes a bf16 output (DOE_DECODE_OUT_BF16).
+    `ws`: a workspace kept for paged decodes alone, zeroed when created
+    (decode_workspace); its split counters then need no clearing per call
+    (DOE_DECODE_COUNTERS_ZEROED)."""
     _need(q, torch.float16, "q")
     _need(seq_lens, torch.int32, "seq_lens")
     if out_dtype not in (torch.float32, torch.bfloat16):
@@ -119,10 +122,18 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
     out = torch.empty((B, H, D), dtype=out_dtype, device=q.device) if out is None else out
     _need(out, out_dtype, "out")
     flags = abi.DECODE_OUT_BF16 if out_dtype == torch.bfloat16 else 0
+    if ws is not None:
+        flags |= abi.DECODE_COUNTERS_ZEROED
     kv = cache.struct()
     lib = abi.lib()
-    ws = lib.doe_paged_decode_workspace_bytes(C.byref(kv), B, H, split_pages)
-    l = _launch(ws, status, stream, q.device)
+    need = lib.doe_paged_decode_workspace_bytes(C.byref(kv), B, H, split_pages)
+    if ws is None:
+        l = _launch(need, status, stream, q.device)
+    else:
+        if ws.numel() < need:
+            raise ValueError(f"decode workspace of {need} bytes needed, {ws.numel()} given")
+        s = stream if stream is not None else torch.cuda.current_stream(q.device)
+        l = abi.Launch(s.cuda_stream, ws.data_ptr(), ws.numel(), status.data_ptr() if status is not None else None)
     nk = new_k.data_ptr() if new_k is not None else None
     nv = new_v.data_ptr() if new_v is not None else None
     if sliding_window or softcap or flags:
@@ -144,6 +155,13 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
             C.byref(kv), B, H, q.data_ptr(), seq_lens.data_ptr(), nk, nv, float(scale), out.data_ptr(),
             split_pages, freq_cis.data_ptr(), freq_cis.shape[0], C.byref(l)))
     return out
+
+
+def decode_workspace(cache: PagedKVCache, num_seqs: int, num_heads: int, split_pages: int = 0) -> torch.Tensor:
+    """A zeroed workspace for paged decodes alone (pass as paged_decode(ws=...))."""
+    kv = cache.struct()
+    need = int(abi.lib().doe_paged_decode_workspace_bytes(C.byref(kv), num_seqs, num_heads, split_pages))
+    return torch.zeros(max(need, 256), dtype=torch.uint8, device=cache.k_pool.device)
 
 
 def paged_append(cache: PagedKVCache, new_k, new_v, positions, status=None, stream=None, freq_cis=None):

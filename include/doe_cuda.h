@@ -304,8 +304,15 @@ int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs,
  *   flags                      DOE_DECODE_OUT_BF16: `out` is bf16 storage
  *                              [B, H, D] (each f32 result rounded to
  *                              nearest even), the input of a bf16 o_proj;
+ *                              DOE_DECODE_COUNTERS_ZEROED: the workspace's
+ *                              split counters are already zero (the workspace
+ *                              serves paged decodes only, the first of them
+ *                              on zeroed memory; every decode that sets no
+ *                              DOE_DEVICE_ERR_TIMEOUT leaves them zero), so
+ *                              the per-call clear is skipped;
  *                              other bits must be 0.                       */
 #define DOE_DECODE_OUT_BF16 0x1u
+#define DOE_DECODE_COUNTERS_ZEROED 0x2u
 typedef struct doe_decode_options {
   const float* freq_cis;
   uint32_t rope_positions;
