@@ -320,13 +320,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const size_t width = (size_t)((sg == 0 ? a.seg_end[0] : (sg == 1 ? a.seg_end[1] : a.seg_end[2])) - base);
         void* dst = sg == 0 ? a.out[0] : (sg == 1 ? a.out[1] : a.out[2]);
         const int col = col0 + row;
+        if (a.residual) {
+          // all residual loads before any store: each (row, column) is read and
+          // written by this thread alone, so an in-place residual (out[0] ==
+          // residual) stays correct while the loads overlap
+          float r[NB];
 #pragma unroll
-        for (int j = 0; j < NB; ++j) {
-          if (j < a.batch) {
-            float y = v[j];
-            if (a.residual) y += a.residual[(size_t)j * a.n_out + col];
-            store_elem(dst, a.dtype, j * width + (col - base), y);
-          }
+          for (int j = 0; j < NB; ++j) r[j] = j < a.batch ? a.residual[(size_t)j * a.n_out + col] : 0.0f;
+#pragma unroll
+          for (int j = 0; j < NB; ++j)
+            if (j < a.batch) static_cast<float*>(dst)[j * width + (col - base)] = v[j] + r[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < NB; ++j)
+            if (j < a.batch) store_elem(dst, a.dtype, j * width + (col - base), v[j]);
         }
       }
     }
@@ -404,18 +411,27 @@ int num_sms() {
   return cached[dev];
 }
 
-uint64_t counters_bytes(uint32_t n_out) { return ((uint64_t)(n_out / lin::BM) * 4 + 255) / 256 * 256; }
+// Workspace layout, the same for every shape so that calls of different
+// sizes can share one workspace: tile counters at the front (room for
+// kMaxTiles tiles), partial tiles from kCountersBytes on.
+constexpr uint64_t kMaxTiles = 16384;
+constexpr uint64_t kCountersBytes = kMaxTiles * 4;
 
 }  // namespace
 
 uint64_t linear_workspace(uint32_t n_out, uint32_t k) {
+  (void)n_out;
   (void)k;
-  return counters_bytes(n_out) + (uint64_t)lin::kMaxCtas * 2 * lin::NB * lin::BM * sizeof(float);
+  return kCountersBytes + (uint64_t)lin::kMaxCtas * 2 * lin::NB * lin::BM * sizeof(float);
 }
 
 int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
                   const doe_linear_out* o, const doe_launch* launch) {
   const uint32_t tiles = n_out / lin::BM, kb = k / lin::BK;
+  if (tiles > kMaxTiles) {
+    set_op_error("doe_linear_bf16: n_out %u exceeds %llu rows", n_out, (unsigned long long)(kMaxTiles * lin::BM));
+    return DOE_UNSUPPORTED;
+  }
   if (k % lin::BK != 0) {
     set_op_error("doe_linear_bf16: k %u must be a multiple of %d", k, lin::BK);
     return DOE_UNSUPPORTED;
@@ -443,7 +459,7 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
   }
   a.residual = o->residual;
   a.counters = static_cast<unsigned*>(launch->workspace);
-  a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(launch->workspace) + counters_bytes(n_out));
+  a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(launch->workspace) + kCountersBytes);
   a.status = launch->status;
   a.batch = (int)batch;
   a.n_out = (int)n_out;

@@ -184,24 +184,37 @@ class Decoder:
         if self.world > 1:
             torch.distributed.all_reduce(t, group=self.group)
 
-    def step(self, x: torch.Tensor) -> torch.Tensor:
+    def step(self, x: torch.Tensor, trace=None) -> torch.Tensor:
+        """One decode token per sequence through every layer; x updated in place.
+
+        trace(layer, name, tensor), when given, sees each intermediate right
+        after the op that writes it (for stage-by-stage checks; not in graphs)."""
         cfg, B, D = self.cfg, self.cfg.batch, self.cfg.head_dim
         first = self.rank == 0
-        for L, cache in zip(self.layers, self.caches):
+        t = trace if trace is not None else (lambda *_: None)
+        for li, (L, cache) in enumerate(zip(self.layers, self.caches)):
+            t(li, "x", x)
             ops.rmsnorm(x, L["g1"], cfg.eps, out=self.xn, status=self.status)
+            t(li, "xn", self.xn)
             ops.linear(self.xn, L["wqkv"], [self.q, self.k, self.v], status=self.status, ws=self.lin_ws)
+            t(li, "q", self.q), t(li, "k", self.k), t(li, "v", self.v)
             ops.paged_decode(cache, self.q.view(B, self.qh, D), self.seq_lens, self.scale,
                              new_k=self.k.view(B, self.kvh, D), new_v=self.v.view(B, self.kvh, D),
                              out=self.attn.view(B, self.qh, D), status=self.status, freq_cis=self.freq_cis,
                              out_dtype=torch.bfloat16, ws=self.dec_ws)
+            t(li, "attn", self.attn)
             ops.linear(self.attn, L["wo"], [self.h], residual=x if first else None, status=self.status,
                        ws=self.lin_ws)
             self._all_reduce(self.h)
+            t(li, "h", self.h)
             ops.rmsnorm(self.h, L["g2"], cfg.eps, out=self.xn, status=self.status)
+            t(li, "hn", self.xn)
             ops.linear(self.xn, L["wgu"], [self.act], swiglu=True, status=self.status, ws=self.lin_ws)
+            t(li, "act", self.act)
             ops.linear(self.act, L["wd"], [x], residual=self.h if first else None, status=self.status,
                        ws=self.lin_ws)
             self._all_reduce(x)
+            t(li, "out", x)
         return x
 
     def launches_per_step(self) -> int:

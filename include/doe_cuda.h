@@ -390,11 +390,13 @@ int doe_rmsnorm_bf16(const float* x, const void* gamma, float eps, void* out,
  *   DOE_LINEAR_SWIGLU  w rows come in 128-row blocks of 64 gate rows then the
  *                      64 matching up rows; out[0] [batch, n_out / 2] =
  *                      silu(gate) * up in `dtype` (silu(g) = g / (1 + e^-g)).
- * Workspace: at least doe_linear_workspace_bytes(n_out, k) bytes.  It starts
- * with per-tile arrival counters that must be zero before the first call on
- * that workspace; every call that sets no DOE_DEVICE_ERR_TIMEOUT leaves them
- * zero again, so one zeroed workspace serves any number of calls that run
- * one after another on a stream.                                           */
+ * n_out at most 2^21.
+ * Workspace: at least doe_linear_workspace_bytes(n_out, k) bytes (the same
+ * for every shape).  It starts with per-tile arrival counters that must be
+ * zero before the first call on that workspace; every call that sets no
+ * DOE_DEVICE_ERR_TIMEOUT leaves them zero again, so one zeroed workspace
+ * serves any number of calls, of any shapes, that run one after another on
+ * a stream.                                                                */
 #define DOE_LINEAR_STORE 0u
 #define DOE_LINEAR_SWIGLU 1u
 #define DOE_DTYPE_BF16 0u

@@ -1,10 +1,21 @@
 """GPU parity of the decoder step (doe_b200.decoder, BASELINE config 5 semantics)
-against the numpy restatement oracle/decoder.py on a small model.
+against the numpy restatement oracle/decoder.py.
 
-Tolerance: the f32 residual stream after all layers within
-2e-3 * max(|ref|, 1) (the fp16/bf16 bound); the kernels and the oracle round
-at the same points, so what remains is summation order and the odd bf16 / f16
-rounding flip that it causes.
+Two checks:
+  - stage by stage, at config 5's full layer shapes too: each op of the real
+    Decoder.step (seen through its trace hook) against the oracle fed the
+    GPU's own inputs to that op.  Rounded stages (RMSNorm, SwiGLU to bf16;
+    q/k/v to f16) within one unit in the last place of the stored type
+    (2^-7 |ref| for bf16, 2^-10 |ref| for f16, the widest ulp of a binade;
+    GEMM-fed stages also 2e-5 * max(|ref|, 1) of f32 accumulation noise);
+    attention within its own 2e-3 * max(|ref|, 1) plus one bf16 ulp; f32
+    stages (o_proj and down_proj with their residual adds) within
+    1e-4 * max(|ref|, 1).
+  - end to end on small models: the f32 residual stream after all layers
+    within 2e-3 * max(|ref|, 1).  At full size two bf16 pipelines that each
+    round correctly drift further apart than that (a one-ulp difference in
+    an activation moves a 14336-term down_proj sum), which is why the full
+    shapes are held to the per-stage bound instead.
 """
 from __future__ import annotations
 
@@ -58,6 +69,78 @@ def test_decoder_step_matches_oracle(cfg):
     got = x.cpu().numpy()
     err = np.abs(got - ref) / np.maximum(np.abs(ref), 1.0)
     assert float(err.max()) <= TOL, f"max rel err {float(err.max()):.3g}"
+
+
+BF16_ULP, F16_ULP = 2.0 ** -7, 2.0 ** -10
+# f32 accumulation error of a several-thousand-term GEMM row, as a share of
+# max(|ref|, 1): results near zero are sums that cancel, whose last bits are
+# noise below any f16 / bf16 ulp at unit scale
+ACC = 2e-5
+
+
+def _ulp_close(got, ref, rel, what, extra=1e-6):
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    bad = np.abs(got - ref) > rel * np.abs(ref) + extra * np.maximum(np.abs(ref), 1.0)
+    assert not bad.any(), f"{what}: {int(bad.sum())} of {bad.size} beyond one ulp; max err " \
+                          f"{float(np.abs(got - ref).max()):.3g}"
+
+
+def _f32_close(got, ref, what, tol=1e-4):
+    err = np.abs(np.asarray(got, np.float64) - ref) / np.maximum(np.abs(ref), 1.0)
+    assert float(err.max()) <= tol, f"{what}: max rel err {float(err.max()):.3g}"
+
+
+@pytest.mark.parametrize("cfg", [SMALL, decoder.DecoderConfig(layers=2, ctx=64)])
+def test_decoder_stages_match_oracle(cfg):
+    import oracle
+
+    dec = decoder.Decoder(cfg, seed=6)
+    layers, caches = _host_state(dec)
+    seen: dict = {}
+
+    def keep(li, name, t):
+        seen[(li, name)] = t.float().cpu().numpy().copy()
+
+    x = torch.from_numpy(_x0(cfg, 7)).cuda()
+    dec.step(x, trace=keep)
+    torch.cuda.synchronize()
+    assert int(dec.status.item()) == 0
+    B, D, qh, kvh = cfg.batch, cfg.head_dim, dec.qh, dec.kvh
+    freq = dec.freq_cis.cpu().numpy()
+    seq_lens = dec.seq_lens.cpu().numpy()
+    pos = seq_lens.astype(np.int64) - 1
+    for li, (L, c) in enumerate(zip(layers, caches)):
+        g = lambda n: seen[(li, n)]  # noqa: E731
+        _ulp_close(g("xn"), odec.rmsnorm(g("x"), L["g1"], cfg.eps), BF16_ULP, f"layer {li} rmsnorm")
+        qkv = odec.matmul(g("xn"), L["wqkv"])
+        for name, lo, hi in (("q", 0, qh * D), ("k", qh * D, (qh + kvh) * D), ("v", (qh + kvh) * D, None)):
+            _ulp_close(g(name), qkv[:, lo:hi].astype(np.float16), F16_ULP, f"layer {li} {name}", extra=ACC)
+        q16 = g("q").astype(np.float16).reshape(B, qh, D)
+        k16 = g("k").astype(np.float16).reshape(B, kvh, D)
+        v16 = g("v").astype(np.float16).reshape(B, kvh, D)
+        rq = np.stack([oracle.rope(q16[b][None].astype(np.float32), freq, position_offset=int(pos[b]))[0]
+                       for b in range(B)]).astype(np.float16)
+        rk = np.stack([oracle.rope(k16[b][None].astype(np.float32), freq, position_offset=int(pos[b]))[0]
+                       for b in range(B)]).astype(np.float16)
+        oracle.paged_append(rk[:, None].view(np.uint16), v16[:, None].view(np.uint16), c["k"], c["v"], c["table"],
+                            pos.astype(np.int32), page_size=c["page_size"])
+        att = oracle.paged_decode(rq.view(np.uint16), c["k"], c["v"], c["table"], seq_lens, dec.scale,
+                                  page_size=c["page_size"])
+        # the attention's own bound (2e-3 * max(|ref|, 1): P is rounded to f16 for
+        # the tensor-core PV) plus the bf16 rounding of its output
+        _ulp_close(g("attn"), odec.bf16_round(att.reshape(B, -1).astype(np.float32)), BF16_ULP,
+                   f"layer {li} attention", extra=2e-3)
+        _f32_close(g("h"), odec.matmul(g("attn"), L["wo"]).astype(np.float64) + g("x"), f"layer {li} o_proj")
+        _ulp_close(g("hn"), odec.rmsnorm(g("h"), L["g2"], cfg.eps), BF16_ULP, f"layer {li} rmsnorm 2")
+        wg, wu = odec.unpack_gate_up(L["wgu"])
+        gg, uu = odec.matmul(g("hn"), wg), odec.matmul(g("hn"), wu)
+        _ulp_close(g("act"), (gg / (np.float32(1.0) + np.exp(-gg)) * uu).astype(np.float32), BF16_ULP,
+                   f"layer {li} swiglu", extra=ACC)
+        _f32_close(g("out"), odec.matmul(g("act"), L["wd"]).astype(np.float64) + g("h"), f"layer {li} down_proj")
+    # the caches hold the same appended rows as the oracle's
+    for c_dev, c in zip(dec.caches, caches):
+        assert np.array_equal(c_dev.k_pool.cpu().numpy().view(np.uint16), c["k"])
+        assert np.array_equal(c_dev.v_pool.cpu().numpy().view(np.uint16), c["v"])
 
 
 def test_decoder_graph_replay_equals_eager_step():

@@ -94,6 +94,24 @@ def test_linear_residual_in_place_and_repeatable():
     assert torch.equal(a, b)
     ws = ops.linear_workspace(n_out, k)
     assert int(ws[: 4 * (n_out // 128)].sum().item()) == 0, "tile counters not left at zero"
+    # one workspace, any shape: every call asks for the same size
+    assert ops.abi.lib().doe_linear_workspace_bytes(128, 64) == ops.abi.lib().doe_linear_workspace_bytes(28672, 14336)
+
+
+def test_linear_calls_of_different_shapes_share_one_workspace():
+    # the decoder runs q|k|v, o_proj, gate|up and down_proj on one workspace:
+    # a large call's tile counters must survive the partial tiles of the others
+    g = np.random.default_rng(21)
+    shapes = [(6144, 512), (4096, 1024), (28672, 256), (4096, 3584), (28672, 256)]
+    ws = ops.linear_workspace(28672, 64)
+    x = {k: _bf16(g, (32, k), 1.0) for _, k in shapes}
+    for rep in range(2):
+        for n, k in shapes:
+            w = _bf16(np.random.default_rng(n + k), (n, k), 0.02)
+            out = torch.full((32, n), float("nan"), dtype=torch.float32, device="cuda")
+            ops.linear(x[k].cuda(), w.cuda(), [out], ws=ws)
+            _close(out, _ref(x[k], w), torch.float32)
+    assert int(ws[: 4 * 224].sum().item()) == 0
 
 
 def test_linear_rejects_bad_shapes():
