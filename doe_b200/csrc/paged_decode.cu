@@ -701,11 +701,24 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
     split_tiles = split_pages * tiles_per_page;
   } else {
     // Long splits amortise each CTA's pipeline fill and stitch (64 tiles for
-    // f16, 128 for int8 measured best on config 3 / 4), but a small batch
-    // still needs about four waves of 3 CTAs per SM on 148 SMs.
-    const uint64_t want = ((uint64_t)max_tiles * num_seqs * Hkv + 1775) / 1776;
+    // f16, 128 for int8 measured best on config 3 / 4, whose work fills
+    // several waves of 3 CTAs per SM on 148 SMs at that length).  Less work
+    // than that (a decode batch of uniform contexts, or one tensor-parallel
+    // rank's few KV heads) runs best with as few splits as still keep about
+    // two CTAs per SM busy, each at most 128 tiles and all of one length.
+    const uint64_t seq_rows = (uint64_t)num_seqs * Hkv;
+    const uint64_t want = ((uint64_t)max_tiles * seq_rows + 1775) / 1776;
     const uint32_t cap = kv->kv_dtype == DOE_KV_INT8 ? 128u : 64u;
-    split_tiles = (uint32_t)(want < 4 ? 4 : (want > cap ? cap : want));
+    if (want >= cap) {
+      split_tiles = cap;
+    } else {
+      uint64_t s = (max_tiles + 127) / 128;
+      const uint64_t fill = (280 + seq_rows - 1) / seq_rows;
+      if (s < fill) s = fill;
+      if (s < 1) s = 1;
+      const uint64_t t = (max_tiles + s - 1) / s;
+      split_tiles = (uint32_t)(t < 4 ? 4 : t);
+    }
   }
   if (split_tiles == 0) split_tiles = 1;
   if (split_tiles > 4 * 32) split_tiles = 4 * 32;  // 4 warps x 32 prefetched page ids
