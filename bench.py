@@ -354,6 +354,9 @@ def measure_decoder(steps, warmup, world, rank, pk):
     torch.cuda.synchronize()
     x.copy_(x0)
     dec.capture(x)
+    launches = dec.launches_per_step()
+    reduction = ("reduction fused into the RMSNorm over peer buffers (doe_tp_reduce_rmsnorm)"
+                 if dec.peers is not None else "NCCL all-reduce")
     try:
         total, each = time_steps(dec.replay, steps, warmup, world)
         total = max_over_ranks(world, [total])[0]
@@ -366,12 +369,12 @@ def measure_decoder(steps, warmup, world, rank, pk):
     rank_bytes = job_bytes / world
     return {"config": "config 5: 4-layer Llama-style decoder, hidden 4096, 32/8 heads, FFN 14336 SwiGLU, "
                       "bf16 weights N(0,0.02) seed 4, batch 32 at ctx 4096, f16 paged KV",
-            "parallelism": f"tp{world} by KV head (NCCL all-reduce after o_proj and down_proj)"
+            "parallelism": f"tp{world} by KV head, {reduction} after o_proj and down_proj"
                            if world > 1 else "tp1",
             "scaling": "strong", "ms_per_step": ms, "tokens_per_s": cfg.batch / (ms / 1e3),
             "bytes_per_step": job_bytes, "gbs": job_bytes / (ms / 1e3) / 1e9,
             "per_gpu_frac": rank_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
-            "gpu_launches_per_step": dec.launches_per_step(), "graph": "one CUDA graph per step",
+            "gpu_launches_per_step": launches, "graph": "one CUDA graph per step",
             "status": status, "output_finite": finite}
 
 

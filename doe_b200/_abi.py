@@ -86,6 +86,15 @@ LINEAR_STORE, LINEAR_SWIGLU = 0, 1
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 
 
+TP_MAX_RANKS = 8
+
+
+class TpPeers(C.Structure):
+    """doe_tp_peers: this rank, the world size and every rank's peer buffer mapped here."""
+
+    _fields_ = [("rank", C.c_uint32), ("world", C.c_uint32), ("buffers", C.c_void_p * TP_MAX_RANKS)]
+
+
 class LinearOut(C.Structure):
     """doe_linear_out: output segments, dtype and epilogue of doe_linear_bf16."""
 
@@ -145,6 +154,13 @@ SIGNATURES = {
     "doe_rmsnorm_bf16": (_I, [_P, _P, _F, _P, _U32, _U32, _LP]),
     "doe_linear_workspace_bytes": (_U64, [_U32, _U32]),
     "doe_linear_bf16": (_I, [_P, _P, _U32, _U32, _U32, C.POINTER(LinearOut), _LP]),
+    "doe_tp_buffer_bytes": (_U64, [_U32, _U32]),
+    "doe_tp_slot_ptr": (_P, [_P, _U32, _U32, _U32]),
+    "doe_peer_buffer_create": (_I, [_U64, C.POINTER(_P), _P]),
+    "doe_peer_buffer_open": (_I, [_P, C.POINTER(_P)]),
+    "doe_peer_buffer_close": (_I, [_P]),
+    "doe_peer_buffer_free": (_I, [_P]),
+    "doe_tp_reduce_rmsnorm": (_I, [C.POINTER(TpPeers), _U32, _P, _F, _P, _P, _U32, _U32, _LP]),
     "doe_attention_decode_f32_noalloc": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _F, _P]),
     "doe_kv_pool_create": (_I, [_U32, _U32, _U32, _U32, C.POINTER(_P)]),
     "doe_kv_pool_destroy": (_I, [_P]),

@@ -85,6 +85,10 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
                   const doe_linear_out* out, const doe_launch* launch);
 int launch_rmsnorm(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
                    const doe_launch* launch);
+uint64_t tp_buffer_bytes(uint32_t rows, uint32_t cols);
+float* tp_slot_ptr(void* buffer, uint32_t slot, uint32_t rows, uint32_t cols);
+int launch_tp_reduce_rmsnorm(const doe_tp_peers* p, uint32_t slot, const void* gamma, float eps, float* h_out,
+                             void* xn_out, uint32_t rows, uint32_t cols, const doe_launch* launch);
 int launch_rope(float* qk, const float* freq_cis, uint32_t seq_len, uint32_t num_heads,
                 uint32_t head_dim, uint32_t position_offset, const doe_launch* launch);
 

@@ -368,6 +368,68 @@ int doe_rmsnorm_bf16(const float* x, const void* gamma, float eps, void* out, ui
 
 uint64_t doe_linear_workspace_bytes(uint32_t n_out, uint32_t k) { return linear_workspace(n_out, k); }
 
+uint64_t doe_tp_buffer_bytes(uint32_t rows, uint32_t cols) { return tp_buffer_bytes(rows, cols); }
+
+float* doe_tp_slot_ptr(void* buffer, uint32_t slot, uint32_t rows, uint32_t cols) {
+  return buffer ? tp_slot_ptr(buffer, slot, rows, cols) : nullptr;
+}
+
+int doe_peer_buffer_create(uint64_t bytes, void** dev_ptr, void* ipc_handle_out) {
+  if (!dev_ptr || !ipc_handle_out || bytes == 0) return invalid("doe_peer_buffer_create: bad arguments");
+  void* p = nullptr;
+  int rc = cuda_status(cudaMalloc(&p, bytes), "cudaMalloc(peer buffer)");
+  if (rc != DOE_OK) return rc;
+  rc = cuda_status(cudaMemset(p, 0, bytes), "cudaMemset(peer buffer)");
+  cudaIpcMemHandle_t h;
+  if (rc == DOE_OK) rc = cuda_status(cudaIpcGetMemHandle(&h, p), "cudaIpcGetMemHandle");
+  if (rc != DOE_OK) {
+    cudaFree(p);
+    return rc;
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handles are 64 bytes");
+  std::memcpy(ipc_handle_out, &h, sizeof(h));
+  *dev_ptr = p;
+  return DOE_OK;
+}
+
+int doe_peer_buffer_open(const void* ipc_handle, void** dev_ptr) {
+  if (!ipc_handle || !dev_ptr) return invalid("doe_peer_buffer_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int doe_peer_buffer_close(void* dev_ptr) {
+  if (!dev_ptr) return DOE_OK;
+  return cuda_status(cudaIpcCloseMemHandle(dev_ptr), "cudaIpcCloseMemHandle");
+}
+
+int doe_peer_buffer_free(void* dev_ptr) {
+  if (!dev_ptr) return DOE_OK;
+  return cuda_status(cudaFree(dev_ptr), "cudaFree(peer buffer)");
+}
+
+int doe_tp_reduce_rmsnorm(const doe_tp_peers* peers, uint32_t slot, const void* gamma, float eps, float* h_out,
+                          void* xn_out, uint32_t rows, uint32_t cols, const doe_launch* launch) {
+  const char* who = "doe_tp_reduce_rmsnorm";
+  if (!peers || !h_out) return invalid("%s: peers and h_out are required", who);
+  if (peers->world == 0 || peers->world > DOE_TP_MAX_RANKS || peers->rank >= peers->world)
+    return invalid("%s: rank %u of world %u", who, peers->rank, peers->world);
+  for (uint32_t i = 0; i < peers->world; ++i)
+    if (!peers->buffers[i] || reinterpret_cast<uintptr_t>(peers->buffers[i]) % 256)
+      return invalid("%s: buffer %u is null or not 256-byte aligned", who, i);
+  if (slot > 1) return invalid("%s: slot must be 0 or 1", who);
+  if (cols == 0 || cols % 4) return invalid("%s: cols must be a positive multiple of 4", who);
+  if (gamma && !xn_out) return invalid("%s: gamma needs xn_out", who);
+  if (reinterpret_cast<uintptr_t>(h_out) % 16 || (gamma && (reinterpret_cast<uintptr_t>(gamma) % 8 ||
+                                                            reinterpret_cast<uintptr_t>(xn_out) % 8)))
+    return invalid("%s: h_out must be 16-byte aligned, gamma and xn_out 8-byte aligned", who);
+  if (!(eps >= 0.0f)) return invalid("%s: eps must be >= 0", who);
+  if (rows == 0) return DOE_OK;
+  if (rows > 2147483647u) return invalid("%s: too many rows", who);
+  return launch_tp_reduce_rmsnorm(peers, slot, gamma, eps, h_out, xn_out, rows, cols, launch_or_default(launch));
+}
+
 int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
                     const doe_linear_out* out, const doe_launch* launch) {
   const char* who = "doe_linear_bf16";

@@ -11,11 +11,12 @@ operators") and the tensor-parallel AllReduce to NCCL:
                                         doe_paged_decode_ex (RoPE of q and the new
                                         K row, fused append, bf16 output)
     MatMul o_proj + Add residual        doe_linear_bf16, f32 out (+ residual on rank 0)
-    AllReduce                           NCCL (torch.distributed), world > 1
-    SimplifiedLayerNormalization       doe_rmsnorm_bf16
+    AllReduce + SimplifiedLayerNorm     world > 1: doe_tp_reduce_rmsnorm (the partial products
+                                        summed over peer buffers inside the norm); or NCCL
+                                        (torch.distributed) + doe_rmsnorm_bf16
     MatMul gate|up + Sigmoid/Mul        doe_linear_bf16, SwiGLU epilogue
     MatMul down_proj + Add residual     doe_linear_bf16, f32 out (+ residual on rank 0)
-    AllReduce                           NCCL, world > 1
+    AllReduce (+ next layer's norm)     as after o_proj
 
 Precision: weights and GEMM inputs bf16 with f32 accumulation; the residual
 stream f32; q/k/v and the KV cache f16 (every bf16-derived value is exact or
@@ -137,8 +138,14 @@ class Decoder:
     capture() records the step in a CUDA graph; replay() reruns it."""
 
     def __init__(self, cfg: DecoderConfig, *, seed: int = 4, rank: int = 0, world: int = 1, group=None,
-                 device=None, layers: list[dict] | None = None, caches: list[PagedKVCache] | None = None):
+                 device=None, layers: list[dict] | None = None, caches: list[PagedKVCache] | None = None,
+                 reduce: str = "fused"):
+        """reduce (world > 1): "fused" sums the partial products over peer
+        buffers inside the following RMSNorm (doe_tp_reduce_rmsnorm); "nccl"
+        all-reduces them with NCCL and normalises separately."""
         cfg.check(world)
+        if reduce not in ("fused", "nccl"):
+            raise ValueError("reduce must be 'fused' or 'nccl'")
         self.cfg, self.rank, self.world, self.group = cfg, rank, world, group
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.device = dev
@@ -178,6 +185,10 @@ class Decoder:
                                   device=dev)
         # the decode's own workspace: its split counters stay zero between calls
         self.dec_ws = ops.decode_workspace(self.caches[0], B, self.qh)
+        self.peers = None
+        if world > 1 and reduce == "fused":
+            from .tp import TpPeers
+            self.peers = TpPeers(B, cfg.hidden, group=group, device=dev)
         self.graph = None
 
     def _all_reduce(self, t: torch.Tensor) -> None:
@@ -191,10 +202,13 @@ class Decoder:
         after the op that writes it (for stage-by-stage checks; not in graphs)."""
         cfg, B, D = self.cfg, self.cfg.batch, self.cfg.head_dim
         first = self.rank == 0
+        fused = self.peers is not None
         t = trace if trace is not None else (lambda *_: None)
         for li, (L, cache) in enumerate(zip(self.layers, self.caches)):
             t(li, "x", x)
-            ops.rmsnorm(x, L["g1"], cfg.eps, out=self.xn, status=self.status)
+            if li == 0 or not fused:
+                ops.rmsnorm(x, L["g1"], cfg.eps, out=self.xn, status=self.status)
+            # (fused: the previous layer's reduction already wrote x and its norm)
             t(li, "xn", self.xn)
             ops.linear(self.xn, L["wqkv"], [self.q, self.k, self.v], status=self.status, ws=self.lin_ws)
             t(li, "q", self.q), t(li, "k", self.k), t(li, "v", self.v)
@@ -203,23 +217,37 @@ class Decoder:
                              out=self.attn.view(B, self.qh, D), status=self.status, freq_cis=self.freq_cis,
                              out_dtype=torch.bfloat16, ws=self.dec_ws)
             t(li, "attn", self.attn)
-            ops.linear(self.attn, L["wo"], [self.h], residual=x if first else None, status=self.status,
-                       ws=self.lin_ws)
-            self._all_reduce(self.h)
+            if fused:
+                # partial o_proj into slot 0 of this rank's peer buffer, then the
+                # sum over ranks and the second norm in one launch
+                ops.linear(self.attn, L["wo"], [self.peers.slots[0]], residual=x if first else None,
+                           status=self.status, ws=self.lin_ws)
+                self.peers.reduce_rmsnorm(0, self.h, L["g2"], cfg.eps, self.xn, status=self.status)
+            else:
+                ops.linear(self.attn, L["wo"], [self.h], residual=x if first else None, status=self.status,
+                           ws=self.lin_ws)
+                self._all_reduce(self.h)
+                ops.rmsnorm(self.h, L["g2"], cfg.eps, out=self.xn, status=self.status)
             t(li, "h", self.h)
-            ops.rmsnorm(self.h, L["g2"], cfg.eps, out=self.xn, status=self.status)
             t(li, "hn", self.xn)
             ops.linear(self.xn, L["wgu"], [self.act], swiglu=True, status=self.status, ws=self.lin_ws)
             t(li, "act", self.act)
-            ops.linear(self.act, L["wd"], [x], residual=self.h if first else None, status=self.status,
-                       ws=self.lin_ws)
-            self._all_reduce(x)
+            if fused:
+                nxt = self.layers[li + 1] if li + 1 < len(self.layers) else None
+                ops.linear(self.act, L["wd"], [self.peers.slots[1]], residual=self.h if first else None,
+                           status=self.status, ws=self.lin_ws)
+                self.peers.reduce_rmsnorm(1, x, nxt["g1"] if nxt else None, cfg.eps,
+                                          self.xn if nxt else None, status=self.status)
+            else:
+                ops.linear(self.act, L["wd"], [x], residual=self.h if first else None, status=self.status,
+                           ws=self.lin_ws)
+                self._all_reduce(x)
             t(li, "out", x)
         return x
 
     def launches_per_step(self) -> int:
-        """Kernels of this library per step (the decode's counter memset not counted)."""
-        return 7 * self.cfg.layers
+        """Kernels of this library per step."""
+        return 7 * self.cfg.layers + (1 if self.peers is not None else 0)
 
     def capture(self, x: torch.Tensor) -> None:
         """Record step(x) (x's storage fixed) in a CUDA graph; call after an eager warm-up step."""
@@ -236,5 +264,11 @@ class Decoder:
         self.graph.replay()
 
     def release(self) -> None:
-        """Drop the CUDA graph (before the process group is destroyed when it holds NCCL calls)."""
+        """Drop the CUDA graph (before the process group is destroyed when it
+        holds NCCL calls) and, after every rank is idle, the peer buffers."""
         self.graph = None
+        if self.peers is not None:
+            torch.cuda.synchronize(self.device)
+            torch.distributed.barrier(group=self.group)
+            self.peers.close()
+            self.peers = None

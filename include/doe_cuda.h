@@ -413,6 +413,43 @@ uint64_t doe_linear_workspace_bytes(uint32_t n_out, uint32_t k);
 int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out,
                     uint32_t k, const doe_linear_out* out, const doe_launch* launch);
 
+/* Tensor-parallel reduction fused into the RMSNorm that consumes it (the
+ * AllReduce after o_proj / down_proj, one process per GPU of one node).
+ * Every rank owns one peer buffer of doe_tp_buffer_bytes(rows, cols) bytes,
+ * created by doe_peer_buffer_create and mapped into the other ranks by
+ * doe_peer_buffer_open on the exported IPC handle (64 bytes).  Layout:
+ * 8 u64 arrival flags (written by the peers), this rank's epoch and exit
+ * counters, then 2 slots of [rows, cols] f32 partial sums.  A linear layer
+ * writes its partial product into slot s of its own buffer
+ * (doe_tp_slot_ptr); doe_tp_reduce_rmsnorm then, on every rank:
+ *   - tells every peer that its slot is complete (a system-scope release
+ *     store of the call's epoch into the peer's flag for this rank);
+ *   - waits (bounded; DOE_DEVICE_ERR_TIMEOUT on expiry) for every peer's flag;
+ *   - sums the world partials of slot s row by row in rank order over
+ *     NVLink, so every rank gets bit-identical sums, writes them to h_out
+ *     [rows, cols] f32, and, with gamma, writes
+ *     xn_out = bf16(h * (1 / sqrt(mean(h^2) + eps)) * gamma) like
+ *     doe_rmsnorm_bf16.
+ * All ranks make the same sequence of calls.  Two slots suffice when the
+ * calls alternate them: a rank overwrites slot s only after a later reduce
+ * saw every peer's flag, which peers raise after reading slot s.  Buffers
+ * start zeroed; cols a multiple of 4; world <= 8.                          */
+#define DOE_TP_MAX_RANKS 8
+typedef struct doe_tp_peers {
+  uint32_t rank;
+  uint32_t world;
+  void* buffers[DOE_TP_MAX_RANKS]; /* every rank's buffer, mapped here; [rank] = own */
+} doe_tp_peers;
+uint64_t doe_tp_buffer_bytes(uint32_t rows, uint32_t cols);
+float* doe_tp_slot_ptr(void* buffer, uint32_t slot, uint32_t rows, uint32_t cols);
+int doe_peer_buffer_create(uint64_t bytes, void** dev_ptr, void* ipc_handle_out);
+int doe_peer_buffer_open(const void* ipc_handle, void** dev_ptr);
+int doe_peer_buffer_close(void* dev_ptr);
+int doe_peer_buffer_free(void* dev_ptr);
+int doe_tp_reduce_rmsnorm(const doe_tp_peers* peers, uint32_t slot, const void* gamma,
+                          float eps, float* h_out, void* xn_out, uint32_t rows,
+                          uint32_t cols, const doe_launch* launch);
+
 /* ======================================================================== */
 /* Allocation-free f32 decode.  This entry point has no counterpart in the   */
 /* reference; it exists for callers that cannot allocate device memory.      */
