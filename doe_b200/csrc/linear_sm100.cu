@@ -54,12 +54,17 @@ constexpr uint32_t kTmemCols = 2 * NB;
 constexpr int kMaxCtas = 512;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
+constexpr int kMaxCluster = 4;            // CTAs of one tile in cluster mode
 enum Bar { FULL0 = 0, EMPTY0 = FULL0 + kStages, ACC_FULL0 = EMPTY0 + kStages, ACC_EMPTY0 = ACC_FULL0 + 2,
-           MMA_DONE = ACC_EMPTY0 + 2, NUM_BARS };
+           MMA_DONE = ACC_EMPTY0 + 2, RECV_FULL = MMA_DONE + 1, NUM_BARS };
 constexpr uint32_t OFF_BAR = kStages * kStageBytes;
 constexpr uint32_t OFF_MISC = OFF_BAR + 8 * NUM_BARS;  // TMEM slot, abort flag, last-arrival flag
 constexpr uint32_t OFF_XCHG = OFF_BAR + 512;            // SwiGLU up values [NB][64] f32
-constexpr uint32_t kSmemBytes = OFF_XCHG + NB * 64 * 4 + 1024;  // + alignment slack
+constexpr uint32_t kTileBytes = BM * NB * 4;            // one f32 accumulator tile (16 KB)
+// cluster mode: the other CTAs' accumulator tiles, row r's 32 values in one
+// 128-byte line with 16-byte chunk c at c ^ (r & 7)
+constexpr uint32_t OFF_RECV = ((OFF_XCHG + NB * 64 * 4 + 1023) / 1024) * 1024;
+constexpr uint32_t kSmemBytes = OFF_RECV + (kMaxCluster - 1) * kTileBytes + 1024;  // + alignment slack
 
 struct Args {
   void* out[3];
@@ -70,6 +75,7 @@ struct Args {
   int32_t* status;
   int batch, n_out, kb, tiles, ctas, epilogue, dtype;
   long long iters;         // tiles * kb
+  int cluster;             // > 1: cluster mode, this many CTAs per tile; else stream-K
 };
 
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -100,6 +106,38 @@ __device__ __forceinline__ bool epi_all(bool ok) {
 }
 
 __device__ __forceinline__ long long it_begin(long long c, const Args& a) { return c * a.iters / a.ctas; }
+
+// This CTA's (tile, k block) iterations [it0, it1): in cluster mode rank r of
+// the tile's cluster takes the r-th of a.cluster even k ranges; otherwise the
+// stream-K share.
+__device__ __forceinline__ void cta_range(const Args& a, long long& it0, long long& it1) {
+  if (a.cluster > 1) {
+    const long long tile = blockIdx.x / a.cluster, r = blockIdx.x % a.cluster;
+    it0 = tile * a.kb + r * a.kb / a.cluster;
+    it1 = tile * a.kb + (r + 1) * a.kb / a.cluster;
+  } else {
+    it0 = it_begin(blockIdx.x, a);
+    it1 = it_begin(blockIdx.x + 1, a);
+  }
+}
+
+// Distributed shared memory: `addr` of this CTA's window -> the same offset in
+// cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// 16 bytes into another cluster CTA's shared memory, counted on its mbarrier.
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float x, float y, float z, float w, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];\n" ::"r"(
+                   addr),
+               "f"(x), "f"(y), "f"(z), "f"(w), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
 // The CTA whose iteration range holds iteration i.
 __device__ __forceinline__ int cta_of(long long i, const Args& a) {
   return (int)(((i + 1) * a.ctas - 1) / a.iters);
@@ -128,11 +166,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   auto bar = [&](int i) { return smem_addr(&bars[i]); };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long it0 = it_begin(blockIdx.x, a), it1 = it_begin(blockIdx.x + 1, a);
+  long long it0, it1;
+  cta_range(a, it0, it1);
+  const uint32_t crank = a.cluster > 1 ? blockIdx.x % a.cluster : 0;  // rank in the tile's cluster
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i >= ACC_EMPTY0 && i < ACC_EMPTY0 + 2) ? 4u : 1u);
     *abort_flag = 0;
+    // cluster mode: the tile's other CTAs send their accumulators here
+    if (a.cluster > 1 && crank == 0) mbar_expect_tx(bar(RECV_FULL), (uint32_t)(a.cluster - 1) * kTileBytes);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 1) {
@@ -143,6 +185,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   }
   tc_fence_before();
   __syncthreads();
+  if (a.cluster > 1) cluster_sync_all();  // every CTA's barriers exist before any remote store
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   pdl_trigger();
@@ -254,7 +297,33 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll
       for (int j = 0; j < NB; ++j) v[j] = __uint_as_float(r[j]);
 
-      if (!whole) {
+      if (a.cluster > 1) {
+        // the tile's k ranges were split over a cluster: ranks 1.. send their
+        // accumulator rows into rank 0's shared memory; rank 0 adds them in
+        // rank order and finishes the tile
+        const uint32_t line = (uint32_t)row * 128u;
+        if (crank != 0) {
+          const uint32_t dst = mapa_rank(sbase + OFF_RECV + (crank - 1) * kTileBytes + line, 0);
+          const uint32_t rbar = mapa_rank(bar(RECV_FULL), 0);
+#pragma unroll
+          for (int c = 0; c < NB / 4; ++c)
+            st_async_v4(dst + (((uint32_t)c ^ (row & 7)) << 4), v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3],
+                        rbar);
+          continue;
+        }
+        if (!epi_all(wait_bar(bar(RECV_FULL), 0, abort_flag, a.status))) break;
+        for (int src = 1; src < a.cluster; ++src) {
+          const uint8_t* rl = smem + OFF_RECV + (src - 1) * kTileBytes + line;
+#pragma unroll
+          for (int c = 0; c < NB / 4; ++c) {
+            const float4 t = *reinterpret_cast<const float4*>(rl + ((c ^ (row & 7)) << 4));
+            v[4 * c] += t.x;
+            v[4 * c + 1] += t.y;
+            v[4 * c + 2] += t.z;
+            v[4 * c + 3] += t.w;
+          }
+        }
+      } else if (!whole) {
         const int slot = tile == first_tile ? 0 : 1;
         float* p = a.part + ((size_t)blockIdx.x * 2 + slot) * NB * BM + row;
 #pragma unroll
@@ -339,8 +408,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     }
   }
 
+  // cluster rank 0 keeps its shared memory until every remote store has
+  // landed, also when it stopped early (bounded)
+  if (a.cluster > 1 && crank == 0 && warp >= 2) mbar_wait_bounded(bar(RECV_FULL), 0);
   tc_fence_before();
   __syncthreads();
+  // no CTA of a cluster leaves before rank 0 holds every accumulator
+  if (a.cluster > 1) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
@@ -417,6 +491,44 @@ int num_sms() {
 constexpr uint64_t kMaxTiles = 16384;
 constexpr uint64_t kCountersBytes = kMaxTiles * 4;
 
+// Clusters of `size` linear CTAs that fit on the device at once (cached per
+// device and size); -1 with the op error set on failure.
+int max_active_clusters(int size) {
+  static int cached[64][lin::kMaxCluster + 1];
+  static bool attr_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    set_op_error("doe_linear_bf16: no current device");
+    return -1;
+  }
+  if (cached[dev][size] != 0) return cached[dev][size] < 0 ? 0 : cached[dev][size];
+  if (!attr_set[dev]) {
+    if (cuda_status(cudaFuncSetAttribute(lin::linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         lin::kSmemBytes),
+                    "cudaFuncSetAttribute(linear)") != DOE_OK)
+      return -1;
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)size);
+  cfg.blockDim = dim3(lin::kThreads);
+  cfg.dynamicSmemBytes = lin::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)size;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cuda_status(cudaOccupancyMaxActiveClusters(&n, lin::linear_kernel, &cfg), "cudaOccupancyMaxActiveClusters") !=
+      DOE_OK)
+    return -1;
+  cached[dev][size] = n > 0 ? n : -2;  // -2: none fit (never chosen)
+  return cached[dev][size] < 0 ? 0 : cached[dev][size];
+}
+
 }  // namespace
 
 uint64_t linear_workspace(uint32_t n_out, uint32_t k) {
@@ -437,13 +549,37 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
     return DOE_UNSUPPORTED;
   }
   const long long iters = (long long)tiles * kb;
-  int ctas = num_sms() * lin::kCtasPerSm;
-  if (ctas > lin::kMaxCtas) ctas = lin::kMaxCtas;
-  // enough stages per CTA to cover the load latency, few CTAs per tile so the
-  // partial-tile reduction stays short
-  long long cap = iters / lin::kMinIters > 0 ? iters / lin::kMinIters : 1;
-  if (cap > (long long)tiles * lin::kMaxSplit) cap = (long long)tiles * lin::kMaxSplit;
-  if ((long long)ctas > cap) ctas = (int)cap;
+  const int sms = num_sms();
+  // Fewer tiles than half the SMs: split each tile's k over a cluster of up to
+  // kMaxCluster CTAs that sum through distributed shared memory.  Otherwise
+  // stream-K over the whole product.
+  // The tile's clusters must all be resident at once (one CTA per SM, a
+  // cluster's CTAs on one GPC), or the split costs a second wave.
+  int cluster = 1;
+  if ((long long)tiles * 2 <= sms) {
+    int c = sms / (int)tiles;
+    if (c > lin::kMaxCluster) c = lin::kMaxCluster;
+    if (c > (int)(kb / lin::kMinIters)) c = (int)(kb / lin::kMinIters);
+    for (; c > 1; --c) {
+      const int fit = max_active_clusters(c);
+      if (fit < 0) return DOE_CUDA_ERROR;
+      if ((int)tiles <= fit) break;
+    }
+    cluster = c;
+  }
+  int ctas;
+  if (cluster > 1) {
+    ctas = (int)tiles * cluster;
+  } else {
+    cluster = 1;
+    ctas = sms * lin::kCtasPerSm;
+    if (ctas > lin::kMaxCtas) ctas = lin::kMaxCtas;
+    // enough stages per CTA to cover the load latency, few CTAs per tile so the
+    // partial-tile reduction stays short
+    long long cap = iters / lin::kMinIters > 0 ? iters / lin::kMinIters : 1;
+    if (cap > (long long)tiles * lin::kMaxSplit) cap = (long long)tiles * lin::kMaxSplit;
+    if ((long long)ctas > cap) ctas = (int)cap;
+  }
   const uint64_t need = linear_workspace(n_out, k);
   if (launch->workspace == nullptr || launch->workspace_bytes < need) {
     set_op_error("doe_linear_bf16: workspace of %llu bytes required, %llu given", (unsigned long long)need,
@@ -469,6 +605,7 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
   a.epilogue = (int)o->epilogue;
   a.dtype = (int)o->dtype;
   a.iters = iters;
+  a.cluster = cluster;
   CUtensorMap mw, mx;
   int rc = encode_rows_map(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, 1, n_out, 64, lin::BM,
                            "doe_linear_bf16");
@@ -484,9 +621,21 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
     if (rc != DOE_OK) return rc;
     attr_set = true;
   }
-  return cuda_status(launch_pdl(lin::linear_kernel, dim3(ctas), dim3(lin::kThreads), lin::kSmemBytes,
-                                static_cast<cudaStream_t>(launch->stream), mw, mx, a),
-                     "linear_kernel");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctas);
+  cfg.blockDim = dim3(lin::kThreads);
+  cfg.dynamicSmemBytes = lin::kSmemBytes;
+  cfg.stream = static_cast<cudaStream_t>(launch->stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cuda_status(cudaLaunchKernelEx(&cfg, lin::linear_kernel, mw, mx, a), "linear_kernel");
 }
 
 int launch_rmsnorm(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
