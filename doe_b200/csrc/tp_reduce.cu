@@ -20,7 +20,8 @@ constexpr uint32_t OFF_FLAGS = 0;   // u64 [DOE_TP_MAX_RANKS], written by the pe
 constexpr uint32_t OFF_EPOCH = 64;  // u64, this rank's last completed epoch
 constexpr uint32_t OFF_EXIT = 72;   // u32, CTAs of the running launch that finished
 constexpr uint32_t OFF_SLOTS = 256;
-constexpr int kThreads = 256;
+constexpr int kThreads = 1024;  // a 4096-wide row: one 16-byte column group per thread, every
+                                // peer's load of it in flight at once
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 1.9 GHz
 
 struct Args {
