@@ -378,6 +378,42 @@ def measure_decoder(steps, warmup, world, rank, pk):
             "status": status, "output_finite": finite}
 
 
+LINEAR_SHAPES = {  # config 5's products at tp1: (n_out, k, SwiGLU)
+    "qkv": (6144, 4096, False), "o_proj": (4096, 4096, False), "gate_up": (28672, 4096, True),
+    "down_proj": (4096, 14336, False)}
+
+
+def measure_linear(steps, warmup, world, pk, only=None):
+    """doe_linear_bf16 on config 5's shapes (batch 32): each step one product,
+    weights rotating over copies that together exceed L2."""
+    import torch
+
+    from doe_b200 import ops
+
+    out = {}
+    for name, (n, k, swiglu) in LINEAR_SHAPES.items():
+        if only and name != only:
+            continue
+        copies = max(2, (300 << 20) // (n * k * 2) + 1)
+        g = torch.Generator(device="cuda")
+        g.manual_seed(5)
+        ws = [(torch.randn((n, k), generator=g, device="cuda") * 0.02).to(torch.bfloat16) for _ in range(copies)]
+        x = torch.randn((32, k), generator=g, device="cuda").to(torch.bfloat16)
+        y = torch.empty((32, n // 2 if swiglu else n), dtype=torch.bfloat16, device="cuda")
+        lws = ops.linear_workspace(n, k)
+        it = iter(range(10 ** 9))
+        total, each = time_steps(lambda: ops.linear(x, ws[next(it) % copies], [y], swiglu=swiglu, ws=lws),
+                                 steps, warmup, world)
+        total = max_over_ranks(world, [total])[0]
+        us = total / steps * 1e3
+        nbytes = n * k * 2 + 32 * k * 2 + y.numel() * 2
+        out[name] = {"n_out": n, "k": k, "swiglu": swiglu, "us": us, "gbs": nbytes / us / 1e3,
+                     "frac": nbytes / us / 1e3 / pk["hbm_gbs"]}
+        del ws
+        torch.cuda.empty_cache()
+    return out
+
+
 def measure_e2e(w, cache, steps, warmup, world, gw=None):
     """Same decode step through doe_cuda_dispatch with host buffers."""
     gw = gw if gw is not None else w
@@ -545,10 +581,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8", "append", "decoder"],
+    ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8", "append", "decoder",
+                                       "linear"],
                     default="all",
                     help="time one workload only (no e2e or CPU leg): headline = config 3, "
-                         "append = config 4b chunk quantise-append, decoder = config 5")
+                         "append = config 4b chunk quantise-append, decoder = config 5, "
+                         "linear = config 5's products one at a time")
+    ap.add_argument("--linear-shape", choices=sorted(LINEAR_SHAPES), default=None,
+                    help="with --only linear: time this product alone")
     ap.add_argument("--split-pages", type=int, default=0,
                     help="pages per split of the paged decode (0 = the library's choice)")
     ap.add_argument("--seqs", type=int, default=0,
@@ -565,8 +605,10 @@ def main():
     pk = peaks()
     from doe_b200 import workloads
 
-    if args.only in ("prefill", "f32", "int8", "append", "decoder"):
-        if args.only == "decoder":
+    if args.only in ("prefill", "f32", "int8", "append", "decoder", "linear"):
+        if args.only == "linear":
+            r = measure_linear(args.steps, args.warmup, world, pk, args.linear_shape)
+        elif args.only == "decoder":
             r = measure_decoder(args.steps, args.warmup, world, rank, pk)
         elif args.only == "prefill":
             r = measure_prefill(args.steps, args.warmup, world, pk)
