@@ -301,8 +301,12 @@ def measure_f32(steps, warmup, world, pk):
             "bytes_per_step": d.bytes_per_step, "l2": "flushed (256 MB write) between steps"}
 
 
-def measure_prefill(steps, warmup, world, pk):
-    """Config 2: causal prefill (tcgen05) incl. the fused paged KV-cache write."""
+def measure_prefill(steps, warmup, world, pk, rank=0):
+    """Config 2: causal prefill (tcgen05) incl. the fused paged KV-cache write.
+
+    With N ranks the prompt is sharded by KV head (each rank takes Hkv/N KV
+    heads and their query heads; outputs and cache stay head-sharded, no
+    collective): the same prompt on more GPUs, strong scaling."""
     import torch
 
     from doe_b200 import ops, workloads
@@ -310,10 +314,15 @@ def measure_prefill(steps, warmup, world, pk):
 
     w = workloads.prefill_f16()
     S = w.q.shape[0]
+    H, Hkv = w.q.shape[1], w.k.shape[1]
+    if Hkv % world:
+        raise ValueError(f"{world} ranks do not divide {Hkv} KV heads")
+    kvh, qh = Hkv // world, H // world
     t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-    q, k, v = t(w.q), t(w.k), t(w.v)
-    out = torch.empty((S, w.q.shape[1], 128), dtype=torch.float32, device="cuda")
-    cache = PagedKVCache(num_pages=S // 16, page_size=16, num_kv_heads=w.k.shape[1], head_dim=128,
+    q = t(w.q[:, rank * qh:(rank + 1) * qh])
+    k, v = t(w.k[:, rank * kvh:(rank + 1) * kvh]), t(w.v[:, rank * kvh:(rank + 1) * kvh])
+    out = torch.empty((S, qh, 128), dtype=torch.float32, device="cuda")
+    cache = PagedKVCache(num_pages=S // 16, page_size=16, num_kv_heads=kvh, head_dim=128,
                          block_table=np.arange(S // 16, dtype=np.int32)[None])
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
@@ -330,10 +339,12 @@ def measure_prefill(steps, warmup, world, pk):
             times.append(a.elapsed_time(b))
     assert int(status.item()) == 0, f"prefill status {int(status.item()):#x}"
     ms, = max_over_ranks(world, [float(np.mean(times))])
-    tflops = w.flops / (ms / 1e3) / 1e12
+    tflops = w.flops / (ms / 1e3) / 1e12  # the whole prompt's flops over the slowest rank's time
     return {"config": "config 2: causal prefill S 2048, 32 heads, D 128, f16 in / f32 acc, seed 1, "
-                      "+ paged KV-cache write", "ms": ms, "tflops": tflops * world,
-            "frac_of_dense_peak": tflops / pk["bf16_tflops"], "flops": w.flops,
+                      "+ paged KV-cache write", "ms": ms, "tflops": tflops,
+            "parallelism": f"{world} ranks by KV head ({kvh} KV heads each)" if world > 1 else "one GPU",
+            "scaling": "strong" if world > 1 else None,
+            "frac_of_dense_peak": tflops / world / pk["bf16_tflops"], "flops": w.flops,
             "peak_tflops": pk["bf16_tflops"], "peak_note": "measured dense bf16 burst (f16 runs at the same rate)",
             "l2": "flushed (256 MB write) between steps"}
 
@@ -611,7 +622,7 @@ def main():
         elif args.only == "decoder":
             r = measure_decoder(args.steps, args.warmup, world, rank, pk)
         elif args.only == "prefill":
-            r = measure_prefill(args.steps, args.warmup, world, pk)
+            r = measure_prefill(args.steps, args.warmup, world, pk, rank)
         elif args.only == "f32":
             r = measure_f32(args.steps, args.warmup, world, pk)
         elif args.only == "append":
@@ -655,7 +666,7 @@ def main():
                                        **ca}
         extras["f32_decode"] = {"config": "config 1: 8 heads, D 64, 512 tokens, f32", **measure_f32(20, 5, world, pk)}
         try:
-            extras["prefill"] = measure_prefill(10, 3, world, pk)
+            extras["prefill"] = measure_prefill(10, 3, world, pk, rank)
         except Exception as e:  # reported, never hidden
             extras["prefill"] = {"error": str(e)[:300]}
         torch.cuda.empty_cache()

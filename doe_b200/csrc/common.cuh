@@ -72,13 +72,17 @@ __device__ __forceinline__ uint32_t prmt(uint32_t x, uint32_t y, uint32_t sel) {
 // operands' ulps), far beyond y's error; y lands on the same side of every
 // rounding boundary and is exactly k + 1/2 in the tie case, where rint takes
 // the even neighbour as the CPU does.
+// The result is a word whose low byte is q (two's complement): y is clamped
+// to [-127, 127] in f32 (the same as clamping rint(y)), and adding 1.5 * 2^23
+// rounds it to an integer, ties to even, in the low mantissa bits, so the
+// sum's bit pattern is 0x4B400000 + q.  Everything stays on the FP32 pipe.
 __device__ __forceinline__ int quantize_s8(float x, float s, float rs) {
   const float y0 = x * rs;
   const float y = fmaf(fmaf(-y0, s, x), rs, y0);
-  const int q = __float2int_rn(y);
-  return q > 127 ? 127 : (q < -127 ? -127 : q);
+  const float c = fminf(fmaxf(y, -127.0f), 127.0f);
+  return (int)__float_as_uint(__fadd_rn(c, 12582912.0f));
 }
-// Low bytes of four ints (two's complement int8 values) packed into a word.
+// Low bytes of four words (two's complement int8 values) packed into a word.
 __device__ __forceinline__ uint32_t pack_s8x4(int q0, int q1, int q2, int q3) {
   return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
 }

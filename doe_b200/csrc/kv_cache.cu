@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(256) paged_append_kernel(const PagedAppendArgs
 #pragma unroll
         for (int i = 0; i < EPL; ++i) {
           const float xv = (i & 1) ? __high2float(x2[i / 2]) : __low2float(x2[i / 2]);
-          dst[i] = (int8_t)(sf != 0.0f ? quantize_s8(xv, sf, rs) : 0);
+          dst[i] = (int8_t)(uint8_t)(sf != 0.0f ? quantize_s8(xv, sf, rs) & 0xff : 0);
         }
         if (lane == 0) (kv ? a.v_scale : a.k_scale)[((size_t)page * Hkv + h) * a.page_size + in_page] = sh;
       }

@@ -3,7 +3,8 @@
 The kernels (`quantize_s8` in doe_b200/csrc/common.cuh) compute
 clamp(rint(x / s), -127, 127) for f16 values x and the f16 row scale s without
 an IEEE division: y0 = x * rcp(s), y = fma(fma(-y0, s, x), rcp(s), y0), then
-round-to-nearest-even.  The CPU definition (oracle/doe_oracle.c, the int8
+round-to-nearest-even (a clamp to +-127 in f32 and an add of 1.5 * 2^23,
+whose low byte is the int8 value).  The CPU definition (oracle/doe_oracle.c, the int8
 append) divides.  This test replays the kernels' arithmetic in float32 with an
 exact-product FMA and requires the same integers as the division: every
 positive and negative f16 value against a sample of f16 scales, exact
@@ -26,7 +27,10 @@ def kernel_quantize(x, s):
     rs = (F32(1.0) / s).astype(F32)  # correctly rounded reciprocal
     y0 = (x * rs).astype(F32)
     y = _fma(_fma(-y0, s, x), rs, y0)
-    return np.clip(np.rint(y).astype(np.int64), -127, 127)
+    # clamp in f32, then round by adding 1.5 * 2^23 (round-half-even in f32)
+    c = np.clip(y, F32(-127), F32(127)).astype(F32)
+    bits = (c + F32(12582912.0)).astype(F32).view(np.uint32)
+    return (bits & 0xFF).astype(np.uint8).view(np.int8).astype(np.int64)
 
 
 def divide_quantize(x, s):
