@@ -120,7 +120,9 @@ SIGNATURES = {
     "doe_cuda_stream": (_P, [_P]),
     "doe_cuda_buffer_ensure": (_I, [_P, _U64, _U64]),
     "doe_cuda_buffer_write": (_I, [_P, _U64, _U64, _P, _U64]),
+    "doe_cuda_buffer_write_async": (_I, [_P, _U64, _U64, _P, _U64]),
     "doe_cuda_buffer_read": (_I, [_P, _U64, _U64, _P, _U64]),
+    "doe_cuda_buffer_read_async": (_I, [_P, _U64, _U64, _P, _U64]),
     "doe_cuda_buffer_release": (_I, [_P, _U64]),
     "doe_cuda_buffer_size": (_I, [_P, _U64, C.POINTER(_U64)]),
     "doe_cuda_buffer_device_ptr": (_I, [_P, _U64, C.POINTER(_P)]),

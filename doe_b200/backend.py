@@ -75,6 +75,11 @@ class CudaBackend:
         self._check("doe_cuda_buffer_write", self._lib.doe_cuda_buffer_write(
             self._h, handle, offset, ptr, nbytes))
 
+    def write_ptr_async(self, handle: int, offset: int, ptr: int, nbytes: int) -> None:
+        """Deferred write from page-locked memory (kept unchanged until flush_queue())."""
+        self._check("doe_cuda_buffer_write_async", self._lib.doe_cuda_buffer_write_async(
+            self._h, handle, offset, ptr, nbytes))
+
     def capture_buffer(self, handle: int, offset: int, size: int) -> bytes:
         out = np.empty(size, np.uint8)
         self._check("doe_cuda_buffer_read", self._lib.doe_cuda_buffer_read(
@@ -83,6 +88,11 @@ class CudaBackend:
 
     def read_into(self, handle: int, offset: int, ptr: int, nbytes: int) -> None:
         self._check("doe_cuda_buffer_read", self._lib.doe_cuda_buffer_read(
+            self._h, handle, offset, ptr, nbytes))
+
+    def read_into_async(self, handle: int, offset: int, ptr: int, nbytes: int) -> None:
+        """Deferred capture into page-locked memory; valid after flush_queue()."""
+        self._check("doe_cuda_buffer_read_async", self._lib.doe_cuda_buffer_read_async(
             self._h, handle, offset, ptr, nbytes))
 
     def release_buffer(self, handle: int) -> None:

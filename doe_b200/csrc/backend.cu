@@ -29,6 +29,14 @@ struct DevBuffer {
   uint64_t bytes = 0;
   std::vector<uint8_t> shadow;  // host copy of small buffers (uniforms)
   bool shadow_valid = false;
+  // Writes run on the upload stream, captures on the download stream and
+  // kernels on the compute stream; these events order them per buffer:
+  // a write waits for the last kernel that bound the buffer (ev_used) and
+  // for a capture still reading it (ev_read); a kernel waits for the writes
+  // and captures before it; a capture waits for the last kernel and for a
+  // write queued after it.
+  cudaEvent_t ev_written = nullptr, ev_used = nullptr, ev_read = nullptr;
+  bool write_pending = false, used = false, read_pending = false;
 };
 
 constexpr uint64_t kShadowMax = 64 * 1024;
@@ -43,7 +51,9 @@ uint64_t now_ns() {
 
 struct doe_cuda_ctx {
   int device = 0;
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;  // kernels
+  cudaStream_t copy = nullptr;    // buffer writes (uploads)
+  cudaStream_t down = nullptr;    // captures (downloads)
   std::unordered_map<uint64_t, DevBuffer> buffers;
   uint8_t* staging = nullptr;  // pinned host
   uint64_t staging_bytes = 0;
@@ -80,7 +90,30 @@ int bind_device(doe_cuda_ctx* ctx) { return cu(ctx, cudaSetDevice(ctx->device), 
 
 int sync_stream(doe_cuda_ctx* ctx) {
   int rc = cu(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  if (rc == DOE_OK) rc = cu(ctx, cudaStreamSynchronize(ctx->copy), "cudaStreamSynchronize(upload)");
+  if (rc == DOE_OK) rc = cu(ctx, cudaStreamSynchronize(ctx->down), "cudaStreamSynchronize(download)");
   if (rc == DOE_OK) ctx->staging_used = 0;
+  return rc;
+}
+
+// A write of `b` on the upload stream waits for the last kernel that bound it
+// and for a capture still reading it.
+int upload_after_uses(doe_cuda_ctx* ctx, DevBuffer& b) {
+  int rc = DOE_OK;
+  if (b.used) rc = cu(ctx, cudaStreamWaitEvent(ctx->copy, b.ev_used, 0), "cudaStreamWaitEvent(upload)");
+  if (rc == DOE_OK && b.read_pending) {
+    rc = cu(ctx, cudaStreamWaitEvent(ctx->copy, b.ev_read, 0), "cudaStreamWaitEvent(upload)");
+    b.read_pending = false;  // what follows this write is ordered after it
+  }
+  return rc;
+}
+// A capture of `b` on the download stream waits for the last kernel that bound
+// it and for a write queued since.
+int download_after_writes(doe_cuda_ctx* ctx, DevBuffer& b) {
+  int rc = DOE_OK;
+  if (b.used) rc = cu(ctx, cudaStreamWaitEvent(ctx->down, b.ev_used, 0), "cudaStreamWaitEvent(download)");
+  if (rc == DOE_OK && b.write_pending)
+    rc = cu(ctx, cudaStreamWaitEvent(ctx->down, b.ev_written, 0), "cudaStreamWaitEvent(download)");
   return rc;
 }
 
@@ -100,9 +133,20 @@ int ensure_buffer(doe_cuda_ctx* ctx, uint64_t handle, uint64_t bytes, DevBuffer*
     return rc;
   }
   DevBuffer& b = ctx->buffers[handle];
-  if (b.ptr) {  // grow: keep the old contents
-    rc = cu(ctx, cudaMemcpyAsync(p, b.ptr, b.bytes, cudaMemcpyDeviceToDevice, ctx->stream),
-            "cudaMemcpyAsync(grow)");
+  if (!b.ev_written) {
+    rc = cu(ctx, cudaEventCreateWithFlags(&b.ev_written, cudaEventDisableTiming), "cudaEventCreate");
+    if (rc == DOE_OK) rc = cu(ctx, cudaEventCreateWithFlags(&b.ev_used, cudaEventDisableTiming), "cudaEventCreate");
+    if (rc == DOE_OK) rc = cu(ctx, cudaEventCreateWithFlags(&b.ev_read, cudaEventDisableTiming), "cudaEventCreate");
+    if (rc != DOE_OK) {
+      cudaFree(p);
+      return rc;
+    }
+  }
+  if (b.ptr) {  // grow: keep the old contents (after every queued copy and kernel)
+    rc = sync_stream(ctx);
+    if (rc == DOE_OK)
+      rc = cu(ctx, cudaMemcpyAsync(p, b.ptr, b.bytes, cudaMemcpyDeviceToDevice, ctx->stream),
+              "cudaMemcpyAsync(grow)");
     if (rc == DOE_OK) rc = sync_stream(ctx);
     cudaFree(b.ptr);
     if (rc != DOE_OK) {
@@ -124,6 +168,10 @@ int ensure_buffer(doe_cuda_ctx* ctx, uint64_t handle, uint64_t bytes, DevBuffer*
     b.shadow.clear();
     b.shadow_valid = false;
   }
+  // the zero fill (and any grow copy) ran on the compute stream: copies wait for it
+  rc = cu(ctx, cudaEventRecord(b.ev_used, ctx->stream), "cudaEventRecord");
+  if (rc != DOE_OK) return rc;
+  b.used = true;
   *out = &b;
   return DOE_OK;
 }
@@ -573,6 +621,8 @@ int doe_cuda_open(int ordinal, doe_cuda_ctx** out) {
   ctx->device = ordinal;
   int rc = bind_device(ctx);
   if (rc == DOE_OK) rc = cu(ctx, cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking), "cudaStreamCreate");
+  if (rc == DOE_OK) rc = cu(ctx, cudaStreamCreateWithFlags(&ctx->copy, cudaStreamNonBlocking), "cudaStreamCreate(upload)");
+  if (rc == DOE_OK) rc = cu(ctx, cudaStreamCreateWithFlags(&ctx->down, cudaStreamNonBlocking), "cudaStreamCreate(download)");
   if (rc == DOE_OK) rc = cu(ctx, cudaMalloc(&ctx->status_dev, sizeof(int32_t)), "cudaMalloc(status)");
   if (rc == DOE_OK) rc = cu(ctx, cudaMemset(ctx->status_dev, 0, sizeof(int32_t)), "cudaMemset(status)");
   if (rc == DOE_OK) rc = cu(ctx, cudaHostAlloc((void**)&ctx->status_host, sizeof(int32_t), cudaHostAllocDefault), "cudaHostAlloc(status)");
@@ -591,8 +641,14 @@ int doe_cuda_close(doe_cuda_ctx* ctx) {
   if (!ctx) return DOE_INVALID_ARGUMENT;
   cudaSetDevice(ctx->device);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
-  for (auto& kv : ctx->buffers)
+  if (ctx->copy) cudaStreamSynchronize(ctx->copy);
+  if (ctx->down) cudaStreamSynchronize(ctx->down);
+  for (auto& kv : ctx->buffers) {
     if (kv.second.ptr) cudaFree(kv.second.ptr);
+    if (kv.second.ev_written) cudaEventDestroy(kv.second.ev_written);
+    if (kv.second.ev_used) cudaEventDestroy(kv.second.ev_used);
+    if (kv.second.ev_read) cudaEventDestroy(kv.second.ev_read);
+  }
   if (ctx->staging) cudaFreeHost(ctx->staging);
   if (ctx->workspace) cudaFree(ctx->workspace);
   if (ctx->status_dev) cudaFree(ctx->status_dev);
@@ -600,6 +656,8 @@ int doe_cuda_close(doe_cuda_ctx* ctx) {
   if (ctx->ev_begin) cudaEventDestroy(ctx->ev_begin);
   if (ctx->ev_end) cudaEventDestroy(ctx->ev_end);
   if (ctx->stream) cudaStreamDestroy(ctx->stream);
+  if (ctx->copy) cudaStreamDestroy(ctx->copy);
+  if (ctx->down) cudaStreamDestroy(ctx->down);
   delete ctx;
   return DOE_OK;
 }
@@ -627,12 +685,37 @@ int doe_cuda_buffer_write(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset, c
   if (b->shadow_valid) std::memcpy(b->shadow.data() + offset, data, size);
   DOE_TRY(ensure_staging(ctx, size));
   std::memcpy(ctx->staging + ctx->staging_used, data, size);
+  DOE_TRY(upload_after_uses(ctx, *b));
   int rc = cu(ctx, cudaMemcpyAsync(static_cast<uint8_t*>(b->ptr) + offset,
                                    ctx->staging + ctx->staging_used, size, cudaMemcpyHostToDevice,
-                                   ctx->stream),
+                                   ctx->copy),
               "cudaMemcpyAsync(H2D)");
   ctx->staging_used += (size + 255) / 256 * 256;
+  if (rc == DOE_OK) rc = cu(ctx, cudaEventRecord(b->ev_written, ctx->copy), "cudaEventRecord");
+  if (rc == DOE_OK) b->write_pending = true;
   return rc;
+}
+
+int doe_cuda_buffer_write_async(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset, const void* data,
+                                uint64_t size) {
+  if (!ctx || (!data && size)) return DOE_INVALID_ARGUMENT;
+  DOE_TRY(bind_device(ctx));
+  cudaPointerAttributes pa;
+  if (size && (cudaPointerGetAttributes(&pa, data) != cudaSuccess || pa.type != cudaMemoryTypeHost)) {
+    cudaGetLastError();
+    return fail(ctx, DOE_INVALID_ARGUMENT, "deferred write: the source must be page-locked host memory");
+  }
+  DevBuffer* b;
+  DOE_TRY(ensure_buffer(ctx, handle, offset + size, &b));
+  if (size == 0) return DOE_OK;
+  if (b->shadow_valid) std::memcpy(b->shadow.data() + offset, data, size);
+  DOE_TRY(upload_after_uses(ctx, *b));
+  DOE_TRY(cu(ctx, cudaMemcpyAsync(static_cast<uint8_t*>(b->ptr) + offset, data, size, cudaMemcpyHostToDevice,
+                                  ctx->copy),
+             "cudaMemcpyAsync(H2D)"));
+  DOE_TRY(cu(ctx, cudaEventRecord(b->ev_written, ctx->copy), "cudaEventRecord"));
+  b->write_pending = true;
+  return DOE_OK;
 }
 
 int doe_cuda_buffer_read(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset, void* dst,
@@ -648,26 +731,54 @@ int doe_cuda_buffer_read(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset, vo
   if (size == 0) return DOE_OK;
   DOE_TRY(bind_device(ctx));
   // The read waits for the copy before returning, so a page-locked
-  // destination can take the DMA directly (no staging hop).
+  // destination can take the DMA directly (no staging hop).  Copies run on
+  // the copy stream after the writes queued there and the last kernel that
+  // bound the buffer.
+  DOE_TRY(download_after_writes(ctx, it->second));
   cudaPointerAttributes pa;
   if (cudaPointerGetAttributes(&pa, dst) == cudaSuccess && pa.type == cudaMemoryTypeHost) {
     DOE_TRY(cu(ctx, cudaMemcpyAsync(dst, static_cast<uint8_t*>(it->second.ptr) + offset, size,
-                                    cudaMemcpyDeviceToHost, ctx->stream),
+                                    cudaMemcpyDeviceToHost, ctx->down),
                "cudaMemcpyAsync(D2H)"));
-    DOE_TRY(cu(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize"));
-    ctx->staging_used = 0;
+    DOE_TRY(cu(ctx, cudaStreamSynchronize(ctx->down), "cudaStreamSynchronize(download)"));
     return DOE_OK;
   }
   cudaGetLastError();  // a pageable pointer is not an error
   DOE_TRY(ensure_staging(ctx, size));
-  DOE_TRY(cu(ctx, cudaMemcpyAsync(ctx->staging + ctx->staging_used,
-                                  static_cast<uint8_t*>(it->second.ptr) + offset, size,
-                                  cudaMemcpyDeviceToHost, ctx->stream),
-             "cudaMemcpyAsync(D2H)"));
   const uint64_t at = ctx->staging_used;
-  DOE_TRY(cu(ctx, cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize"));
+  ctx->staging_used += (size + 255) / 256 * 256;  // the staged uploads queued before stay intact
+  DOE_TRY(cu(ctx, cudaMemcpyAsync(ctx->staging + at, static_cast<uint8_t*>(it->second.ptr) + offset, size,
+                                  cudaMemcpyDeviceToHost, ctx->down),
+             "cudaMemcpyAsync(D2H)"));
+  DOE_TRY(cu(ctx, cudaStreamSynchronize(ctx->down), "cudaStreamSynchronize(download)"));
   std::memcpy(dst, ctx->staging + at, size);
-  ctx->staging_used = 0;
+  return DOE_OK;
+}
+
+int doe_cuda_buffer_read_async(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset, void* dst,
+                               uint64_t size) {
+  if (!ctx || (!dst && size)) return DOE_INVALID_ARGUMENT;
+  auto it = ctx->buffers.find(handle);
+  if (it == ctx->buffers.end())
+    return fail(ctx, DOE_NOT_FOUND, "capture: unknown handle %llu", (unsigned long long)handle);
+  if (offset + size > it->second.bytes)
+    return fail(ctx, DOE_OUT_OF_RANGE, "capture: [%llu, %llu) beyond %llu bytes",
+                (unsigned long long)offset, (unsigned long long)(offset + size),
+                (unsigned long long)it->second.bytes);
+  if (size == 0) return DOE_OK;
+  DOE_TRY(bind_device(ctx));
+  cudaPointerAttributes pa;
+  if (cudaPointerGetAttributes(&pa, dst) != cudaSuccess || pa.type != cudaMemoryTypeHost) {
+    cudaGetLastError();
+    return fail(ctx, DOE_INVALID_ARGUMENT, "deferred capture: the destination must be page-locked host memory");
+  }
+  DOE_TRY(download_after_writes(ctx, it->second));
+  DOE_TRY(cu(ctx, cudaMemcpyAsync(dst, static_cast<uint8_t*>(it->second.ptr) + offset, size, cudaMemcpyDeviceToHost,
+                                  ctx->down),
+             "cudaMemcpyAsync(D2H)"));
+  // a later write or kernel must not change the bytes before the copy has read them
+  DOE_TRY(cu(ctx, cudaEventRecord(it->second.ev_read, ctx->down), "cudaEventRecord"));
+  it->second.read_pending = true;
   return DOE_OK;
 }
 
@@ -753,6 +864,19 @@ int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel, const char* entry_p
   }
   int rc = bind_device(ctx);
   DispatchCtx d{ctx, bindings, num_bindings, kernel};
+  // the kernel runs after the writes and captures queued for its buffers
+  for (uint32_t i = 0; i < num_bindings && rc == DOE_OK && bindings; ++i) {
+    auto bit = ctx->buffers.find(bindings[i].handle);
+    if (bit == ctx->buffers.end()) continue;
+    if (bit->second.write_pending) {
+      rc = cu(ctx, cudaStreamWaitEvent(ctx->stream, bit->second.ev_written, 0), "cudaStreamWaitEvent");
+      bit->second.write_pending = false;
+    }
+    if (rc == DOE_OK && bit->second.read_pending) {  // the kernel may overwrite bytes a capture reads
+      rc = cu(ctx, cudaStreamWaitEvent(ctx->stream, bit->second.ev_read, 0), "cudaStreamWaitEvent");
+      bit->second.read_pending = false;
+    }
+  }
   const bool timed = ctx->timestamps;
   if (rc == DOE_OK && timed) rc = cu(ctx, cudaEventRecord(ctx->ev_begin, ctx->stream), "cudaEventRecord");
   const uint64_t t1 = now_ns();
@@ -773,6 +897,14 @@ int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel, const char* entry_p
     }
   }
   if (rc == DOE_OK && timed) rc = cu(ctx, cudaEventRecord(ctx->ev_end, ctx->stream), "cudaEventRecord");
+  // later writes and captures of the bound buffers wait for this kernel
+  for (uint32_t i = 0; i < num_bindings && rc == DOE_OK && bindings; ++i) {
+    auto bit = ctx->buffers.find(bindings[i].handle);
+    if (bit != ctx->buffers.end()) {
+      rc = cu(ctx, cudaEventRecord(bit->second.ev_used, ctx->stream), "cudaEventRecord");
+      bit->second.used = true;
+    }
+  }
   const uint64_t t2 = now_ns();
   res.setup_ns = t1 - t0;
   res.encode_ns = t2 - t1;

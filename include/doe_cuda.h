@@ -121,6 +121,20 @@ int doe_cuda_buffer_write(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset,
  * device bytes into caller memory.                                         */
 int doe_cuda_buffer_read(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset,
                          void* dst, uint64_t size);
+/* capture_buffer in the deferred queue mode (set_queue_wait_mode,
+ * backend_iface.zig:18): the device-to-host copy is queued on the backend
+ * stream after the work already queued, and the call returns at once.  `dst`
+ * must be page-locked host memory (cudaHostAlloc / cudaHostRegister); its
+ * bytes are valid after the next doe_cuda_flush.  A serving loop queues step
+ * i + 1 while step i still runs.                                           */
+int doe_cuda_buffer_read_async(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset,
+                               void* dst, uint64_t size);
+/* execute_buffer_write_bytes in the deferred mode: `data` must be page-locked
+ * host memory, copied by DMA on the backend's copy stream after the call
+ * returns (no staging copy); the caller keeps it unchanged until the next
+ * doe_cuda_flush.  Ordered like doe_cuda_buffer_write.                     */
+int doe_cuda_buffer_write_async(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset,
+                                const void* data, uint64_t size);
 int doe_cuda_buffer_release(doe_cuda_ctx* ctx, uint64_t handle);
 int doe_cuda_buffer_size(doe_cuda_ctx* ctx, uint64_t handle, uint64_t* bytes);
 int doe_cuda_buffer_device_ptr(doe_cuda_ctx* ctx, uint64_t handle, void** out);

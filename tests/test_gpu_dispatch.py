@@ -57,6 +57,27 @@ def test_buffer_roundtrip_grow_and_errors(be):
         be.capture_buffer(7, 0, 4)
 
 
+def test_deferred_capture_lands_at_flush(be):
+    g = np.random.default_rng(1)
+    data = g.integers(0, 256, 1 << 20, dtype=np.uint8)
+    be.execute_buffer_write_bytes(8, 0, data)
+    pinned = torch.zeros(1 << 20, dtype=torch.uint8).pin_memory()
+    be.read_into_async(8, 0, pinned.data_ptr(), 1 << 20)
+    be.flush_queue()
+    assert np.array_equal(pinned.numpy(), data)
+    # a deferred write from pinned memory lands before the next kernel / capture
+    src = torch.from_numpy(data[::-1].copy()).pin_memory()
+    be.write_ptr_async(8, 0, src.data_ptr(), 1 << 20)
+    be.read_into_async(8, 0, pinned.data_ptr(), 1 << 20)
+    be.flush_queue()
+    assert np.array_equal(pinned.numpy(), data[::-1])
+    # pageable destinations are refused (the copy would outlive the call)
+    host = np.zeros(16, np.uint8)
+    with pytest.raises(abi.DoeError) as e:
+        be.read_into_async(8, 0, host.ctypes.data, 16)
+    assert e.value.rc == abi.DOE_INVALID_ARGUMENT
+
+
 def test_attention_decode_wgsl_dispatch(be):
     w = workloads.decode_f32()
     be.execute_buffer_write_bytes(1, 0, _u32(8, 64, 512, float(np.float32(w.scale))))
@@ -183,3 +204,54 @@ def test_paged_decode_dispatch_matches_operator(be):
     assert np.array_equal(out.reshape(ref.shape), ref.cpu().numpy())
     assert np.array_equal(np.frombuffer(be.capture_buffer(42, 0, kp.nbytes), np.float16).reshape(kp.shape),
                           c.k_pool.cpu().numpy())
+
+
+def test_queued_steps_on_alternating_buffers_match_synchronous_steps(be):
+    # writes run on the backend's copy stream and kernels on its compute
+    # stream, ordered per buffer by events; four decode steps queued back to
+    # back (new queries each step, two buffer sets alternating, deferred
+    # captures) must give what one synchronous step at a time gives
+    w = workloads.small_paged(4, [40, 300, 7, 129])
+    g = np.random.default_rng(8)
+    qs = [g.standard_normal(w.q.shape, dtype=np.float32).astype(np.float16) for _ in range(4)]
+    out_bytes = w.num_seqs * w.num_heads * w.head_dim * 4
+    uni = _u32(w.num_seqs, w.num_heads, w.num_kv_heads, w.head_dim, w.page_size, w.num_pages,
+               w.block_table.shape[1], 0, float(np.float32(w.scale)), 0)
+    from doe_b200.kv import PagedKVCache
+    c = PagedKVCache(num_pages=w.num_pages, page_size=w.page_size, num_kv_heads=w.num_kv_heads,
+                     head_dim=w.head_dim, block_table=w.block_table)
+    workloads.fill_pools(c, 6)
+    kp, vp = c.k_pool.cpu().numpy(), c.v_pool.cpu().numpy()
+
+    def setup(b):
+        for h, arr in ((60, uni), (62, kp), (63, vp), (64, w.block_table)):
+            b.execute_buffer_write_bytes(h, 0, arr)
+
+    def binds(o):
+        return [Bind(0, 60, size=40), Bind(1, 70 + o), Bind(2, 62), Bind(3, 63), Bind(4, 64), Bind(5, 71 + o),
+                Bind(6, 72 + o, size=out_bytes), Bind(7, 73 + o), Bind(8, 74 + o)]
+
+    def upload(b, i, o):
+        for h, arr in ((70 + o, qs[i]), (71 + o, w.seq_lens), (73 + o, w.new_k), (74 + o, w.new_v)):
+            b.execute_buffer_write_bytes(h, 0, arr)
+
+    setup(be)
+    expected = []
+    for i in range(4):  # one step at a time, synchronous captures
+        upload(be, i, 0)
+        be.execute_kernel_dispatch("attention_paged_decode", binds(0))
+        expected.append(np.frombuffer(be.capture_buffer(72, 0, out_bytes), np.float32).copy())
+    b2 = CudaBackend(0)
+    try:
+        setup(b2)
+        outs = [torch.zeros(out_bytes, dtype=torch.uint8).pin_memory() for _ in range(4)]
+        for i in range(4):  # queued
+            o = 10 * (i & 1)
+            upload(b2, i, o)
+            b2.execute_kernel_dispatch("attention_paged_decode", binds(o))
+            b2.read_into_async(72 + o, 0, outs[i].data_ptr(), out_bytes)
+        b2.flush_queue()
+        for i in range(4):
+            assert np.array_equal(outs[i].numpy().view(np.float32), expected[i]), f"step {i}"
+    finally:
+        b2.close()
