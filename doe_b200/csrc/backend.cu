@@ -790,6 +790,9 @@ int doe_cuda_buffer_release(doe_cuda_ctx* ctx, uint64_t handle) {
   DOE_TRY(bind_device(ctx));
   DOE_TRY(sync_stream(ctx));
   cudaFree(it->second.ptr);
+  if (it->second.ev_written) cudaEventDestroy(it->second.ev_written);
+  if (it->second.ev_used) cudaEventDestroy(it->second.ev_used);
+  if (it->second.ev_read) cudaEventDestroy(it->second.ev_read);
   ctx->buffers.erase(it);
   return DOE_OK;
 }

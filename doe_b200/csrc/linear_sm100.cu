@@ -28,6 +28,8 @@
 // Every mbarrier wait is bounded; on timeout the kernel sets
 // DOE_DEVICE_ERR_TIMEOUT, the roles stop, copies and MMAs still in flight are
 // waited for (bounded) and TMEM is freed.  No cluster multicast.
+#include <atomic>
+
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -468,7 +470,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
 namespace {
 
 int num_sms() {
-  static int cached[64] = {0};
+  static std::atomic<int> cached[64];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     cudaGetLastError();
@@ -480,9 +482,9 @@ int num_sms() {
       cudaGetLastError();
       n = 148;
     }
-    cached[dev] = n;
+    cached[dev].store(n);
   }
-  return cached[dev];
+  return cached[dev].load();
 }
 
 // Workspace layout, the same for every shape so that calls of different
@@ -493,23 +495,28 @@ constexpr uint64_t kCountersBytes = kMaxTiles * 4;
 
 // Clusters of `size` linear CTAs that fit on the device at once (cached per
 // device and size); -1 with the op error set on failure.
+// The kernel's dynamic shared-memory limit, raised once per device.
+int set_smem_attr(int dev) {
+  static std::atomic<bool> done[64];
+  if (done[dev].load()) return DOE_OK;
+  int rc = cuda_status(cudaFuncSetAttribute(lin::linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            lin::kSmemBytes),
+                       "cudaFuncSetAttribute(linear)");
+  if (rc == DOE_OK) done[dev].store(true);
+  return rc;
+}
+
 int max_active_clusters(int size) {
-  static int cached[64][lin::kMaxCluster + 1];
-  static bool attr_set[64];
+  static std::atomic<int> cached[64][lin::kMaxCluster + 1];
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
     cudaGetLastError();
     set_op_error("doe_linear_bf16: no current device");
     return -1;
   }
-  if (cached[dev][size] != 0) return cached[dev][size] < 0 ? 0 : cached[dev][size];
-  if (!attr_set[dev]) {
-    if (cuda_status(cudaFuncSetAttribute(lin::linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         lin::kSmemBytes),
-                    "cudaFuncSetAttribute(linear)") != DOE_OK)
-      return -1;
-    attr_set[dev] = true;
-  }
+  const int have = cached[dev][size].load();
+  if (have != 0) return have < 0 ? 0 : have;
+  if (set_smem_attr(dev) != DOE_OK) return -1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)size);
   cfg.blockDim = dim3(lin::kThreads);
@@ -525,8 +532,8 @@ int max_active_clusters(int size) {
   if (cuda_status(cudaOccupancyMaxActiveClusters(&n, lin::linear_kernel, &cfg), "cudaOccupancyMaxActiveClusters") !=
       DOE_OK)
     return -1;
-  cached[dev][size] = n > 0 ? n : -2;  // -2: none fit (never chosen)
-  return cached[dev][size] < 0 ? 0 : cached[dev][size];
+  cached[dev][size].store(n > 0 ? n : -2);  // -2: none fit (never chosen)
+  return n > 0 ? n : 0;
 }
 
 }  // namespace
@@ -613,13 +620,15 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
     rc = encode_rows_map(&mx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, 1, batch, 64, lin::NB,
                          "doe_linear_bf16");
   if (rc != DOE_OK) return rc;
-  static bool attr_set = false;
-  if (!attr_set) {
-    rc = cuda_status(cudaFuncSetAttribute(lin::linear_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          lin::kSmemBytes),
-                     "cudaFuncSetAttribute(linear)");
+  {
+    int dev = 0;
+    rc = cuda_status(cudaGetDevice(&dev), "cudaGetDevice");
+    if (rc == DOE_OK && (dev < 0 || dev >= 64)) {
+      set_op_error("doe_linear_bf16: device ordinal %d beyond 63", dev);
+      rc = DOE_UNSUPPORTED;
+    }
+    if (rc == DOE_OK) rc = set_smem_attr(dev);
     if (rc != DOE_OK) return rc;
-    attr_set = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(ctas);

@@ -42,19 +42,24 @@ class TpPeers:
         handle = (C.c_ubyte * 64)()
         abi.check("doe_peer_buffer_create", lib.doe_peer_buffer_create(nbytes, C.byref(own), handle))
         self._own = own.value
-        handles = [None] * self.world
-        dist.all_gather_object(handles, bytes(handle), group=group)
         self._opened: list[int] = []
-        ptrs = []
-        for r, h in enumerate(handles):
-            if r == self.rank:
-                ptrs.append(self._own)
-                continue
-            p = C.c_void_p()
-            abi.check("doe_peer_buffer_open", lib.doe_peer_buffer_open((C.c_ubyte * 64).from_buffer_copy(h),
-                                                                       C.byref(p)))
-            self._opened.append(p.value)
-            ptrs.append(p.value)
+        self.slots = []
+        try:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            ptrs = []
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                p = C.c_void_p()
+                abi.check("doe_peer_buffer_open",
+                          lib.doe_peer_buffer_open((C.c_ubyte * 64).from_buffer_copy(h), C.byref(p)))
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+        except BaseException:
+            self.close()
+            raise
         self.struct = abi.TpPeers(self.rank, self.world,
                                   (C.c_void_p * abi.TP_MAX_RANKS)(*ptrs, *([None] * (abi.TP_MAX_RANKS - self.world))))
         # this rank's two partial slots as torch tensors (outputs of the linear layers)
