@@ -162,7 +162,8 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   return v;
 }
 
-template <bool INT8, int GROUP>
+// CAP: the score softcap is compiled in only where a launch asks for it
+template <bool INT8, int GROUP, bool CAP>
 __global__ void __launch_bounds__(kWarps * 32)
     paged_decode_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                         const PagedDecodeArgs a) {
@@ -417,8 +418,7 @@ __global__ void __launch_bounds__(kWarps * 32)
           sv = (sv - q1152) * (e ? __high2float(k2) : __low2float(k2));
         }
         // softcap (…wgsl:197-199): cap * tanh((q.k * scale) / cap), then log2 domain
-        const float xs = a.softcap > 0.0f ? a.softcap * tanhf(sv * a.scale / a.softcap) * kLog2e
-                                          : sv * a.scale_log2;
+        const float xs = CAP ? a.softcap * tanhf(sv * a.scale / a.softcap) * kLog2e : sv * a.scale_log2;
         x[nb][e] = valid[nb][e] ? xs : -INFINITY;
       }
     float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
@@ -671,20 +671,28 @@ template __global__ void combine_splits_kernel<true>(const CombineArgs);
 template __global__ void combine_splits_kernel<false>(const CombineArgs);
 
 // ---------------------------------------------------------------------------
-template <bool INT8, int GROUP>
-static int launch_one(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const PagedDecodeArgs& a, dim3 grid,
+template <bool INT8, int GROUP, bool CAP>
+static int launch_cap(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const PagedDecodeArgs& a, dim3 grid,
                       cudaStream_t st) {
   constexpr int smem = Ring<INT8>::kSmem;
   static bool attr = false;  // per instantiation
   if (!attr) {
-    int rc = cuda_status(cudaFuncSetAttribute(paged_decode_kernel<INT8, GROUP>,
+    int rc = cuda_status(cudaFuncSetAttribute(paged_decode_kernel<INT8, GROUP, CAP>,
                                               cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                          "cudaFuncSetAttribute(paged_decode)");
     if (rc != DOE_OK) return rc;
     attr = true;
   }
-  return cuda_status(launch_pdl(paged_decode_kernel<INT8, GROUP>, grid, dim3(kWarps * 32), smem, st, tm_k, tm_v, a),
-                     "paged_decode_kernel");
+  return cuda_status(
+      launch_pdl(paged_decode_kernel<INT8, GROUP, CAP>, grid, dim3(kWarps * 32), smem, st, tm_k, tm_v, a),
+      "paged_decode_kernel");
+}
+
+template <bool INT8, int GROUP>
+static int launch_one(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const PagedDecodeArgs& a, dim3 grid,
+                      cudaStream_t st) {
+  return a.softcap > 0.0f ? launch_cap<INT8, GROUP, true>(tm_k, tm_v, a, grid, st)
+                          : launch_cap<INT8, GROUP, false>(tm_k, tm_v, a, grid, st);
 }
 
 int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_heads,
