@@ -125,6 +125,34 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   }
 }
 
+// Two f32 lanes per instruction (sm_100 packed FP32): a * b + c and a + b,
+// each lane rounded as the scalar instruction would round it.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rc, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+      "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// max(a, b, c) in one instruction (sm_100), NaN handling as fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;\n" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 2^x with the SFU's approximate exp2 (max relative error ~2^-22); -inf -> +0.
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -371,13 +399,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 64; ++i)
           if (i >= key_lim) r[i] = __float_as_uint(-INFINITY);
       }
-      float mx[8];
+      // row max of the 64 scores: three-input max, four independent chains
+      float mx[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = __uint_as_float(r[i]);
+      for (int i = 0; i < 4; ++i) mx[i] = __uint_as_float(r[i]);
 #pragma unroll
-      for (int i = 8; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
-      float m_raw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                          fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int i = 4; i < 64; i += 2)
+        mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
+      float m_raw = fmax3(fmax3(mx[0], mx[1], mx[2]), mx[3], -INFINITY);
       // the pair's agreed row max; the barrier also proves both halves have
       // read their S columns before either overwrites S with P
       float* xb = xchg + (j & 1) * 512;
@@ -390,24 +419,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float corr = (grow && m_used != -INFINITY) ? ex2(m_used - m_new) : 1.0f;
       const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
       if (!ok) continue;  // barriers above were kept in step; nothing else to do
-      // p = 2^(s * scale * log2e - m): one FFMA + one MUFU.EX2 per score
-      float sums[8];
+      // p = 2^(s * scale * log2e - m): one packed FFMA per two scores and one
+      // MUFU.EX2 per score.  Each half's row sum is taken after its P store is
+      // issued, so the adds overlap the store's latency.
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(neg_m, neg_m);
+      float2 s2[4];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sums[i] = 0.0f;
+      for (int i = 0; i < 4; ++i) s2[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const float x0 = fmaf(__uint_as_float(r[c * 32 + 2 * e]), a.scale_log2, neg_m);
-          const float x1 = fmaf(__uint_as_float(r[c * 32 + 2 * e + 1]), a.scale_log2, neg_m);
-          const float p0 = ex2(x0);
-          const float p1 = ex2(x1);
-          sums[e & 7] += p0 + p1;
+          const int i = c * 32 + 2 * e;
+          const float2 xx = ffma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sc2, nm2);
+          const float p0 = ex2(xx.x);
+          const float p1 = ex2(xx.y);
+          r[i] = __float_as_uint(p0);
+          r[i + 1] = __float_as_uint(p1);
           w[e] = pack_half2(p0, p1);
         }
         tmem_st16(lane_base + p_col + c * 16, w);
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int i = c * 32 + 2 * e;
+          s2[e & 3] = fadd2(s2[e & 3], make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])));
+        }
       }
+      const float2 s4 = fadd2(fadd2(s2[0], s2[1]), fadd2(s2[2], s2[3]));
+      const float sum = s4.x + s4.y;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // the running max rose by more than 2^8: rescale this half-row of O
         // (quiescent: S_x(j)'s commit covered PV_x(j-1), and PV_x(j) waits for
@@ -426,7 +466,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(P_FULL_A + x));
-      const float sum = ((sums[0] + sums[1]) + (sums[2] + sums[3])) + ((sums[4] + sums[5]) + (sums[6] + sums[7]));
       l = l * corr + sum;  // this half's share of the row sum
       m_used = m_new;
     }
