@@ -40,6 +40,18 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
+def clock_max_mhz(index: int = 0):
+    """The SM's maximum clock from NVML (None when NVML is unavailable)."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        return float(pynvml.nvmlDeviceGetMaxClockInfo(pynvml.nvmlDeviceGetHandleByIndex(index),
+                                                      pynvml.NVML_CLOCK_SM))
+    except Exception:
+        return None
+
+
 def peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -299,6 +311,55 @@ def measure_f32(steps, warmup, world, pk):
     ms, = max_over_ranks(world, [float(np.mean(times))])
     return {"us_per_step": ms * 1e3, "gbs": world * d.bytes_per_step / (ms / 1e3) / 1e9,
             "bytes_per_step": d.bytes_per_step, "l2": "flushed (256 MB write) between steps"}
+
+
+def measure_ep(steps, warmup, world, pk):
+    """The ORT EP's basic f32 operators at HBM-sized shapes (inputs + outputs
+    larger than L2): Softmax and LayerNorm over [8192, 4096], Gelu over 64 Mi
+    elements, Add over 32 Mi, and a 4096^3 MatMul against the FP32 pipe's
+    nominal peak (SMs x 128 lanes x 2 flop x max SM clock)."""
+    import torch
+
+    from doe_b200 import ort_ep
+
+    g = torch.Generator(device="cuda").manual_seed(6)
+    rnd = lambda *shape: torch.randn(*shape, device="cuda", generator=g)
+    x = rnd(8192, 4096)
+    scale = rnd(4096)
+    u = rnd(64 << 20)
+    a2, b2 = rnd(32 << 20), rnd(32 << 20)
+    ma, mb = rnd(4096, 4096), rnd(4096, 4096)
+    cases = {
+        "softmax": (lambda: ort_ep.execute("softmax", x), 2 * x.numel() * 4, None),
+        "layernorm": (lambda: ort_ep.execute("layernorm", x, scale), 2 * x.numel() * 4, None),
+        "gelu": (lambda: ort_ep.execute("gelu", u), 2 * u.numel() * 4, None),
+        "add": (lambda: ort_ep.execute("add", a2, b2), 3 * a2.numel() * 4, None),
+        "matmul": (lambda: ort_ep.execute("matmul", ma, mb), 3 * 4096 * 4096 * 4, 2 * 4096 ** 3),
+    }
+    props = torch.cuda.get_device_properties(0)
+    clk = clock_max_mhz() or 1965.0
+    fp32_peak = props.multi_processor_count * 128 * 2 * clk * 1e6 / 1e12
+    out = {"config": "ORT EP basic f32 ops: softmax / layernorm [8192, 4096], gelu 64Mi, add 32Mi, "
+                     "matmul 4096^3", "l2": "each step's inputs + outputs exceed L2"}
+    for name, (fn, nbytes, flops) in cases.items():
+        times = []
+        for i in range(warmup + steps):
+            ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev[0].record()
+            fn()
+            ev[1].record()
+            torch.cuda.synchronize()
+            if i >= warmup:
+                times.append(ev[0].elapsed_time(ev[1]))
+        ms, = max_over_ranks(world, [float(np.mean(times))])
+        r = {"ms": ms, "gbs": nbytes / (ms / 1e3) / 1e9}
+        r["hbm_frac"] = r["gbs"] / pk["hbm_gbs"]
+        if flops:
+            r["tflops"] = flops / (ms / 1e3) / 1e12
+            r["fp32_frac"] = r["tflops"] / fp32_peak
+            r["fp32_peak_tflops"] = fp32_peak
+        out[name] = r
+    return out
 
 
 def measure_prefill(steps, warmup, world, pk, rank=0):
@@ -605,7 +666,7 @@ def main():
     ap.add_argument("--no-extras", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--only", choices=["all", "headline", "prefill", "f32", "int8", "append", "decoder",
-                                       "linear"],
+                                       "linear", "ep"],
                     default="all",
                     help="time one workload only (no e2e or CPU leg): headline = config 3, "
                          "append = config 4b chunk quantise-append, decoder = config 5, "
@@ -628,8 +689,10 @@ def main():
     pk = peaks()
     from doe_b200 import workloads
 
-    if args.only in ("prefill", "f32", "int8", "append", "decoder", "linear"):
-        if args.only == "linear":
+    if args.only in ("prefill", "f32", "int8", "append", "decoder", "linear", "ep"):
+        if args.only == "ep":
+            r = measure_ep(args.steps, args.warmup, world, pk)
+        elif args.only == "linear":
             r = measure_linear(args.steps, args.warmup, world, pk, args.linear_shape)
         elif args.only == "decoder":
             r = measure_decoder(args.steps, args.warmup, world, rank, pk)
@@ -683,6 +746,11 @@ def main():
             extras["prefill"] = {"error": str(e)[:300]}
         torch.cuda.empty_cache()
         extras["decoder"] = measure_decoder(10, 3, world, rank, pk)
+        torch.cuda.empty_cache()
+        try:
+            extras["ort_ep"] = measure_ep(5, 3, world, pk)
+        except Exception as e:  # reported, never hidden
+            extras["ort_ep"] = {"error": str(e)[:300]}
         torch.cuda.empty_cache()
 
     e2e = None

@@ -84,6 +84,9 @@ DECODE_OUT_BF16 = 0x1
 DECODE_COUNTERS_ZEROED = 0x2
 LINEAR_STORE, LINEAR_SWIGLU = 0, 1
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
+EP_IDENTITY, EP_RELU, EP_SIGMOID, EP_TANH, EP_GELU = 0, 1, 2, 3, 4
+EP_ADD, EP_ADD_RELU = 0, 1
+EP_MATMUL_RELU = 0x1
 
 
 TP_MAX_RANKS = 8
@@ -154,6 +157,14 @@ SIGNATURES = {
     "doe_kv_read_dense": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _U32, _U32, _LP]),
     "doe_rope_f32": (_I, [_P, _P, _U32, _U32, _U32, _U32, _LP]),
     "doe_rmsnorm_bf16": (_I, [_P, _P, _F, _P, _U32, _U32, _LP]),
+    "doe_ep_unary_f32": (_I, [_U32, _P, _P, _U64, _LP]),
+    "doe_ep_binary_f32": (_I, [_U32, _P, _P, _P, _U64, _LP]),
+    "doe_ep_softmax_f32": (_I, [_P, _P, _U64, _U32, _LP]),
+    "doe_ep_layernorm_f32": (_I, [_P, _P, _F, _P, _U64, _U32, _LP]),
+    "doe_ep_concat_f32": (_I, [_P, _P, _P, _U64, _U64, _U64, _U64, _LP]),
+    "doe_ep_matmul_f32": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _LP]),
+    "doe_ep_gemm_relu_gemm_workspace_bytes": (_U64, [_U32, _U32]),
+    "doe_ep_gemm_relu_gemm_f32": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _LP]),
     "doe_linear_workspace_bytes": (_U64, [_U32, _U32]),
     "doe_linear_bf16": (_I, [_P, _P, _U32, _U32, _U32, C.POINTER(LinearOut), _LP]),
     "doe_tp_buffer_bytes": (_U64, [_U32, _U32]),

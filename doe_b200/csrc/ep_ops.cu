@@ -1,0 +1,333 @@
+// ep_ops.cu -- the ONNX Runtime plugin EP's basic f32 operators on the GPU.
+//
+// The reference EP computes these on the host, one node at a time
+// (runtime/bridge/onnxruntime-ep/src/doe_ort_ep.cc:1899-2401).  Here each is a
+// kernel on device tensors, so an ONNX graph whose nodes the EP claims stays
+// in HBM between nodes:
+//   element-wise  Identity, Relu, Sigmoid, Tanh, Gelu (erf form)   :1899-2017
+//                 Add, AddRelu                                      :1933,2380
+//   rows          Softmax over the last axis (max-shifted exp, then
+//                 multiply by 1 / sum; sum 0 -> 0)                  :2019-2058
+//                 LayerNormalization over the last axis, scale only
+//                 ((x - mean) * 1/sqrt(var + eps) * scale)          :2060-2106
+//   Concat        two inputs along one axis                         :2108-2163
+//   MatMul        rank-2 f32 [M,K] x [K,N], optionally + an addend of
+//                 the output's shape (Gemm, MatMulAdd) and Relu
+//                 (MatMulAddRelu); GemmReluGemm is two of them       :2165-2378
+// Everything is f32 with f32 accumulation.  The matrix product runs on the
+// FP32 pipe: the tensor cores' f32-input form (TF32) keeps 10 mantissa bits,
+// which misses the 1e-5 relative agreement the reference's f32 loops define.
+// Sums are reduced in a different order than the reference's left folds
+// (tree reductions, FMA in the product), within that tolerance.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace doe {
+namespace ep {
+
+constexpr int kThreads = 256;
+
+template <int OP>
+__device__ __forceinline__ float unary(float v) {
+  if constexpr (OP == DOE_EP_RELU) return v < 0.0f ? 0.0f : v;
+  else if constexpr (OP == DOE_EP_SIGMOID) return 1.0f / (1.0f + expf(-v));
+  else if constexpr (OP == DOE_EP_TANH) return tanhf(v);
+  else if constexpr (OP == DOE_EP_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+  else return v;  // Identity
+}
+
+template <int OP>
+__device__ __forceinline__ float binary(float a, float b) {
+  const float s = a + b;
+  if constexpr (OP == DOE_EP_ADD_RELU) return s < 0.0f ? 0.0f : s;
+  else return s;
+}
+
+// y[i] = f(x[i]); VEC: float4 over n / 4 elements (all pointers 16-byte
+// aligned), the scalar tail by the first threads.
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(kThreads) unary_kernel(const float* __restrict__ x, float* y, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if constexpr (VEC) {
+    const uint64_t n4 = n / 4;
+    for (uint64_t v = i; v < n4; v += stride) {
+      float4 t = reinterpret_cast<const float4*>(x)[v];
+      t.x = unary<OP>(t.x);
+      t.y = unary<OP>(t.y);
+      t.z = unary<OP>(t.z);
+      t.w = unary<OP>(t.w);
+      reinterpret_cast<float4*>(y)[v] = t;
+    }
+    i += n4 * 4;
+  }
+  for (; i < n; i += stride) y[i] = unary<OP>(x[i]);
+}
+
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(kThreads)
+    binary_kernel(const float* __restrict__ a, const float* __restrict__ b, float* y, uint64_t n) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if constexpr (VEC) {
+    const uint64_t n4 = n / 4;
+    for (uint64_t v = i; v < n4; v += stride) {
+      const float4 p = reinterpret_cast<const float4*>(a)[v];
+      const float4 q = reinterpret_cast<const float4*>(b)[v];
+      reinterpret_cast<float4*>(y)[v] =
+          make_float4(binary<OP>(p.x, q.x), binary<OP>(p.y, q.y), binary<OP>(p.z, q.z), binary<OP>(p.w, q.w));
+    }
+    i += n4 * 4;
+  }
+  for (; i < n; i += stride) y[i] = binary<OP>(a[i], b[i]);
+}
+
+// Block-wide reduction of one value per thread (sum or max); every thread
+// gets the result.  `red` holds kThreads / 32 partials; the leading barrier
+// lets a caller reuse it back to back.
+template <bool MAX>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MAX ? fmaxf(v, w) : v + w;
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = red[0];
+#pragma unroll
+  for (int w = 1; w < kThreads / 32; ++w) v = MAX ? fmaxf(v, red[w]) : v + red[w];
+  return v;
+}
+
+// One CTA per row (grid-stride over rows).  CACHE: the row is read from HBM
+// once into shared memory (cols floats); otherwise each pass re-reads it.
+// SOFTMAX: y = exp(x - max) * (sum != 0 ? 1 / sum : 0)
+// else:    y = (x - mean) * (1 / sqrt(var + eps)) * scale, var = mean((x - mean)^2)
+template <bool SOFTMAX, bool CACHE>
+__global__ void __launch_bounds__(kThreads)
+    rows_kernel(const float* x, const float* __restrict__ scale, float eps, float* y, uint64_t rows, uint32_t cols) {
+  extern __shared__ float srow[];
+  __shared__ float red[kThreads / 32];
+  const float inv_cols = 1.0f / (float)cols;
+  for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const float* xr = x + row * cols;
+    float* yr = y + row * cols;
+    auto at = [&](uint32_t i) { return CACHE ? srow[i] : xr[i]; };
+    // pass 1: max (softmax) or sum (layer norm), caching the row
+    float acc = SOFTMAX ? -INFINITY : 0.0f;
+    for (uint32_t i = threadIdx.x; i < cols; i += kThreads) {
+      const float v = xr[i];
+      if (CACHE) srow[i] = v;
+      acc = SOFTMAX ? fmaxf(acc, v) : acc + v;
+    }
+    const float first = block_reduce<SOFTMAX>(acc, red);
+    // pass 2: sum of exp (softmax) or of squared deviations (layer norm)
+    const float mean = SOFTMAX ? 0.0f : first * inv_cols;
+    acc = 0.0f;
+    for (uint32_t i = threadIdx.x; i < cols; i += kThreads) {
+      const float v = at(i);
+      if (SOFTMAX) {
+        acc += expf(v - first);
+      } else {
+        const float d = v - mean;
+        acc += d * d;
+      }
+    }
+    const float second = block_reduce<false>(acc, red);
+    // pass 3: the output row
+    if (SOFTMAX) {
+      const float inv = second != 0.0f ? 1.0f / second : 0.0f;
+      for (uint32_t i = threadIdx.x; i < cols; i += kThreads) yr[i] = expf(at(i) - first) * inv;
+    } else {
+      const float inv_std = 1.0f / sqrtf(second * inv_cols + eps);
+      for (uint32_t i = threadIdx.x; i < cols; i += kThreads) yr[i] = (at(i) - mean) * inv_std * scale[i];
+    }
+    __syncthreads();  // the cached row is rewritten by the next row
+  }
+}
+
+// y[o, 0:a_axis*inner] = a[o, :], y[o, a_axis*inner:] = b[o, :]
+__global__ void __launch_bounds__(kThreads)
+    concat_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y, uint64_t outer,
+                  uint64_t a_run, uint64_t b_run) {
+  const uint64_t run = a_run + b_run, total = outer * run;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const uint64_t o = i / run, r = i - o * run;
+    y[i] = r < a_run ? a[o * a_run + r] : b[o * b_run + (r - a_run)];
+  }
+}
+
+// C[M,N] = A[M,K] B[K,N] (+ addend[M,N]) (then Relu), all row-major f32.
+// 128 x 128 output tile per CTA, 256 threads with 8 x 8 outputs each, K
+// steps of 8 through two shared-memory stages (A stored k-major so both
+// operands are read as float4 rows).  Loads outside the matrices read 0;
+// each output is one FMA chain over k in order.
+constexpr int TM = 128, TN = 128, TK = 8;
+
+__global__ void __launch_bounds__(kThreads)
+    matmul_kernel(const float* __restrict__ A, const float* __restrict__ B, const float* __restrict__ addend,
+                  float* __restrict__ C, int M, int K, int N, int relu) {
+  __shared__ __align__(16) float As[2][TK][TM];
+  __shared__ __align__(16) float Bs[2][TK][TN];
+  const int tid = threadIdx.x;
+  const int m0 = blockIdx.y * TM, n0 = blockIdx.x * TN;
+  const int tr = tid / 16, tc = tid % 16;  // 16 x 16 threads, 8 x 8 outputs each
+  // loader mapping: A tile 128 x 8 -> each thread 4 elements of one row;
+  // B tile 8 x 128 -> each thread 4 consecutive columns of one k row
+  const int a_row = tid / 2, a_k = (tid % 2) * 4;
+  const int b_k = tid / 32, b_col = (tid % 32) * 4;
+  float ra[4], rb[4];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int gm = m0 + a_row, gk = k0 + a_k + i;
+      ra[i] = (gm < M && gk < K) ? A[(size_t)gm * K + gk] : 0.0f;
+      const int gk2 = k0 + b_k, gn = n0 + b_col + i;
+      rb[i] = (gk2 < K && gn < N) ? B[(size_t)gk2 * N + gn] : 0.0f;
+    }
+  };
+  auto stash = [&](int s) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) As[s][a_k + i][a_row] = ra[i];
+    *reinterpret_cast<float4*>(&Bs[s][b_k][b_col]) = make_float4(rb[0], rb[1], rb[2], rb[3]);
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+
+  const int steps = (K + TK - 1) / TK;
+  fetch(0);
+  stash(0);
+  __syncthreads();
+  for (int s = 0; s < steps; ++s) {
+    const int cur = s & 1;
+    if (s + 1 < steps) fetch((s + 1) * TK);  // global loads in flight during the math
+#pragma unroll
+    for (int kk = 0; kk < TK; ++kk) {
+      // rows tr*4 .. +3 and 64 + tr*4 .. +3; columns tc*4 .. +3 and 64 + tc*4 .. +3
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][kk][tr * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][kk][64 + tr * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][kk][tc * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][kk][64 + tc * 4]);
+      const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    if (s + 1 < steps) {
+      stash(cur ^ 1);  // the other stage was last read before the previous barrier
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int gm = m0 + (i < 4 ? tr * 4 + i : 64 + tr * 4 + (i - 4));
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int gn = n0 + (j < 4 ? tc * 4 + j : 64 + tc * 4 + (j - 4));
+      if (gn >= N) continue;
+      const size_t o = (size_t)gm * N + gn;
+      float v = acc[i][j];
+      if (addend != nullptr) v += addend[o];
+      if (relu) v = v < 0.0f ? 0.0f : v;
+      C[o] = v;
+    }
+  }
+}
+
+unsigned grid_for(uint64_t work, int per_block) {
+  const uint64_t want = (work + per_block - 1) / per_block;
+  const uint64_t cap = (uint64_t)num_sms() * 8;
+  return (unsigned)(want < 1 ? 1 : (want < cap ? want : cap));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+template <int OP>
+int launch_unary_op(const float* x, float* y, uint64_t n, cudaStream_t s) {
+  const bool vec = aligned16(x) && aligned16(y);
+  const unsigned g = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+  if (vec) unary_kernel<OP, true><<<g, kThreads, 0, s>>>(x, y, n);
+  else unary_kernel<OP, false><<<g, kThreads, 0, s>>>(x, y, n);
+  return cuda_status(cudaGetLastError(), "ep unary_kernel");
+}
+
+template <int OP>
+int launch_binary_op(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s) {
+  const bool vec = aligned16(a) && aligned16(b) && aligned16(y);
+  const unsigned g = grid_for(vec ? (n + 3) / 4 : n, kThreads);
+  if (vec) binary_kernel<OP, true><<<g, kThreads, 0, s>>>(a, b, y, n);
+  else binary_kernel<OP, false><<<g, kThreads, 0, s>>>(a, b, y, n);
+  return cuda_status(cudaGetLastError(), "ep binary_kernel");
+}
+
+// Rows up to this many floats are cached in shared memory (one read of x).
+constexpr uint32_t kMaxCachedCols = 48 * 1024 / 4;
+
+template <bool SOFTMAX>
+int launch_rows(const float* x, const float* scale, float eps, float* y, uint64_t rows, uint32_t cols,
+                cudaStream_t s) {
+  const unsigned g = grid_for(rows, 1);
+  if (cols <= kMaxCachedCols)
+    rows_kernel<SOFTMAX, true><<<g, kThreads, cols * sizeof(float), s>>>(x, scale, eps, y, rows, cols);
+  else
+    rows_kernel<SOFTMAX, false><<<g, kThreads, 0, s>>>(x, scale, eps, y, rows, cols);
+  return cuda_status(cudaGetLastError(), SOFTMAX ? "ep softmax rows_kernel" : "ep layernorm rows_kernel");
+}
+
+}  // namespace ep
+
+int launch_ep_unary(uint32_t op, const float* x, float* y, uint64_t n, const doe_launch* l) {
+  const cudaStream_t s = static_cast<cudaStream_t>(l->stream);
+  switch (op) {
+    case DOE_EP_IDENTITY: return ep::launch_unary_op<DOE_EP_IDENTITY>(x, y, n, s);
+    case DOE_EP_RELU: return ep::launch_unary_op<DOE_EP_RELU>(x, y, n, s);
+    case DOE_EP_SIGMOID: return ep::launch_unary_op<DOE_EP_SIGMOID>(x, y, n, s);
+    case DOE_EP_TANH: return ep::launch_unary_op<DOE_EP_TANH>(x, y, n, s);
+    case DOE_EP_GELU: return ep::launch_unary_op<DOE_EP_GELU>(x, y, n, s);
+    default: return DOE_INVALID_ARGUMENT;
+  }
+}
+
+int launch_ep_binary(uint32_t op, const float* a, const float* b, float* y, uint64_t n, const doe_launch* l) {
+  const cudaStream_t s = static_cast<cudaStream_t>(l->stream);
+  switch (op) {
+    case DOE_EP_ADD: return ep::launch_binary_op<DOE_EP_ADD>(a, b, y, n, s);
+    case DOE_EP_ADD_RELU: return ep::launch_binary_op<DOE_EP_ADD_RELU>(a, b, y, n, s);
+    default: return DOE_INVALID_ARGUMENT;
+  }
+}
+
+int launch_ep_softmax(const float* x, float* y, uint64_t rows, uint32_t cols, const doe_launch* l) {
+  return ep::launch_rows<true>(x, nullptr, 0.0f, y, rows, cols, static_cast<cudaStream_t>(l->stream));
+}
+
+int launch_ep_layernorm(const float* x, const float* scale, float eps, float* y, uint64_t rows, uint32_t cols,
+                        const doe_launch* l) {
+  return ep::launch_rows<false>(x, scale, eps, y, rows, cols, static_cast<cudaStream_t>(l->stream));
+}
+
+int launch_ep_concat(const float* a, const float* b, float* y, uint64_t outer, uint64_t a_run, uint64_t b_run,
+                     const doe_launch* l) {
+  const unsigned g = ep::grid_for(outer * (a_run + b_run), ep::kThreads);
+  ep::concat_kernel<<<g, ep::kThreads, 0, static_cast<cudaStream_t>(l->stream)>>>(a, b, y, outer, a_run, b_run);
+  return cuda_status(cudaGetLastError(), "ep concat_kernel");
+}
+
+int launch_ep_matmul(const float* a, const float* b, const float* addend, float* y, uint32_t m, uint32_t k,
+                     uint32_t n, bool relu, const doe_launch* l) {
+  const dim3 grid((n + ep::TN - 1) / ep::TN, (m + ep::TM - 1) / ep::TM);
+  ep::matmul_kernel<<<grid, ep::kThreads, 0, static_cast<cudaStream_t>(l->stream)>>>(a, b, addend, y, (int)m,
+                                                                                       (int)k, (int)n, relu ? 1 : 0);
+  return cuda_status(cudaGetLastError(), "ep matmul_kernel");
+}
+
+}  // namespace doe

@@ -85,6 +85,18 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
                   const doe_linear_out* out, const doe_launch* launch);
 int launch_rmsnorm(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
                    const doe_launch* launch);
+int num_sms();  // of the current device, cached per device
+
+// ORT plugin EP basic operators (ep_ops.cu)
+int launch_ep_unary(uint32_t op, const float* x, float* y, uint64_t n, const doe_launch* launch);
+int launch_ep_binary(uint32_t op, const float* a, const float* b, float* y, uint64_t n, const doe_launch* launch);
+int launch_ep_softmax(const float* x, float* y, uint64_t rows, uint32_t cols, const doe_launch* launch);
+int launch_ep_layernorm(const float* x, const float* scale, float eps, float* y, uint64_t rows, uint32_t cols,
+                        const doe_launch* launch);
+int launch_ep_concat(const float* a, const float* b, float* y, uint64_t outer, uint64_t a_run, uint64_t b_run,
+                     const doe_launch* launch);
+int launch_ep_matmul(const float* a, const float* b, const float* addend, float* y, uint32_t m, uint32_t k,
+                     uint32_t n, bool relu, const doe_launch* launch);
 uint64_t tp_buffer_bytes(uint32_t rows, uint32_t cols);
 float* tp_slot_ptr(void* buffer, uint32_t slot, uint32_t rows, uint32_t cols);
 int launch_tp_reduce_rmsnorm(const doe_tp_peers* p, uint32_t slot, const void* gamma, float eps, float* h_out,

@@ -467,8 +467,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
 }  // namespace lin
 
 // ---- host -----------------------------------------------------------------
-namespace {
-
+// SM count of the current device (cached per device).
 int num_sms() {
   static std::atomic<int> cached[64];
   int dev = 0;
@@ -486,6 +485,9 @@ int num_sms() {
   }
   return cached[dev].load();
 }
+
+namespace {
+
 
 // Workspace layout, the same for every shape so that calls of different
 // sizes can share one workspace: tile counters at the front (room for

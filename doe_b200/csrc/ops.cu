@@ -366,6 +366,114 @@ int doe_rmsnorm_bf16(const float* x, const void* gamma, float eps, void* out, ui
   return launch_rmsnorm(x, gamma, eps, out, rows, cols, launch_or_default(launch));
 }
 
+// ---- ORT plugin EP basic operators (doe_ort_ep.cc:1899-2401) -------------
+namespace {
+
+bool overlaps(const void* p, uint64_t p_bytes, const void* q, uint64_t q_bytes) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(p), b = reinterpret_cast<uintptr_t>(q);
+  return p_bytes != 0 && q_bytes != 0 && a < b + q_bytes && b < a + p_bytes;
+}
+
+constexpr uint64_t kMaxElems = 1ull << 40;  // a sanity bound on element counts (4 TiB of f32)
+
+}  // namespace
+
+int doe_ep_unary_f32(uint32_t op, const float* x, float* y, uint64_t n, const doe_launch* launch) {
+  if (op > DOE_EP_GELU) return invalid("doe_ep_unary_f32: unknown op %u", op);
+  if (n == 0) return DOE_OK;
+  if (!x || !y) return invalid("doe_ep_unary_f32: null pointer");
+  if (n > kMaxElems) return invalid("doe_ep_unary_f32: n too large");
+  if (x != y && overlaps(x, n * 4, y, n * 4)) return invalid("doe_ep_unary_f32: x and y partly overlap");
+  return launch_ep_unary(op, x, y, n, launch_or_default(launch));
+}
+
+int doe_ep_binary_f32(uint32_t op, const float* a, const float* b, float* y, uint64_t n,
+                      const doe_launch* launch) {
+  if (op > DOE_EP_ADD_RELU) return invalid("doe_ep_binary_f32: unknown op %u", op);
+  if (n == 0) return DOE_OK;
+  if (!a || !b || !y) return invalid("doe_ep_binary_f32: null pointer");
+  if (n > kMaxElems) return invalid("doe_ep_binary_f32: n too large");
+  if ((a != y && overlaps(a, n * 4, y, n * 4)) || (b != y && overlaps(b, n * 4, y, n * 4)))
+    return invalid("doe_ep_binary_f32: an input partly overlaps y");
+  return launch_ep_binary(op, a, b, y, n, launch_or_default(launch));
+}
+
+int doe_ep_softmax_f32(const float* x, float* y, uint64_t rows, uint32_t cols, const doe_launch* launch) {
+  if (rows == 0 || cols == 0) return DOE_OK;  // ExecuteSoftmax returns early for an empty axis
+  if (!x || !y) return invalid("doe_ep_softmax_f32: null pointer");
+  if (rows > kMaxElems / cols) return invalid("doe_ep_softmax_f32: too many elements");
+  if (x != y && overlaps(x, rows * cols * 4, y, rows * cols * 4))
+    return invalid("doe_ep_softmax_f32: x and y partly overlap");
+  return launch_ep_softmax(x, y, rows, cols, launch_or_default(launch));
+}
+
+int doe_ep_layernorm_f32(const float* x, const float* scale, float epsilon, float* y, uint64_t rows,
+                         uint32_t cols, const doe_launch* launch) {
+  if (rows == 0 || cols == 0) return DOE_OK;
+  if (!x || !scale || !y) return invalid("doe_ep_layernorm_f32: null pointer");
+  if (!(epsilon >= 0.0f)) return invalid("doe_ep_layernorm_f32: epsilon must be >= 0");
+  if (rows > kMaxElems / cols) return invalid("doe_ep_layernorm_f32: too many elements");
+  if (x != y && overlaps(x, rows * cols * 4, y, rows * cols * 4))
+    return invalid("doe_ep_layernorm_f32: x and y partly overlap");
+  if (overlaps(scale, (uint64_t)cols * 4, y, rows * cols * 4))
+    return invalid("doe_ep_layernorm_f32: scale overlaps y");
+  return launch_ep_layernorm(x, scale, epsilon, y, rows, cols, launch_or_default(launch));
+}
+
+int doe_ep_concat_f32(const float* a, const float* b, float* y, uint64_t outer, uint64_t a_axis, uint64_t b_axis,
+                      uint64_t inner, const doe_launch* launch) {
+  if (a_axis > kMaxElems || b_axis > kMaxElems || inner > kMaxElems || outer > kMaxElems)
+    return invalid("doe_ep_concat_f32: dimension too large");
+  const uint64_t a_run = a_axis * inner, b_run = b_axis * inner;
+  if (a_run > kMaxElems || b_run > kMaxElems) return invalid("doe_ep_concat_f32: too many elements");
+  if (outer == 0 || a_run + b_run == 0) return DOE_OK;
+  if (outer > kMaxElems / (a_run + b_run)) return invalid("doe_ep_concat_f32: too many elements");
+  if (!y || (a_run && !a) || (b_run && !b)) return invalid("doe_ep_concat_f32: null pointer");
+  const uint64_t yb = outer * (a_run + b_run) * 4;
+  if (overlaps(a, outer * a_run * 4, y, yb) || overlaps(b, outer * b_run * 4, y, yb))
+    return invalid("doe_ep_concat_f32: y overlaps an input");
+  return launch_ep_concat(a, b, y, outer, a_run, b_run, launch_or_default(launch));
+}
+
+int doe_ep_matmul_f32(const float* a, const float* b, const float* addend, float* y, uint32_t m, uint32_t k,
+                      uint32_t n, uint32_t flags, const doe_launch* launch) {
+  if (flags & ~DOE_EP_MATMUL_RELU) return invalid("doe_ep_matmul_f32: unknown flags %#x", flags);
+  if (m > 0x7fffffffu || k > 0x7fffffffu || n > 0x7fffffffu)
+    return invalid("doe_ep_matmul_f32: m, k and n must be below 2^31");
+  if (m == 0 || n == 0) return DOE_OK;
+  if ((m + 127u) / 128u > 65535u) return invalid("doe_ep_matmul_f32: m above 65535 * 128");
+  if (!y || (k && (!a || !b))) return invalid("doe_ep_matmul_f32: null pointer");
+  if ((uint64_t)m > (1ull << 62) / ((uint64_t)n * 4)) return invalid("doe_ep_matmul_f32: output too large");
+  const uint64_t yb = (uint64_t)m * n * 4;
+  if (overlaps(a, (uint64_t)m * k * 4, y, yb) || overlaps(b, (uint64_t)k * n * 4, y, yb))
+    return invalid("doe_ep_matmul_f32: y overlaps a or b");
+  if (addend && addend != y && overlaps(addend, yb, y, yb))
+    return invalid("doe_ep_matmul_f32: addend partly overlaps y");
+  return launch_ep_matmul(a, b, addend, y, m, k, n, (flags & DOE_EP_MATMUL_RELU) != 0, launch_or_default(launch));
+}
+
+uint64_t doe_ep_gemm_relu_gemm_workspace_bytes(uint32_t batch, uint32_t hidden) {
+  return ((uint64_t)batch * hidden * 4 + 255) & ~uint64_t(255);
+}
+
+int doe_ep_gemm_relu_gemm_f32(const float* x, const float* w1, const float* b1, const float* w2, const float* b2,
+                              float* y, uint32_t batch, uint32_t in_dim, uint32_t hidden, uint32_t out_dim,
+                              const doe_launch* launch) {
+  const doe_launch* l = launch_or_default(launch);
+  if (batch == 0 || out_dim == 0) return DOE_OK;
+  if (!b2 || !y || (hidden && (!b1 || !w2)) || (hidden && in_dim && (!x || !w1)))
+    return invalid("doe_ep_gemm_relu_gemm_f32: null pointer");
+  const uint64_t need = doe_ep_gemm_relu_gemm_workspace_bytes(batch, hidden);
+  if (hidden && (!l->workspace || l->workspace_bytes < need))
+    return invalid("doe_ep_gemm_relu_gemm_f32: the hidden activations need a workspace of %llu bytes",
+                   (unsigned long long)need);
+  float* h = static_cast<float*>(l->workspace);
+  int rc = DOE_OK;
+  if (hidden) rc = doe_ep_matmul_f32(x, w1, b1, h, batch, in_dim, hidden, DOE_EP_MATMUL_RELU, l);
+  if (rc == DOE_OK) rc = doe_ep_matmul_f32(h, w2, b2, y, batch, hidden, out_dim, 0, l);
+  return rc;
+}
+
 uint64_t doe_linear_workspace_bytes(uint32_t n_out, uint32_t k) { return linear_workspace(n_out, k); }
 
 uint64_t doe_tp_buffer_bytes(uint32_t rows, uint32_t cols) { return tp_buffer_bytes(rows, cols); }

@@ -491,6 +491,66 @@ int doe_attention_decode_f32_noalloc(const float* q, const float* k_cache,
                                      uint32_t kv_len, float scale, void* stream);
 
 /* ======================================================================== */
+/* ONNX Runtime plugin EP basic operators (f32), on device tensors.  Each    */
+/* replaces one of the EP's host compute kernels                            */
+/* (runtime/bridge/onnxruntime-ep/src/doe_ort_ep.cc), with the same         */
+/* arithmetic in f32; reductions may sum in another order (agreement with   */
+/* the host loops is within 1e-5 * max(|ref|, 1)).  Tensors are dense and    */
+/* row-major; element-wise and row ops may run in place (y == x).  Shape    */
+/* rules the EP checks before Compute (ValidateSameRuntimeShape,           */
+/* ValidateRuntimeMatMulShape, doe_ort_ep.cc:1864-1897) are the caller's;   */
+/* sizes that cannot be valid are rejected with DOE_INVALID_ARGUMENT.       */
+/* ======================================================================== */
+#define DOE_EP_IDENTITY 0u /* ExecuteIdentity  :1919  y = x                 */
+#define DOE_EP_RELU 1u     /* ExecuteRelu      :1955  y = x < 0 ? 0 : x     */
+#define DOE_EP_SIGMOID 2u  /* ExecuteSigmoid   :1971  y = 1 / (1 + e^-x)    */
+#define DOE_EP_TANH 3u     /* ExecuteTanh      :1987  y = tanh(x)           */
+#define DOE_EP_GELU 4u     /* ExecuteGelu      :2003  0.5x(1 + erf(x/sqrt2)) */
+#define DOE_EP_ADD 0u      /* ExecuteAdd       :1933  y = a + b             */
+#define DOE_EP_ADD_RELU 1u /* ExecuteAddRelu   :2380  y = relu(a + b)       */
+#define DOE_EP_MATMUL_RELU 0x1u /* doe_ep_matmul_f32 flag: relu(. + addend) */
+
+/* y[i] = op(x[i]) for i < n (op: DOE_EP_IDENTITY .. DOE_EP_GELU).          */
+int doe_ep_unary_f32(uint32_t op, const float* x, float* y, uint64_t n,
+                     const doe_launch* launch);
+/* y[i] = op(a[i], b[i]) (op: DOE_EP_ADD, DOE_EP_ADD_RELU).                 */
+int doe_ep_binary_f32(uint32_t op, const float* a, const float* b, float* y,
+                      uint64_t n, const doe_launch* launch);
+/* ExecuteSoftmax :2021: each of `rows` rows of `cols`:
+ * y = exp(x - max) * (sum != 0 ? 1 / sum : 0).  cols == 0 is a no-op.     */
+int doe_ep_softmax_f32(const float* x, float* y, uint64_t rows, uint32_t cols,
+                       const doe_launch* launch);
+/* ExecuteLayerNorm :2062 (scale only; the EP uses epsilon 1e-5):
+ * y = (x - mean) * (1 / sqrt(var + epsilon)) * scale[c], var the mean
+ * squared deviation, per row of `cols`; scale [cols].                      */
+int doe_ep_layernorm_f32(const float* x, const float* scale, float epsilon,
+                         float* y, uint64_t rows, uint32_t cols,
+                         const doe_launch* launch);
+/* ExecuteConcat :2110: a [outer, a_axis, inner] and b [outer, b_axis,
+ * inner] -> y [outer, a_axis + b_axis, inner] (a first).  y must not
+ * overlap a or b.                                                          */
+int doe_ep_concat_f32(const float* a, const float* b, float* y, uint64_t outer,
+                      uint64_t a_axis, uint64_t b_axis, uint64_t inner,
+                      const doe_launch* launch);
+/* ExecuteMatMul :2165, ExecuteGemm :2197, ExecuteMatMulAdd :2302,
+ * ExecuteMatMulAddRelu :2341: y[m, n] = sum_k a[m, k] b[k, n]
+ * (+ addend[m, n] when addend != NULL) (then relu with DOE_EP_MATMUL_RELU).
+ * a [m, k], b [k, n], addend and y [m, n]; y must not overlap a or b;
+ * m, k and n below 2^31.                                                  */
+int doe_ep_matmul_f32(const float* a, const float* b, const float* addend,
+                      float* y, uint32_t m, uint32_t k, uint32_t n,
+                      uint32_t flags, const doe_launch* launch);
+/* ExecuteGemmReluGemm :2236: h = relu(x w1 + b1), y = h w2 + b2 with x
+ * [batch, in], w1 [in, hidden], b1 [batch, hidden], w2 [hidden, out], b2
+ * and y [batch, out].  h lives in launch->workspace, which must hold
+ * doe_ep_gemm_relu_gemm_workspace_bytes(batch, hidden) bytes.              */
+uint64_t doe_ep_gemm_relu_gemm_workspace_bytes(uint32_t batch, uint32_t hidden);
+int doe_ep_gemm_relu_gemm_f32(const float* x, const float* w1, const float* b1,
+                              const float* w2, const float* b2, float* y,
+                              uint32_t batch, uint32_t in_dim, uint32_t hidden,
+                              uint32_t out_dim, const doe_launch* launch);
+
+/* ======================================================================== */
 /* Host KV page pool -- hands out physical pages and keeps the per-sequence  */
 /* block tables that the paged kernels read (the reference takes one         */
 /* page_table binding per dispatch, attention_head256_f16kv.wgsl:38).       */

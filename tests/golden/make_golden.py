@@ -9,7 +9,9 @@ It imports the reference's own numpy attention code
 ``shard_kv_along_position``, ``stitch_kv_axis_sharded_partials``) and its
 canary test constants (``bench/tests/test_attention_canary_identity.py``),
 and reads the attention-slice determinism fixtures
-(``bench/fixtures/determinism/*attention-slice*``).  The outputs are small
+(``bench/fixtures/determinism/*attention-slice*``), and reads the ORT plugin
+EP's session smoke cases as text
+(``runtime/bridge/onnxruntime-ep/src/doe_ort_ep_session_smoke.cc``).  The outputs are small
 .npz / .json files; nothing at test time reads the reference tree.
 """
 from __future__ import annotations
@@ -17,6 +19,7 @@ from __future__ import annotations
 import argparse
 import hashlib
 import json
+import re
 import sys
 from pathlib import Path
 
@@ -121,15 +124,75 @@ def make_decode_sim(stitch_mod) -> None:
                         expected=expected, tol=np.array([5e-5, 5e-4]))
 
 
+def _braced(text: str, start: int) -> str:
+    """The balanced {...} group that opens at or after text[start]."""
+    i = text.index("{", start)
+    depth = 0
+    for j in range(i, len(text)):
+        depth += {"{": 1, "}": -1}.get(text[j], 0)
+        if depth == 0:
+            return text[i:j + 1]
+    raise ValueError("unbalanced braces")
+
+
+def _numbers(group: str) -> list:
+    """Nested numeric initialiser lists ({1.0f, -2.0f} / {{1, 4}, {4}}) as lists."""
+    inner = group.strip()[1:-1].strip()
+    if inner.startswith("{"):
+        out, pos = [], 0
+        while True:
+            k = inner.find("{", pos)
+            if k < 0:
+                return out
+            g = _braced(inner, k)
+            out.append(_numbers(g))
+            pos = k + len(g)
+    return [float(t.rstrip("f")) for t in re.findall(r"-?\d+(?:\.\d*)?(?:e-?\d+)?f?", inner)]
+
+
+def make_ort_ep_cases(root: Path) -> None:
+    """The ORT plugin EP's session smoke cases (inputs and expected outputs)."""
+    src = (root / "runtime/bridge/onnxruntime-ep/src/doe_ort_ep_session_smoke.cc").read_text()
+    body = _braced(src, src.index("std::vector<SmokeCaseSpec> BuildSmokeCases()"))
+    cases, pos = [], 0
+    while True:
+        k = body.find("SmokeCaseSpec{", pos)
+        if k < 0:
+            break
+        spec = _braced(body, k)
+        pos = k + len(spec)
+        name = re.search(r'\.case_name = "([a-z_]+)"', spec).group(1)
+        field = lambda f: _numbers(_braced(spec, spec.index(f".{f} =")))
+        cases.append({"name": name, "input_dims": [[int(d) for d in dims] for dims in field("input_dims")],
+                      "output_dims": [int(d) for d in field("output_dims")],
+                      "inputs": field("inputs"), "expected": field("expected_output")})
+    out = {"source": "runtime/bridge/onnxruntime-ep/src/doe_ort_ep_session_smoke.cc:808-950 (BuildSmokeCases); "
+                     "tolerance :578-584 (absolute 1e-5)",
+           "tolerance_abs": 1e-5, "cases": cases}
+    (HERE / "ort_ep_smoke_cases.json").write_text(json.dumps(out, indent=1) + "\n")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", type=Path, required=True)
+    ap.add_argument("--only", choices=["stitch", "canary", "slice", "decode_sim", "ort_ep"], default=None,
+                    help="regenerate one fixture only")
     args = ap.parse_args()
+    if args.only == "ort_ep":
+        make_ort_ep_cases(args.reference)
+        print("golden fixtures written to", HERE)
+        return
     stitch_mod, canary_mod = _import_reference(args.reference)
-    make_stitch_cases(stitch_mod)
-    make_canary(canary_mod)
-    make_slice_kat(args.reference)
-    make_decode_sim(stitch_mod)
+    if args.only in (None, "stitch"):
+        make_stitch_cases(stitch_mod)
+    if args.only in (None, "canary"):
+        make_canary(canary_mod)
+    if args.only in (None, "slice"):
+        make_slice_kat(args.reference)
+    if args.only in (None, "decode_sim"):
+        make_decode_sim(stitch_mod)
+    if args.only is None:
+        make_ort_ep_cases(args.reference)
     print("golden fixtures written to", HERE)
 
 
