@@ -345,6 +345,9 @@ def measure_ep(steps, warmup, world, pk):
         times = []
         for i in range(warmup + steps):
             ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # keep the GPU busy while the host validates, allocates and
+            # enqueues, so the events bracket device time only
+            torch.cuda._sleep(1_000_000)
             ev[0].record()
             fn()
             ev[1].record()

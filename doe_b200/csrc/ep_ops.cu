@@ -43,44 +43,65 @@ __device__ __forceinline__ float binary(float a, float b) {
   else return s;
 }
 
-// y[i] = f(x[i]); VEC: float4 over n / 4 elements (all pointers 16-byte
-// aligned), the scalar tail by the first threads.
+// y[i] = f(x[i]).  VEC: float4 over the first n / 4 * 4 elements (all
+// pointers 16-byte aligned), kUnroll float4 loads in flight per thread before
+// their stores; the scalar tail (n % 4) by the first threads.
+constexpr int kUnroll = 4;
+
 template <int OP, bool VEC>
-__global__ void __launch_bounds__(kThreads) unary_kernel(const float* __restrict__ x, float* y, uint64_t n) {
+__global__ void __launch_bounds__(kThreads) unary_kernel(const float* x, float* y, uint64_t n) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t i = t;
   if constexpr (VEC) {
     const uint64_t n4 = n / 4;
-    for (uint64_t v = i; v < n4; v += stride) {
-      float4 t = reinterpret_cast<const float4*>(x)[v];
-      t.x = unary<OP>(t.x);
-      t.y = unary<OP>(t.y);
-      t.z = unary<OP>(t.z);
-      t.w = unary<OP>(t.w);
-      reinterpret_cast<float4*>(y)[v] = t;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    for (uint64_t base = t; base < n4; base += stride * kUnroll) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (base + u * stride < n4) v[u] = x4[base + u * stride];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (base + u * stride < n4)
+          __stcs(y4 + base + u * stride,
+                 make_float4(unary<OP>(v[u].x), unary<OP>(v[u].y), unary<OP>(v[u].z), unary<OP>(v[u].w)));
     }
-    i += n4 * 4;
+    i = n4 * 4 + t;
   }
   for (; i < n; i += stride) y[i] = unary<OP>(x[i]);
 }
 
 template <int OP, bool VEC>
-__global__ void __launch_bounds__(kThreads)
-    binary_kernel(const float* __restrict__ a, const float* __restrict__ b, float* y, uint64_t n) {
+__global__ void __launch_bounds__(kThreads) binary_kernel(const float* a, const float* b, float* y, uint64_t n) {
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-  uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  uint64_t i = t;
   if constexpr (VEC) {
     const uint64_t n4 = n / 4;
-    for (uint64_t v = i; v < n4; v += stride) {
-      const float4 p = reinterpret_cast<const float4*>(a)[v];
-      const float4 q = reinterpret_cast<const float4*>(b)[v];
-      reinterpret_cast<float4*>(y)[v] =
-          make_float4(binary<OP>(p.x, q.x), binary<OP>(p.y, q.y), binary<OP>(p.z, q.z), binary<OP>(p.w, q.w));
+    const float4* a4 = reinterpret_cast<const float4*>(a);
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    float4* y4 = reinterpret_cast<float4*>(y);
+    for (uint64_t base = t; base < n4; base += stride * kUnroll) {
+      float4 p[kUnroll], q[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (base + u * stride < n4) {
+          p[u] = a4[base + u * stride];
+          q[u] = b4[base + u * stride];
+        }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (base + u * stride < n4)
+          __stcs(y4 + base + u * stride, make_float4(binary<OP>(p[u].x, q[u].x), binary<OP>(p[u].y, q[u].y),
+                                                     binary<OP>(p[u].z, q[u].z), binary<OP>(p[u].w, q[u].w)));
     }
-    i += n4 * 4;
+    i = n4 * 4 + t;
   }
   for (; i < n; i += stride) y[i] = binary<OP>(a[i], b[i]);
 }
+
 
 // Block-wide reduction of one value per thread (sum or max); every thread
 // gets the result.  `red` holds kThreads / 32 partials; the leading barrier
@@ -103,50 +124,98 @@ __device__ __forceinline__ float block_reduce(float v, float* red) {
 
 // One CTA per row (grid-stride over rows).  CACHE: the row is read from HBM
 // once into shared memory (cols floats); otherwise each pass re-reads it.
+// VEC: rows are read and written as float4 (cols % 4 == 0, x, y and scale
+// 16-byte aligned), kUnroll loads in flight per thread.
 // SOFTMAX: y = exp(x - max) * (sum != 0 ? 1 / sum : 0)
 // else:    y = (x - mean) * (1 / sqrt(var + eps)) * scale, var = mean((x - mean)^2)
-template <bool SOFTMAX, bool CACHE>
+template <bool SOFTMAX, bool CACHE, bool VEC>
 __global__ void __launch_bounds__(kThreads)
     rows_kernel(const float* x, const float* __restrict__ scale, float eps, float* y, uint64_t rows, uint32_t cols) {
-  extern __shared__ float srow[];
+  extern __shared__ float4 srow4[];
+  float* srow = reinterpret_cast<float*>(srow4);
   __shared__ float red[kThreads / 32];
   const float inv_cols = 1.0f / (float)cols;
+  constexpr uint32_t W = VEC ? 4 : 1;  // floats per access
+  const uint32_t units = cols / W;
   for (uint64_t row = blockIdx.x; row < rows; row += gridDim.x) {
     const float* xr = x + row * cols;
     float* yr = y + row * cols;
-    auto at = [&](uint32_t i) { return CACHE ? srow[i] : xr[i]; };
+    auto load = [&](uint32_t u) -> float4 {
+      if constexpr (VEC) return reinterpret_cast<const float4*>(xr)[u];
+      else return make_float4(xr[u], 0.0f, 0.0f, 0.0f);
+    };
+    auto cached = [&](uint32_t u) -> float4 {
+      if constexpr (!CACHE) return load(u);
+      else if constexpr (VEC) return srow4[u];
+      else return make_float4(srow[u], 0.0f, 0.0f, 0.0f);
+    };
+    // combine the W live lanes of a unit into acc
+    auto fold = [&](float acc, float4 v, auto&& f) {
+      acc = f(acc, v.x);
+      if constexpr (VEC) {
+        acc = f(acc, v.y);
+        acc = f(acc, v.z);
+        acc = f(acc, v.w);
+      }
+      return acc;
+    };
+    auto mx = [](float a, float v) { return fmaxf(a, v); };
+    auto sum = [](float a, float v) { return a + v; };
     // pass 1: max (softmax) or sum (layer norm), caching the row
     float acc = SOFTMAX ? -INFINITY : 0.0f;
-    for (uint32_t i = threadIdx.x; i < cols; i += kThreads) {
-      const float v = xr[i];
-      if (CACHE) srow[i] = v;
-      acc = SOFTMAX ? fmaxf(acc, v) : acc + v;
+    for (uint32_t base = threadIdx.x; base < units; base += kThreads * kUnroll) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k)
+        if (base + k * kThreads < units) v[k] = load(base + k * kThreads);
+#pragma unroll
+      for (int k = 0; k < kUnroll; ++k)
+        if (base + k * kThreads < units) {
+          const uint32_t u = base + k * kThreads;
+          if constexpr (CACHE) {
+            if constexpr (VEC) srow4[u] = v[k];
+            else srow[u] = v[k].x;
+          }
+          acc = SOFTMAX ? fold(acc, v[k], mx) : fold(acc, v[k], sum);
+        }
     }
     const float first = block_reduce<SOFTMAX>(acc, red);
     // pass 2: sum of exp (softmax) or of squared deviations (layer norm)
     const float mean = SOFTMAX ? 0.0f : first * inv_cols;
-    acc = 0.0f;
-    for (uint32_t i = threadIdx.x; i < cols; i += kThreads) {
-      const float v = at(i);
-      if (SOFTMAX) {
-        acc += expf(v - first);
-      } else {
+    auto second_term = [&](float a, float v) {
+      if constexpr (SOFTMAX) return a + expf(v - first);
+      else {
         const float d = v - mean;
-        acc += d * d;
+        return a + d * d;
       }
-    }
+    };
+    acc = 0.0f;
+    for (uint32_t u = threadIdx.x; u < units; u += kThreads) acc = fold(acc, cached(u), second_term);
     const float second = block_reduce<false>(acc, red);
     // pass 3: the output row
-    if (SOFTMAX) {
-      const float inv = second != 0.0f ? 1.0f / second : 0.0f;
-      for (uint32_t i = threadIdx.x; i < cols; i += kThreads) yr[i] = expf(at(i) - first) * inv;
-    } else {
-      const float inv_std = 1.0f / sqrtf(second * inv_cols + eps);
-      for (uint32_t i = threadIdx.x; i < cols; i += kThreads) yr[i] = (at(i) - mean) * inv_std * scale[i];
+    const float inv = SOFTMAX ? (second != 0.0f ? 1.0f / second : 0.0f) : 1.0f / sqrtf(second * inv_cols + eps);
+    for (uint32_t u = threadIdx.x; u < units; u += kThreads) {
+      const float4 v = cached(u);
+      if constexpr (SOFTMAX) {
+        if constexpr (VEC)
+          __stcs(reinterpret_cast<float4*>(yr) + u, make_float4(expf(v.x - first) * inv, expf(v.y - first) * inv,
+                                                                expf(v.z - first) * inv, expf(v.w - first) * inv));
+        else yr[u] = expf(v.x - first) * inv;
+      } else {
+        if constexpr (VEC) {
+          const float4 s = reinterpret_cast<const float4*>(scale)[u];
+          __stcs(reinterpret_cast<float4*>(yr) + u,
+                 make_float4((v.x - mean) * inv * s.x, (v.y - mean) * inv * s.y, (v.z - mean) * inv * s.z,
+                             (v.w - mean) * inv * s.w));
+        } else {
+          yr[u] = (v.x - mean) * inv * scale[u];
+        }
+      }
     }
     __syncthreads();  // the cached row is rewritten by the next row
   }
 }
+
 
 // y[o, 0:a_axis*inner] = a[o, :], y[o, a_axis*inner:] = b[o, :]
 __global__ void __launch_bounds__(kThreads)
@@ -243,9 +312,19 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-unsigned grid_for(uint64_t work, int per_block) {
+// A grid-stride kernel's grid: one wave of the CTAs that fit on the SMs at
+// once (registers and shared memory permitting), or fewer when there is
+// less work.  A second, partial wave would leave SMs idle at the end.
+template <typename Kernel>
+unsigned resident_grid(Kernel kernel, size_t smem, uint64_t work, int per_block) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess ||
+      per_sm < 1) {
+    cudaGetLastError();
+    per_sm = 1;
+  }
   const uint64_t want = (work + per_block - 1) / per_block;
-  const uint64_t cap = (uint64_t)num_sms() * 8;
+  const uint64_t cap = (uint64_t)num_sms() * per_sm;
   return (unsigned)(want < 1 ? 1 : (want < cap ? want : cap));
 }
 
@@ -253,19 +332,24 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 
 
 template <int OP>
 int launch_unary_op(const float* x, float* y, uint64_t n, cudaStream_t s) {
-  const bool vec = aligned16(x) && aligned16(y);
-  const unsigned g = grid_for(vec ? (n + 3) / 4 : n, kThreads);
-  if (vec) unary_kernel<OP, true><<<g, kThreads, 0, s>>>(x, y, n);
-  else unary_kernel<OP, false><<<g, kThreads, 0, s>>>(x, y, n);
+  if (aligned16(x) && aligned16(y)) {
+    const unsigned g = resident_grid(unary_kernel<OP, true>, 0, (n / 4 + kUnroll - 1) / kUnroll, kThreads);
+    unary_kernel<OP, true><<<g, kThreads, 0, s>>>(x, y, n);
+  } else {
+    unary_kernel<OP, false><<<resident_grid(unary_kernel<OP, false>, 0, n, kThreads), kThreads, 0, s>>>(x, y, n);
+  }
   return cuda_status(cudaGetLastError(), "ep unary_kernel");
 }
 
 template <int OP>
 int launch_binary_op(const float* a, const float* b, float* y, uint64_t n, cudaStream_t s) {
-  const bool vec = aligned16(a) && aligned16(b) && aligned16(y);
-  const unsigned g = grid_for(vec ? (n + 3) / 4 : n, kThreads);
-  if (vec) binary_kernel<OP, true><<<g, kThreads, 0, s>>>(a, b, y, n);
-  else binary_kernel<OP, false><<<g, kThreads, 0, s>>>(a, b, y, n);
+  if (aligned16(a) && aligned16(b) && aligned16(y)) {
+    const unsigned g = resident_grid(binary_kernel<OP, true>, 0, (n / 4 + kUnroll - 1) / kUnroll, kThreads);
+    binary_kernel<OP, true><<<g, kThreads, 0, s>>>(a, b, y, n);
+  } else {
+    const unsigned g = resident_grid(binary_kernel<OP, false>, 0, n, kThreads);
+    binary_kernel<OP, false><<<g, kThreads, 0, s>>>(a, b, y, n);
+  }
   return cuda_status(cudaGetLastError(), "ep binary_kernel");
 }
 
@@ -275,11 +359,18 @@ constexpr uint32_t kMaxCachedCols = 48 * 1024 / 4;
 template <bool SOFTMAX>
 int launch_rows(const float* x, const float* scale, float eps, float* y, uint64_t rows, uint32_t cols,
                 cudaStream_t s) {
-  const unsigned g = grid_for(rows, 1);
-  if (cols <= kMaxCachedCols)
-    rows_kernel<SOFTMAX, true><<<g, kThreads, cols * sizeof(float), s>>>(x, scale, eps, y, rows, cols);
-  else
-    rows_kernel<SOFTMAX, false><<<g, kThreads, 0, s>>>(x, scale, eps, y, rows, cols);
+  const bool vec = cols % 4 == 0 && aligned16(x) && aligned16(y) && (scale == nullptr || aligned16(scale));
+  const size_t smem = cols * sizeof(float);
+  auto go = [&](auto kernel, size_t bytes) {
+    kernel<<<resident_grid(kernel, bytes, rows, 1), kThreads, bytes, s>>>(x, scale, eps, y, rows, cols);
+  };
+  if (cols <= kMaxCachedCols) {
+    if (vec) go(rows_kernel<SOFTMAX, true, true>, smem);
+    else go(rows_kernel<SOFTMAX, true, false>, smem);
+  } else {
+    if (vec) go(rows_kernel<SOFTMAX, false, true>, 0);
+    else go(rows_kernel<SOFTMAX, false, false>, 0);
+  }
   return cuda_status(cudaGetLastError(), SOFTMAX ? "ep softmax rows_kernel" : "ep layernorm rows_kernel");
 }
 
@@ -317,7 +408,7 @@ int launch_ep_layernorm(const float* x, const float* scale, float eps, float* y,
 
 int launch_ep_concat(const float* a, const float* b, float* y, uint64_t outer, uint64_t a_run, uint64_t b_run,
                      const doe_launch* l) {
-  const unsigned g = ep::grid_for(outer * (a_run + b_run), ep::kThreads);
+  const unsigned g = ep::resident_grid(ep::concat_kernel, 0, outer * (a_run + b_run), ep::kThreads);
   ep::concat_kernel<<<g, ep::kThreads, 0, static_cast<cudaStream_t>(l->stream)>>>(a, b, y, outer, a_run, b_run);
   return cuda_status(cudaGetLastError(), "ep concat_kernel");
 }
