@@ -62,6 +62,37 @@ __device__ __forceinline__ uint32_t prmt(uint32_t x, uint32_t y, uint32_t sel) {
   return __byte_perm(x, y, sel);
 }
 
+// Two f32 lanes per instruction (sm_100 packed FP32): a * b + c, a + b and
+// a * b, each lane rounded as the scalar instruction would round it.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rc, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+      "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "add.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n.reg .b64 ra, rb, rd;\n"
+      "mov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\n"
+      "mul.rn.f32x2 rd, ra, rb;\nmov.b64 {%0, %1}, rd;\n}\n"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
 // int8 KV quantisation of one element: clamp(rint(x / s), -127, 127) for an
 // f16 value x and the row's f16 scale s = f16(absmax / 127) > 0, equal to the
 // CPU definition's rint of the f32 IEEE quotient.  The quotient is formed from
@@ -82,6 +113,31 @@ __device__ __forceinline__ int quantize_s8(float x, float s, float rs) {
   const float c = fminf(fmaxf(y, -127.0f), 127.0f);
   return (int)__float_as_uint(__fadd_rn(c, 12582912.0f));
 }
+// The row scale's f32 quotient amax / 127 without an IEEE division:
+// q0 = amax * RN(1/127), then one residual correction (Markstein's method),
+// the residual exact in an FMA.  For every finite f16 amax >= 0 this is the
+// correctly rounded quotient (checked exhaustively against exact rational
+// arithmetic), so f16(result) equals f16(amax / 127) of the CPU definition.
+__device__ __forceinline__ float div127(float amax) {
+  constexpr float kInv127 = 0x1.020408p-7f;  // RN_f32(1 / 127)
+  const float q0 = amax * kInv127;
+  return fmaf(fmaf(-q0, 127.0f, amax), kInv127, q0);
+}
+
+// quantize_s8 on two elements with a normal f16 scale (2^-14 <= s <= 65504),
+// in sm_100 packed FP32.  With s = f16(amax / 127) normal, |x / s| <=
+// 127 / (1 - 2^-11) < 127.07 for |x| <= amax, so rint never leaves
+// [-127, 127] and the clamp of quantize_s8 cannot change the result; the
+// rest is the same arithmetic (y0 * (-s) is -y0 * s exactly).
+__device__ __forceinline__ void quantize_s8x2_normal(float2 x, float s, float rs, int& q0, int& q1) {
+  const float2 rs2 = make_float2(rs, rs);
+  const float2 y0 = fmul2(x, rs2);
+  const float2 y = ffma2(ffma2(y0, make_float2(-s, -s), x), rs2, y0);
+  const float2 c = fadd2(y, make_float2(12582912.0f, 12582912.0f));
+  q0 = (int)__float_as_uint(c.x);
+  q1 = (int)__float_as_uint(c.y);
+}
+
 // Low bytes of four words (two's complement int8 values) packed into a word.
 __device__ __forceinline__ uint32_t pack_s8x4(int q0, int q1, int q2, int q3) {
   return __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);

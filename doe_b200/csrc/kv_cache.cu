@@ -68,7 +68,7 @@ __global__ void __launch_bounds__(256) paged_append_kernel(const PagedAppendArgs
         for (int i = 0; i < EPL / 2; ++i)
           amax = fmaxf(amax, fmaxf(fabsf(__low2float(x2[i])), fabsf(__high2float(x2[i]))));
         amax = warp_max(amax);
-        const __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
+        const __half sh = __float2half_rn(div127(amax));
         const float sf = __half2float(sh);
         const float rs = sf != 0.0f ? __frcp_rn(sf) : 0.0f;
         int8_t* dst = reinterpret_cast<int8_t*>(kv ? a.v_pool : a.k_pool) + (row * Hkv + h) * D +
@@ -154,10 +154,14 @@ __global__ void __launch_bounds__(128) paged_append_d128_kernel(const PagedAppen
     // both half-warps run this together (ROWS is even); offsets <= 8 stay in a half
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
+    const __half sh = __float2half_rn(div127(amax));
     const float sf = __half2float(sh);
     int q[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (sf != 0.0f) {
+    if (sf >= 0x1p-14f && sf <= 65504.0f) {  // normal scale: packed, no clamp needed
+      const float rs = __frcp_rn(sf);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) quantize_s8x2_normal(__half22float2(hx[e]), sf, rs, q[2 * e], q[2 * e + 1]);
+    } else if (sf != 0.0f) {
       const float rs = __frcp_rn(sf);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {

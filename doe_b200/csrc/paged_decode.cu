@@ -113,7 +113,7 @@ __device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
       float x[4] = {__low2float(h01), __high2float(h01), __low2float(h23), __high2float(h23)};
       float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
       amax = warp_max(amax);
-      __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
+      __half sh = __float2half_rn(div127(amax));
       float sf = __half2float(sh);
       int qv[4] = {0, 0, 0, 0};
       if (sf != 0.0f) {

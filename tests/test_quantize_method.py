@@ -74,3 +74,57 @@ def test_random_rows_with_row_scales():
         keep = (s != 0)[:, 0]
         x, s = x[keep], np.broadcast_to(s[keep], x[keep].shape)
         np.testing.assert_array_equal(kernel_quantize(x, s), divide_quantize(x, s))
+
+
+def _rn32(fr):
+    """Exact round-to-nearest-even of a rational to float32 (as a Fraction)."""
+    from fractions import Fraction as Fr
+
+    if fr == 0:
+        return Fr(0)
+    sign, a = (-1 if fr < 0 else 1), abs(fr)
+    e = a.numerator.bit_length() - a.denominator.bit_length()
+    if Fr(2) ** e > a:
+        e -= 1
+    if Fr(2) ** (e + 1) <= a:
+        e += 1
+    sh = 149 if e < -126 else 23 - e
+    m = a * Fr(2) ** sh
+    n = m.numerator // m.denominator
+    rem = m - n
+    if rem > Fr(1, 2) or (rem == Fr(1, 2) and n % 2 == 1):
+        n += 1
+    return sign * Fr(n) / Fr(2) ** sh
+
+
+def test_row_scale_quotient_is_correctly_rounded_for_every_f16():
+    """div127 (common.cuh): q0 = amax * RN(1/127), q = fma(fma(-q0, 127, amax),
+    RN(1/127), q0) equals RN_f32(amax / 127) for every finite f16 amax >= 0,
+    each FMA modelled exactly (one rounding of the exact value)."""
+    from fractions import Fraction as Fr
+
+    r = _rn32(Fr(1, 127))
+    assert float(r) == float.fromhex("0x1.020408p-7")
+    for v in _f16(np.arange(0, 0x7C00, dtype=np.uint16)).astype(np.float64):
+        a = Fr(float(v))
+        q0 = _rn32(a * r)
+        q = _rn32(_rn32(a - q0 * 127) * r + q0)
+        assert q == _rn32(a / 127), v
+
+
+def test_normal_scale_needs_no_clamp():
+    """quantize_s8x2_normal skips the clamp when s = f16(amax / 127) is a normal
+    f16: the row maximum itself (the largest quotient) must already land in
+    [-127, 127], with and without the clamp, for every f16 amax."""
+    amax = _f16(np.arange(1, 0x7C00, dtype=np.uint16))
+    s = (amax.astype(np.float64) / 127).astype(F32).astype(np.float16).astype(F32)
+    normal = (s >= F32(2.0 ** -14)) & (s <= F32(65504))
+    x, s = amax[normal], s[normal]
+    rs = (F32(1.0) / s).astype(F32)
+    y0 = (x * rs).astype(F32)
+    y = _fma(_fma(-y0, s, x), rs, y0)
+    assert np.abs(y).max() < 127.5
+    bits = (y + F32(12582912.0)).astype(F32).view(np.uint32)
+    q = (bits & 0xFF).astype(np.uint8).view(np.int8).astype(np.int64)
+    np.testing.assert_array_equal(q, divide_quantize(x, s))
+    np.testing.assert_array_equal(q, divide_quantize(-x, s) * -1)
