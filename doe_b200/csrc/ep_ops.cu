@@ -19,6 +19,10 @@
 // which misses the 1e-5 relative agreement the reference's f32 loops define.
 // Sums are reduced in a different order than the reference's left folds
 // (tree reductions, FMA in the product), within that tolerance.
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -315,13 +319,28 @@ __global__ void __launch_bounds__(kThreads)
 // A grid-stride kernel's grid: one wave of the CTAs that fit on the SMs at
 // once (registers and shared memory permitting), or fewer when there is
 // less work.  A second, partial wave would leave SMs idle at the end.
+// The occupancy query is cached per (kernel, device, shared-memory bytes).
 template <typename Kernel>
 unsigned resident_grid(Kernel kernel, size_t smem, uint64_t work, int per_block) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t>, int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) cudaGetLastError();
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), dev, smem);
   int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess ||
-      per_sm < 1) {
-    cudaGetLastError();
-    per_sm = 1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) per_sm = it->second;
+  }
+  if (per_sm == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kThreads, smem) != cudaSuccess ||
+        per_sm < 1) {
+      cudaGetLastError();
+      per_sm = 1;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = per_sm;
   }
   const uint64_t want = (work + per_block - 1) / per_block;
   const uint64_t cap = (uint64_t)num_sms() * per_sm;
