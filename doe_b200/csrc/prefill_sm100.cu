@@ -19,7 +19,8 @@
 //   warp 16    TMEM owner + MMA issuer (whole warp, one elected lane issues):
 //              S_A = Q_A K^T, S_B = Q_B K^T, then O_A += P_A V and O_B += P_B V,
 //              ping-ponging so the tensor core works on one tile while the
-//              other tile's softmax runs
+//              other tile's softmax runs; each PV runs in two halves, the
+//              first as soon as the softmax has published P's first chunk
 //   warps 0-7  softmax of tile A, warps 8-15 softmax of tile B: row r (TMEM
 //              lane r) is shared by two threads, one per half of the 128 keys
 //              (warps w and w + 4 of a tile); each reads its 64 scores from TMEM
@@ -59,7 +60,7 @@ constexpr long long kWaitCycles = 4000000000LL;      // ~2 s at 1.9 GHz
 constexpr uint32_t kSuspendNs = 20000;                // try_wait sleep hint (the 2 s bound is checked between)
 
 enum Bar { Q_FULL, K_FULL0, K_FULL1, V_FULL0, V_FULL1, K_EMPTY0, K_EMPTY1, V_EMPTY0, V_EMPTY1,
-           S_FULL_A, S_FULL_B, P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, MMA_DONE, NUM_BARS };
+           S_FULL_A, S_FULL_B, P_HALF_A, P_HALF_B, P_FULL_A, P_FULL_B, O_FULL_A, O_FULL_B, MMA_DONE, NUM_BARS };
 
 struct Args {
   float* out;               // [S, H, D] f32
@@ -182,7 +183,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kv = nA > nB ? nA : nB;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i == P_FULL_A || i == P_FULL_B) ? 8u : 1u);
+    // P_HALF_x / P_FULL_x take one arrival from each of tile x's 8 softmax warps
+    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i >= P_HALF_A && i <= P_FULL_B) ? 8u : 1u);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
@@ -285,12 +287,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       commit_elect(bar(S_FULL_A + x));
     };
     // O_x += P_x V_j with P_x (f16) in TMEM columns [128x, 128x + 64)
-    auto issue_pv = [&](int x, int j) {
+    // part 0: keys [0, 32) and [64, 96), the first P chunk of each half-row
+    // (published on P_HALF_x); part 1: keys [32, 64) and [96, 128)
+    auto issue_pv = [&](int x, int j, int part) {
       const uint64_t v = dv + (((j & 1) * kTile) >> 4);
 #pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk)
+      for (int i = 0; i < 4; ++i) {
+        const int kk = (i >> 1) * 4 + part * 2 + (i & 1);  // 16-key slice
         umma_ts_elect(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, v + ((kk * 16 * 128) >> 4), idp,
-                      (j > 0 || kk > 0) ? 1u : 0u);
+                      (j > 0 || part > 0 || i > 0) ? 1u : 0u);
+      }
     };
     // bounded wait by every lane, agreed across the warp so it stays converged
     auto wait = [&](int b, uint32_t parity) {
@@ -311,10 +317,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (j >= nt) continue;
         // every mbarrier wait here costs the issue stream ~100 cycles even when
         // the phase is complete, so each is taken only once per step
+        // the first half of PV_x(j) runs while the softmax stores the rest of P
+        ok = wait(P_HALF_A + x, j & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(x, j, 0);
         ok = wait(P_FULL_A + x, j & 1);
         if (!ok) break;
         tc_fence_after();
-        issue_pv(x, j);
+        issue_pv(x, j, 1);
         if (j == nt - 1) commit_elect(bar(O_FULL_A + x));
         if (j + 1 < nt) {
           if (!k_ready) {
@@ -399,15 +410,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
       if (!ok) continue;  // barriers above were kept in step; nothing else to do
       // p = 2^(s * scale * log2e - m): one packed FFMA per two scores and one
-      // MUFU.EX2 per score.  Each half's row sum is taken after its P store is
-      // issued, so the adds overlap the store's latency.
+      // MUFU.EX2 per score.  Chunk 0 (the half-row's first 32 keys) is stored
+      // first and published on P_HALF_x once chunk 1's exponentials and sums
+      // are done, by which time its store has landed: the tensor core then
+      // runs the first half of PV_x(j) while chunk 1 is stored.
       const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(neg_m, neg_m);
       float2 s2[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) s2[i] = make_float2(0.0f, 0.0f);
+      uint32_t w[2][16];
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t w[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int i = c * 32 + 2 * e;
@@ -416,9 +429,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float p1 = ex2(xx.y);
           r[i] = __float_as_uint(p0);
           r[i + 1] = __float_as_uint(p1);
-          w[e] = pack_half2(p0, p1);
+          w[c][e] = pack_half2(p0, p1);
         }
-        tmem_st16(lane_base + p_col + c * 16, w);
+        if (c == 0) tmem_st16(lane_base + p_col, w[0]);
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int i = c * 32 + 2 * e;
@@ -429,8 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sum = s4.x + s4.y;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
         // the running max rose by more than 2^8: rescale this half-row of O
-        // (quiescent: S_x(j)'s commit covered PV_x(j-1), and PV_x(j) waits for
-        // this warp's P_FULL arrival below)
+        // (quiescent: S_x(j)'s commit covered PV_x(j-1), and no MMA of PV_x(j)
+        // starts before this warp's P_HALF arrival below)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {  // 16 columns at a time
           uint32_t o[16];
@@ -441,7 +454,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(lane_base + o_col + c * 16, o);
         }
       }
-      tmem_wait_st();  // P (and any O rescale) has landed
+      tmem_wait_st();  // P chunk 0 (and any O rescale) has landed
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(P_HALF_A + x));
+      tmem_st16(lane_base + p_col + 16, w[1]);
+      tmem_wait_st();  // P chunk 1 has landed
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(P_FULL_A + x));
