@@ -140,7 +140,8 @@ def test_concat_exact(shapes, axis):
     assert np.array_equal(got, oep.concat(a, b, axis))
 
 
-@pytest.mark.parametrize("m,k,n", [(2, 3, 2), (1, 1, 1), (129, 65, 131), (256, 512, 384), (7, 1000, 3)])
+@pytest.mark.parametrize("m,k,n", [(2, 3, 2), (1, 1, 1), (129, 65, 131), (256, 512, 384), (7, 1000, 3),
+                                   (130, 68, 260), (1, 4, 4)])
 def test_matmul_family_matches_oracle(m, k, n):
     g = np.random.default_rng(m * 7 + k * 3 + n)
     a = g.standard_normal((m, k), dtype=np.float32)
