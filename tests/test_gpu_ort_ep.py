@@ -159,7 +159,7 @@ def test_matmul_empty_inner_dimension_gives_addend():
     assert np.array_equal(got, np.maximum(c, 0))
 
 
-@pytest.mark.parametrize("b,i,h,o", [(1, 2, 3, 2), (33, 100, 257, 10)])
+@pytest.mark.parametrize("b,i,h,o", [(1, 2, 3, 2), (33, 100, 257, 10), (32, 64, 256, 16)])
 def test_gemm_relu_gemm_matches_oracle(b, i, h, o):
     g = np.random.default_rng(b + i + h + o)
     x = g.standard_normal((b, i), dtype=np.float32)
