@@ -221,6 +221,77 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 
+// Rows of at most kThreads * kUnroll float4 (4096 floats), read and written as
+// float4: each thread keeps its part of the row in registers, and the CTA's
+// next row is loaded while this one is reduced and written (rows belong to
+// CTAs by row % gridDim.x, so in place the prefetched row is never one being
+// written).  Same arithmetic as rows_kernel; softmax keeps exp(x - max) from
+// the sum pass for the output pass.
+template <bool SOFTMAX>
+__global__ void __launch_bounds__(kThreads)
+    rows_reg_kernel(const float* x, const float* __restrict__ scale, float eps, float* y, uint64_t rows,
+                    uint32_t cols) {
+  __shared__ float red[kThreads / 32];
+  const uint32_t units = cols / 4;
+  const float inv_cols = 1.0f / (float)cols;
+  float4 cur[kUnroll], nxt[kUnroll];
+  auto load_row = [&](uint64_t row, float4 (&v)[kUnroll]) {
+    const float4* xr = reinterpret_cast<const float4*>(x + row * cols);
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const uint32_t u = threadIdx.x + k * kThreads;
+      if (u < units) v[k] = xr[u];
+    }
+  };
+  uint64_t row = blockIdx.x;
+  if (row < rows) load_row(row, cur);
+  for (; row < rows; row += gridDim.x) {
+    const uint64_t next = row + gridDim.x;
+    if (next < rows) load_row(next, nxt);
+    float acc = SOFTMAX ? -INFINITY : 0.0f;
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k)
+      if (threadIdx.x + k * kThreads < units) {
+        const float4 v = cur[k];
+        acc = SOFTMAX ? fmaxf(fmaxf(acc, v.x), fmaxf(fmaxf(v.y, v.z), v.w)) : acc + v.x + v.y + v.z + v.w;
+      }
+    const float first = block_reduce<SOFTMAX>(acc, red);
+    const float mean = SOFTMAX ? 0.0f : first * inv_cols;
+    acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k)
+      if (threadIdx.x + k * kThreads < units) {
+        float4& v = cur[k];
+        if (SOFTMAX) {
+          v = make_float4(expf(v.x - first), expf(v.y - first), expf(v.z - first), expf(v.w - first));
+          acc += v.x + v.y + v.z + v.w;
+        } else {
+          const float dx = v.x - mean, dy = v.y - mean, dz = v.z - mean, dw = v.w - mean;
+          acc += dx * dx + dy * dy + dz * dz + dw * dw;
+        }
+      }
+    const float second = block_reduce<false>(acc, red);
+    const float inv = SOFTMAX ? (second != 0.0f ? 1.0f / second : 0.0f) : 1.0f / sqrtf(second * inv_cols + eps);
+    float4* yr = reinterpret_cast<float4*>(y + row * cols);
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) {
+      const uint32_t u = threadIdx.x + k * kThreads;
+      if (u < units) {
+        const float4 v = cur[k];
+        if (SOFTMAX) {
+          __stcs(yr + u, make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv));
+        } else {
+          const float4 sc = reinterpret_cast<const float4*>(scale)[u];
+          __stcs(yr + u, make_float4((v.x - mean) * inv * sc.x, (v.y - mean) * inv * sc.y,
+                                     (v.z - mean) * inv * sc.z, (v.w - mean) * inv * sc.w));
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kUnroll; ++k) cur[k] = nxt[k];
+  }
+}
+
 // y[o, 0:a_axis*inner] = a[o, :], y[o, a_axis*inner:] = b[o, :]
 __global__ void __launch_bounds__(kThreads)
     concat_kernel(const float* __restrict__ a, const float* __restrict__ b, float* __restrict__ y, uint64_t outer,
@@ -471,7 +542,9 @@ int launch_rows(const float* x, const float* scale, float eps, float* y, uint64_
   auto go = [&](auto kernel, size_t bytes) {
     kernel<<<resident_grid(kernel, bytes, rows, 1), kThreads, bytes, s>>>(x, scale, eps, y, rows, cols);
   };
-  if (cols <= kMaxCachedCols) {
+  if (vec && cols <= (uint32_t)(kThreads * kUnroll * 4)) {
+    go(rows_reg_kernel<SOFTMAX>, 0);
+  } else if (cols <= kMaxCachedCols) {
     if (vec) go(rows_kernel<SOFTMAX, true, true>, smem);
     else go(rows_kernel<SOFTMAX, true, false>, smem);
   } else {
