@@ -210,12 +210,13 @@ __global__ void __launch_bounds__(kF32Warps * 32) decode_f32_cluster_kernel(cons
 // will not run a cluster that large (the caller then uses the workspace path).
 template <int PER_LANE>
 static int launch_cluster_one(const DecodeF32Args& a, cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<bool> attr[kMaxDevices];
+  int rc = once_per_device(attr, [] {
     cudaFuncSetAttribute(decode_f32_cluster_kernel<PER_LANE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    cudaGetLastError();
-    attr = true;
-  }
+    cudaGetLastError();  // a device that refuses non-portable sizes leaves an error to clear
+    return (int)DOE_OK;
+  });
+  if (rc != DOE_OK) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.max_splits, a.num_heads);
   cfg.blockDim = dim3(kF32Warps * 32);
@@ -227,14 +228,17 @@ static int launch_cluster_one(const DecodeF32Args& a, cudaStream_t s) {
   at[0].val.clusterDim.z = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  // whether the device runs a cluster of this size, asked once per size
-  static int runs[kF32MaxCluster + 1] = {};  // 0 unknown, 1 yes, -1 no
-  int& known = runs[a.max_splits];
+  // whether the device runs a cluster of this size, asked once per device and size
+  static std::atomic<int> runs[kMaxDevices][kF32MaxCluster + 1];  // 0 unknown, 1 yes, -1 no
+  const int dev = current_device();
+  if (dev < 0) return DOE_CUDA_ERROR;
+  int known = runs[dev][a.max_splits].load();
   if (known == 0) {
     int clusters = 0;
     known = (cudaOccupancyMaxActiveClusters(&clusters, decode_f32_cluster_kernel<PER_LANE>, &cfg) ==
                  cudaSuccess && clusters >= 1) ? 1 : -1;
     cudaGetLastError();
+    runs[dev][a.max_splits].store(known);
   }
   if (known < 0) return DOE_UNSUPPORTED;
   return cuda_status(cudaLaunchKernelEx(&cfg, decode_f32_cluster_kernel<PER_LANE>, a),

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/doe_cuda.h"
 
 namespace doe {
@@ -28,6 +30,24 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 void set_op_error(const char* fmt, ...);
+
+// Per-device state of the host launchers (function attributes, occupancy
+// answers) is kept for ordinals below kMaxDevices.
+constexpr int kMaxDevices = 64;
+// The current device's ordinal, or -1 (with the op error set) when there is
+// none or it is not below kMaxDevices.
+int current_device();
+// Runs `set` (returning a doe status) once per device for one call site's
+// flags; a failure is returned and the next call tries again.
+template <typename F>
+int once_per_device(std::atomic<bool> (&done)[kMaxDevices], F&& set) {
+  const int dev = current_device();
+  if (dev < 0) return DOE_CUDA_ERROR;
+  if (done[dev].load(std::memory_order_acquire)) return DOE_OK;
+  const int rc = set();
+  if (rc == DOE_OK) done[dev].store(true, std::memory_order_release);
+  return rc;
+}
 int cuda_status(cudaError_t err, const char* where);
 
 // Arguments of the head256-semantics online-softmax kernel (attn_generic.cu).

@@ -467,6 +467,16 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __re
 }  // namespace lin
 
 // ---- host -----------------------------------------------------------------
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    cudaGetLastError();
+    set_op_error("no current CUDA device (or its ordinal is %d or more)", kMaxDevices);
+    return -1;
+  }
+  return dev;
+}
+
 // SM count of the current device (cached per device).
 int num_sms() {
   static std::atomic<int> cached[64];

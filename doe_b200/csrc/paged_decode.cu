@@ -675,14 +675,13 @@ template <bool INT8, int GROUP, bool CAP>
 static int launch_cap(const CUtensorMap& tm_k, const CUtensorMap& tm_v, const PagedDecodeArgs& a, dim3 grid,
                       cudaStream_t st) {
   constexpr int smem = Ring<INT8>::kSmem;
-  static bool attr = false;  // per instantiation
-  if (!attr) {
-    int rc = cuda_status(cudaFuncSetAttribute(paged_decode_kernel<INT8, GROUP, CAP>,
-                                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-                         "cudaFuncSetAttribute(paged_decode)");
-    if (rc != DOE_OK) return rc;
-    attr = true;
-  }
+  static std::atomic<bool> attr[kMaxDevices];  // per instantiation and device
+  const int rc = once_per_device(attr, [] {
+    return cuda_status(cudaFuncSetAttribute(paged_decode_kernel<INT8, GROUP, CAP>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                       "cudaFuncSetAttribute(paged_decode)");
+  });
+  if (rc != DOE_OK) return rc;
   return cuda_status(
       launch_pdl(paged_decode_kernel<INT8, GROUP, CAP>, grid, dim3(kWarps * 32), smem, st, tm_k, tm_v, a),
       "paged_decode_kernel");

@@ -558,14 +558,13 @@ int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, 
     mcv = mv;
   }
   if (rc != DOE_OK) return rc;
-  static bool attr_set = false;
-  if (!attr_set) {
-    rc = cuda_status(cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          pf::kSmemBytes),
-                     "cudaFuncSetAttribute(prefill)");
-    if (rc != DOE_OK) return rc;
-    attr_set = true;
-  }
+  static std::atomic<bool> attr_set[kMaxDevices];
+  rc = once_per_device(attr_set, [] {
+    return cuda_status(cudaFuncSetAttribute(pf::prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            pf::kSmemBytes),
+                       "cudaFuncSetAttribute(prefill)");
+  });
+  if (rc != DOE_OK) return rc;
   const uint64_t ctas = (uint64_t)a.n_pairs * num_heads;
   pf::prefill_kernel<<<(unsigned)ctas, pf::kThreads, pf::kSmemBytes,
                        static_cast<cudaStream_t>(launch->stream)>>>(mq, mk, mv, mck, mcv, a);
