@@ -52,3 +52,19 @@ def test_config4_paged_int8_draws():
     assert w.kv_bytes_per_token() == 2080
     used = w.block_table[w.block_table >= 0]
     assert np.array_equal(np.sort(used), np.arange(w.num_pages))
+
+
+def test_config5_decoder_bytes():
+    """Config 5: bf16 linear weights 1,744,830,464 B and f16 KV 2,147,483,648 B
+    at ctx 4096 (4 layers, batch 32); the bench's count adds the RMSNorm
+    weights (2 x 4096 bf16 per layer) and the appended token (ctx + 1)."""
+    from doe_b200.decoder import DecoderConfig
+
+    cfg = DecoderConfig()
+    assert (cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.layers, cfg.batch, cfg.ctx) == \
+        (4096, 32, 8, 128, 14336, 4, 32, 4096)
+    norms = 2 * 2 * cfg.hidden * cfg.layers
+    assert cfg.weight_bytes() - norms == 1_744_830_464
+    per_token = cfg.batch * cfg.kv_heads * cfg.head_dim * 2 * 2 * cfg.layers
+    assert cfg.kv_read_bytes() - per_token == 2_147_483_648
+    assert cfg.weight_bytes() + cfg.kv_read_bytes() == 3_892_903_936
