@@ -7,6 +7,9 @@ views of its two surfaces:
   doe_b200.backend  -- the handle / kernel_dispatch backend (Doe's BackendIface)
   doe_b200.ops      -- direct operator launches on torch device tensors
   doe_b200.kv       -- the KV page pool and the device paged cache
+  doe_b200.ort_ep   -- the ORT plugin EP's basic f32 operators (execute(kind, ...))
+  doe_b200.decoder  -- a Llama-style decoder step on the library's kernels
+  doe_b200.tp       -- peer buffers for its tensor-parallel reduction
 """
 from ._abi import DoeError, lib  # noqa: F401
 
