@@ -5,7 +5,8 @@
   (runtime/bridge/onnxruntime-ep/src/doe_ort_ep_session_smoke.cc:578-584,
   808-950; fixture tests/golden/ort_ep_smoke_cases.json).
 - doe_b200.ort_ep.validate applies the EP's runtime shape rules with its
-  messages before any device call.
+  messages before any device call, and the C ABI's doe_ep_* entry points
+  reject bad arguments before any launch.
 """
 from __future__ import annotations
 
@@ -97,3 +98,41 @@ def test_validate_shapes_and_messages():
 def test_execute_needs_cuda_tensors():
     with pytest.raises(ValueError, match="CUDA float32"):
         ort_ep.execute("relu", torch.zeros(4))
+
+
+def test_c_abi_validation_precedes_any_launch():
+    """The doe_ep_* entry points reject bad calls on the host: nothing below
+    reaches a kernel (the fake pointers are never dereferenced)."""
+    import ctypes as C
+
+    from doe_b200 import _abi as abi
+
+    lib = abi.lib()
+    x, y = 0x10000, 0x20000  # 16-byte aligned, disjoint for n <= 4096
+    inval = abi.DOE_INVALID_ARGUMENT
+    assert lib.doe_ep_unary_f32(9, x, y, 4, None) == inval
+    assert "unknown op" in abi.op_error()
+    assert lib.doe_ep_unary_f32(abi.EP_RELU, None, y, 4, None) == inval
+    assert lib.doe_ep_unary_f32(abi.EP_RELU, x, x + 4, 100, None) == inval
+    assert "overlap" in abi.op_error()
+    assert lib.doe_ep_unary_f32(abi.EP_RELU, None, None, 0, None) == abi.DOE_OK  # empty: nothing to do
+    assert lib.doe_ep_binary_f32(5, x, x, y, 4, None) == inval
+    assert lib.doe_ep_binary_f32(abi.EP_ADD, x, y + 8, y, 16, None) == inval  # b partly overlaps y
+    assert lib.doe_ep_softmax_f32(x, y, 1 << 40, 4096, None) == inval
+    assert lib.doe_ep_softmax_f32(None, None, 0, 5, None) == abi.DOE_OK
+    assert lib.doe_ep_softmax_f32(None, None, 5, 0, None) == abi.DOE_OK  # empty axis (ExecuteSoftmax)
+    assert lib.doe_ep_layernorm_f32(x, x + 64, -1.0, y, 1, 4, None) == inval
+    assert "epsilon" in abi.op_error()
+    assert lib.doe_ep_layernorm_f32(x, y + 16, 1e-5, y, 2, 16, None) == inval  # scale inside y
+    assert lib.doe_ep_concat_f32(x, x + 4096, x + 32, 1, 4, 4, 4, None) == inval  # y over a
+    assert lib.doe_ep_matmul_f32(x, x, None, y, 4, 4, 4, 2, None) == inval
+    assert "flags" in abi.op_error()
+    assert lib.doe_ep_matmul_f32(x, x, None, y, 1 << 31, 4, 4, 0, None) == inval
+    assert lib.doe_ep_matmul_f32(x, x, None, y, 65535 * 128 + 1, 1, 1, 0, None) == inval
+    assert lib.doe_ep_matmul_f32(x, x + 0x1000, None, x + 8, 4, 4, 4, 0, None) == inval  # y over a
+    assert lib.doe_ep_matmul_f32(None, None, None, None, 0, 4, 4, 0, None) == abi.DOE_OK
+    rc = lib.doe_ep_gemm_relu_gemm_f32(x, x, x, x, x, y, 2, 2, 2, 2, None)
+    assert rc == inval and "workspace" in abi.op_error()
+    assert lib.doe_ep_gemm_relu_gemm_workspace_bytes(32, 1000) == 128000
+    l = abi.Launch(None, None, 0, None)
+    assert lib.doe_ep_gemm_relu_gemm_f32(x, x, x, x, x, y, 0, 2, 2, 2, C.byref(l)) == abi.DOE_OK
