@@ -40,6 +40,10 @@ FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
+# the headline metric; both arms (ours and --impl reference) report it
+METRIC = "decode-attn HBM GB/s (config 3 paged GQA decode, fused append)"
+
+
 def clock_max_mhz(index: int = 0):
     """The SM's maximum clock from NVML (None when NVML is unavailable)."""
     try:
@@ -635,7 +639,7 @@ def run_reference(args):
         samples.append(s)
     v = float(np.mean(vals))
     line = {
-        "impl": "reference", "metric": "decode-attn HBM GB/s (config 3 paged GQA decode)",
+        "impl": "reference", "metric": METRIC,
         "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": float(np.mean([s["seconds"] for s in samples]) * 1e3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
@@ -774,7 +778,7 @@ def main():
             "algorithmic_bytes_per_launch": head["bytes_per_step"]["total"]}
     if rank == 0:
         line = {
-            "metric": "decode-attn HBM GB/s (config 3 paged GQA decode, fused append)",
+            "metric": METRIC,
             "value": head["gbs"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": head["ms_per_step"], "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded)",
