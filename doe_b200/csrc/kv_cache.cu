@@ -9,8 +9,10 @@
 //   stitch        : bench/tools/attention_kv_axis_sharded_stitch.py:46-90
 //   rope          : bench/inference-pipeline/kernels/rope.wgsl:12-35
 //
-// All copies are bit-exact; the int8 quantiser uses IEEE division and
-// round-to-nearest-even so it matches the CPU definition bit for bit.
+// All copies are bit-exact.  The int8 quantiser (quantize_s8, div127 in
+// common.cuh) forms its quotients from correctly rounded reciprocals and one
+// exact residual correction, and rounds half to even, so it gives the CPU
+// definition's IEEE-division results bit for bit.
 #include "common.cuh"
 
 namespace doe {
