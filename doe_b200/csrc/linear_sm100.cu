@@ -15,6 +15,16 @@
 // TMEM; otherwise it writes its f32 partial tile to the workspace and the
 // last contributor to arrive sums all the tile's partials in contributor
 // order (the result does not depend on arrival order) and runs the epilogue.
+// Work split (cluster): when there are at most half as many tiles as SMs, a
+// tile's k range is split over a cluster of up to 4 CTAs instead (the largest
+// size whose clusters are all resident at once).  Ranks 1-3 send their f32
+// accumulators into rank 0's shared memory with st.async over distributed
+// shared memory; rank 0 sums them in rank order and runs the epilogue.
+// Epilogues: store into up to three column segments (bf16, f16 or f32),
+// SwiGLU over interleaved 64-row gate / up blocks, or f32 plus a residual.
+// Launched with programmatic dependent launch: the first ring of weight
+// boxes is issued before griddepcontrol.wait, since no kernel of a step
+// writes the weights.
 //
 //   warp 0     TMA producer: per k block one 128 x 64 weight box and one
 //              32 x 64 activation box (rows past `batch` read as zero) into

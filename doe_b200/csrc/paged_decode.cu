@@ -1,5 +1,7 @@
 // paged_decode.cu -- batched GQA decode over a paged KV cache (f16 or int8),
-// split-K over the KV length with a combine kernel, fused new-token append.
+// split-K over the KV length with the splits stitched by the last CTA of each
+// (sequence, kv head) to finish, fused new-token append.  Also the combine
+// kernel of the f32 decode's many-split path (launch_combine_natural).
 //
 // Semantics: attention_head256_f16kv.wgsl with query_len 1 (every key of the
 // sequence active), GQA kv_head = h / (H / Hkv) (…wgsl:46-49), paged rows
@@ -40,7 +42,7 @@ struct PagedDecodeArgs {
   float* out;               // [B, H, D] f32, or bf16 storage when out_bf16
   float* part_o;            // [B*Hkv*max_splits, GROUP, D]
   float* part_ml;           // [B*Hkv*max_splits, GROUP, 2]
-  unsigned* counters;       // [B*Hkv] arrivals per (b, g); zeroed before each launch
+  unsigned* counters;       // [B*Hkv] arrivals per (b, g); zero at launch, left zero by the stitch
   int32_t* status;
   const float* freq_cis;    // RoPE table [rope_positions, D/2, {cos, sin}] or null
   int rope_positions;
