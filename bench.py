@@ -238,6 +238,16 @@ def sharded(make, world, rank):
     return workloads.subset(gw, mine), gw
 
 
+def strong_split(w, world, rank):
+    """This rank's shard of ONE batch split by sequence over `world` ranks
+    (LPT on token counts): the same sequences on more GPUs, strong scaling."""
+    from doe_b200 import shard, workloads
+
+    if world == 1:
+        return w, w
+    return workloads.subset(w, shard.lpt_assign(w.seq_lens, world)[rank]), w
+
+
 def measure_paged(w, fill_seed, steps, warmup, world, pk, split_pages=0, gw=None):
     gw = gw if gw is not None else w
     cache, dev = build_paged(w, fill_seed)
@@ -261,7 +271,7 @@ def measure_paged(w, fill_seed, steps, warmup, world, pk, split_pages=0, gw=None
     return res, cache, dev
 
 
-def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512):
+def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512, gw=None):
     import torch
 
     from doe_b200 import ops
@@ -280,12 +290,15 @@ def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512):
     local_ms = total
     total, = max_over_ranks(world, [total])
     assert int(status.item()) == 0
-    rows = w.num_seqs * chunk * w.num_kv_heads
-    rd = 2 * rows * w.head_dim * 2 + w.num_seqs * 4
-    wr = 2 * rows * (w.head_dim + 2)
-    gbs = world * (rd + wr) * steps / (total / 1e3) / 1e9
-    return {"ms_per_step": total / steps, "gbs": gbs, "bytes_per_step": rd + wr,
-            "frac": (rd + wr) * steps / (local_ms / 1e3) / 1e9 / pk["hbm_gbs"]}
+    def nbytes(seqs):
+        rows = seqs * chunk * w.num_kv_heads
+        return 2 * rows * w.head_dim * 2 + seqs * 4 + 2 * rows * (w.head_dim + 2)
+
+    gw = gw if gw is not None else w
+    job = nbytes(gw.num_seqs) * (world if gw is w else 1)
+    return {"ms_per_step": total / steps, "gbs": job * steps / (total / 1e3) / 1e9,
+            "bytes_per_step": nbytes(w.num_seqs), "job_bytes_per_step": job,
+            "frac": nbytes(w.num_seqs) * steps / (local_ms / 1e3) / 1e9 / pk["hbm_gbs"]}
 
 
 def measure_f32(steps, warmup, world, pk):
@@ -551,9 +564,18 @@ def measure_e2e(w, cache, steps, warmup, world, gw=None):
     be.flush_queue()
     elapsed = time.perf_counter() - t0
     elapsed, = max_over_ranks(world, [elapsed])
-    # the e2e output must equal the operator path's output
-    ok = bool(np.isfinite(hout.numpy()).all())
     be.close()
+    # the e2e output must equal the operator path's output on the same inputs:
+    # the same kernel and split plan, splits stitched in split order, so the
+    # bits agree
+    from doe_b200 import ops
+
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    ref = ops.paged_decode(cache, t(w.q), t(w.seq_lens), w.scale, new_k=t(w.new_k), new_v=t(w.new_v))
+    torch.cuda.synchronize()
+    ok = bool(np.array_equal(hout.numpy(), ref.cpu().numpy()))
+    if not ok:
+        raise RuntimeError("e2e: the doe_cuda_dispatch output differs from the operator path's output")
     sb = gw.step_bytes()["total"]
     return {"value": sb * steps / elapsed / 1e9, "unit": "GB/s",
             "tokens_per_s": gw.tokens_per_step() * steps / elapsed,
@@ -562,7 +584,7 @@ def measure_e2e(w, cache, steps, warmup, world, gw=None):
             "d2h_bytes_per_step": int(out_bytes),
             "timer": "host perf_counter around K steps (each step: 4 deferred H2D writes from pinned memory, "
                      "dispatch, deferred D2H capture, alternating two buffer sets; one flush at the end)",
-            "output_finite": ok}
+            "output_equals_operator_path": ok}
 
 
 # ---------------------------------------------------------------------------
@@ -708,14 +730,17 @@ def main():
         elif args.only == "f32":
             r = measure_f32(args.steps, args.warmup, world, pk)
         elif args.only == "append":
-            w4, _ = sharded(lambda r: workloads.paged_int8(seed=3 + r, num_seqs=args.seqs or 32), world, rank)
+            w4, g4 = strong_split(workloads.paged_int8(num_seqs=args.seqs or 32), world, rank)
             cache4, _ = build_paged(w4, 3)
             r = {"config": "config 4b: 32 x 512 tokens quantised into the paged cache",
-                 **measure_chunk_append(w4, cache4, args.steps, args.warmup, world, pk)}
+                 "scaling": "strong" if world > 1 else None,
+                 **measure_chunk_append(w4, cache4, args.steps, args.warmup, world, pk, gw=g4)}
         else:
-            w4, g4 = sharded(lambda r: workloads.paged_int8(seed=3 + r, num_seqs=args.seqs or 32),
-                             world, rank)
+            w4, g4 = strong_split(workloads.paged_int8(num_seqs=args.seqs or 32), world, rank)
             r, _, _ = measure_paged(w4, 3, args.steps, args.warmup, world, pk, args.split_pages, g4)
+            r = {"config": "config 4: 32 seqs, ctx U[8192,32768] seed 3, int8 KV + f16 scales",
+                 "scaling": "strong" if world > 1 else None,
+                 "parallelism": f"the 32 sequences split over {world} ranks (LPT on tokens)", **r}
         if rank == 0:
             print(json.dumps({"only": args.only, **r}))
         if world > 1:
@@ -735,16 +760,22 @@ def main():
 
     extras = {}
     if not args.no_extras:
-        w4, g4 = sharded(lambda r: workloads.paged_int8(seed=3 + r), world, rank)
+        # config 4 as BASELINE.json states it: the same 32 sequences split by
+        # sequence over the N GPUs (strong scaling)
+        w4, g4 = strong_split(workloads.paged_int8(), world, rank)
         r4, cache4, _ = measure_paged(w4, 3, max(5, args.steps // 2), 3, world, pk, 0, g4)
-        ca = measure_chunk_append(w4, cache4, 5, 3, world, pk)
+        ca = measure_chunk_append(w4, cache4, 5, 3, world, pk, gw=g4)
         del cache4
         torch.cuda.empty_cache()
+        par4 = (f"the 32 sequences split over {world} ranks (LPT on tokens, {w4.num_seqs} on rank 0)"
+                if world > 1 else "one GPU")
         extras["int8_decode"] = {"config": "config 4: 32 seqs, ctx U[8192,32768] seed 3, int8 KV + f16 scales",
+                                 "parallelism": par4, "scaling": "strong" if world > 1 else None,
                                  "gbs": r4["gbs"], "tokens_per_s": r4["tokens_per_s"],
                                  "ms_per_step": r4["ms_per_step"], "kernel_frac": r4["frac"],
-                                 "bytes_per_step": r4["bytes_per_step"]["total"]}
+                                 "bytes_per_step": r4["global_bytes_per_step"]}
         extras["int8_chunk_append"] = {"config": "config 4b: 32 x 512 tokens quantised into the paged cache",
+                                       "parallelism": par4, "scaling": "strong" if world > 1 else None,
                                        **ca}
         extras["f32_decode"] = {"config": "config 1: 8 heads, D 64, 512 tokens, f32", **measure_f32(20, 5, world, pk)}
         try:

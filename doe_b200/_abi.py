@@ -34,6 +34,13 @@ DOE_DEVICE_ERR_TIMEOUT = 0x8
 DOE_KV_F16 = 0
 DOE_KV_INT8 = 1
 
+# set_upload_behavior usage modes
+DOE_UPLOAD_COPY_DST_COPY_SRC = 0
+DOE_UPLOAD_COPY_DST = 1
+
+# bytes of the scratch array behind doe_attention_decode_f32_noalloc
+DOE_NOALLOC_SCRATCH_BYTES = 1 << 18
+
 
 class DoeError(RuntimeError):
     def __init__(self, fn: str, rc: int, msg: str = ""):
@@ -135,6 +142,7 @@ SIGNATURES = {
     "doe_cuda_prewarm_kernel": (_I, [_P, C.c_char_p]),
     "doe_cuda_prewarm_upload": (_I, [_P, _U64]),
     "doe_cuda_set_queue_sync_mode": (_I, [_P, _I]),
+    "doe_cuda_set_upload_behavior": (_I, [_P, _I, C.c_uint32]),
     "doe_cuda_set_gpu_timestamp_mode": (_I, [_P, _I]),
     "doe_cuda_flush": (_I, [_P, C.POINTER(_U64)]),
     "doe_attention_decode_f32_workspace_bytes": (_U64, [_U32, _U32, _U32]),

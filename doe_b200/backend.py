@@ -126,6 +126,12 @@ class CudaBackend:
     def prewarm_upload_path(self, max_upload_bytes: int) -> None:
         self._check("doe_cuda_prewarm_upload", self._lib.doe_cuda_prewarm_upload(self._h, max_upload_bytes))
 
+    def set_upload_behavior(self, mode: int, submit_every: int) -> None:
+        """Flush the queue after every `submit_every` buffer writes (0 counts as
+        1; 2**32 - 1 never); `mode` is the upload usage (DOE_UPLOAD_*)."""
+        self._check("doe_cuda_set_upload_behavior",
+                    self._lib.doe_cuda_set_upload_behavior(self._h, int(mode), int(submit_every)))
+
     def set_queue_sync_mode(self, per_command: bool) -> None:
         self._check("doe_cuda_set_queue_sync_mode",
                     self._lib.doe_cuda_set_queue_sync_mode(self._h, int(per_command)))

@@ -64,6 +64,11 @@ struct doe_cuda_ctx {
   int32_t* status_host = nullptr;  // pinned
   bool per_command_sync = false;
   bool timestamps = false;
+  // set_upload_behavior: the queue is flushed after every `submit_every`
+  // buffer writes (UINT32_MAX: never, the reference's lazy default)
+  int upload_mode = 0;
+  uint32_t upload_submit_every = UINT32_MAX;
+  uint32_t pending_uploads = 0;
   cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
   bool timing_open = false;
   std::string last_error;
@@ -174,6 +179,16 @@ int ensure_buffer(doe_cuda_ctx* ctx, uint64_t handle, uint64_t bytes, DevBuffer*
   b.used = true;
   *out = &b;
   return DOE_OK;
+}
+
+// One more buffer write was queued: flush the queue when set_upload_behavior's
+// submit_every writes have accumulated (runtime/zig/src/backend/vulkan/
+// backend_execute.zig:51-55).
+int upload_submitted(doe_cuda_ctx* ctx) {
+  if (ctx->upload_submit_every == UINT32_MAX) return DOE_OK;
+  if (++ctx->pending_uploads < ctx->upload_submit_every) return DOE_OK;
+  ctx->pending_uploads = 0;
+  return sync_stream(ctx);
 }
 
 int ensure_staging(doe_cuda_ctx* ctx, uint64_t bytes) {
@@ -348,9 +363,59 @@ int run_attention_prefill_wgsl(const DispatchCtx& d) {
                                                          u[1], u[2], scale, &l));
 }
 
+// Rounds f32 query rows to f16 (nearest even), the operand type of the
+// tcgen05 prefill; four elements per thread.
+__global__ void query_to_f16_kernel(const float4* __restrict__ x, uint2* __restrict__ y, uint64_t n4) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    const float4 v = __ldcs(x + i);
+    const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<const uint32_t*>(&lo);
+    o.y = *reinterpret_cast<const uint32_t*>(&hi);
+    y[i] = o;
+  }
+}
+
+// The exec-v1 prefill ops in the form the tensor-core prefill computes: every
+// query row of a prompt against the same prompt's keys, head_dim 128, dense
+// [pos, Hkv, D] K/V from position 0, no softcap, window or kv_len buffer.
+bool prefill_shape(const doe_attn_uniforms& u) {
+  return u.head_dim == 128 && u.query_len == u.seq_len && u.seq_len > 0 && u.start_pos == 0 &&
+         u.kv_start == 0 && u.kv_layout == 0 && u.kv_len_source == 0 && u.attn_softcap == 0.0f &&
+         u.sliding_window == 0 && u.num_kv_heads != 0 && u.num_heads % u.num_kv_heads == 0;
+}
+
+// attention_prefill / attention_prefill_kv_axis_sharded on the tcgen05 prefill:
+// Q is rounded to f16 into the context workspace (the kernel's operands are
+// f16; K and V already are), then the prefill writes the f32 output rows.
+int run_prefill_tc(const DispatchCtx& d, const doe_attn_uniforms& u, const Bound& q, const Bound& k,
+                   const Bound& v, const Bound& o) {
+  const uint64_t S = u.seq_len, H = u.num_heads, Hkv = u.num_kv_heads, D = u.head_dim;
+  DOE_TRY(need(d, k, S * Hkv * D * 2, "K"));
+  DOE_TRY(need(d, v, S * Hkv * D * 2, "V"));
+  const uint64_t n = S * H * D;
+  DOE_TRY(ensure_workspace(d.ctx, n * 2));
+  const int threads = 256;
+  const uint64_t want = (n / 4 + threads - 1) / threads;
+  const unsigned blocks = (unsigned)(want < 4096 ? want : 4096);
+  query_to_f16_kernel<<<blocks, threads, 0, d.ctx->stream>>>(reinterpret_cast<const float4*>(q.ptr),
+                                                            static_cast<uint2*>(d.ctx->workspace), n / 4);
+  DOE_TRY(cu(d.ctx, cudaGetLastError(), "query_to_f16_kernel"));
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_attention_prefill_f16(d.ctx->workspace, k.ptr, v.ptr, (float*)o.ptr, u.seq_len,
+                                                    u.num_heads, u.num_kv_heads, u.head_dim, u.scale,
+                                                    u.is_causal ? 1u : 0u, nullptr, 0, 0, &l));
+}
+
+bool aligned16(const Bound& b) { return (reinterpret_cast<uintptr_t>(b.ptr) & 15) == 0; }
+
 // attention_head{256,512}_f16kv.wgsl and exec-v1 attention ops: the 15-word
 // uniform; Q f32, K f16, V f16, output f32, kv_len_buffer, page_table.
-int run_attention_online(const DispatchCtx& d, uint32_t fixed_head_dim) {
+// `prefill`: the exec-v1 prefill names, which take the tcgen05 prefill when
+// the uniform is a whole-prompt prefill it computes (prefill_shape) and the
+// bindings are 16-byte aligned; other uniforms run the head256 kernel.
+int run_attention_online(const DispatchCtx& d, uint32_t fixed_head_dim, bool prefill = false) {
   doe_attn_uniforms u;
   DOE_TRY(read_uniform(d, 0, &u, 60));
   u.pad = 0;
@@ -368,10 +433,12 @@ int run_attention_online(const DispatchCtx& d, uint32_t fixed_head_dim) {
   DOE_TRY(need(d, q, qbytes, "Q"));
   DOE_TRY(need(d, o, qbytes, "output"));
   if (u.kv_len_source != 0) DOE_TRY(need(d, klb, 4, "kv_len_buffer"));
-  doe_launch l = make_launch(d.ctx);
   if (u.num_kv_heads == 0 || u.num_heads % u.num_kv_heads != 0 || u.head_dim == 0 ||
       u.head_dim > 512 || u.kv_layout > 2)
     return fail(d.ctx, DOE_INVALID_ARGUMENT, "%s: inconsistent uniform block", d.kernel);
+  if (prefill && prefill_shape(u) && aligned16(q) && aligned16(k) && aligned16(v) && aligned16(o))
+    return run_prefill_tc(d, u, q, k, v, o);
+  doe_launch l = make_launch(d.ctx);
   GenericAttnArgs a;
   std::memset(&a, 0, sizeof(a));
   a.u = u;
@@ -558,6 +625,7 @@ enum class Op {
   kDecodeWgsl,
   kPrefillWgsl,
   kOnline,
+  kPrefill,
   kOnline256,
   kOnline512,
   kKvWrite,
@@ -585,7 +653,8 @@ Op lookup(const char* k) {
       {"attention_head512_f16kv.wgsl", Op::kOnline512},
       {"attention", Op::kOnline},
       {"attention_sliding", Op::kOnline},
-      {"attention_prefill", Op::kOnline},
+      {"attention_prefill", Op::kPrefill},
+      {"attention_prefill_kv_axis_sharded", Op::kPrefill},
       {"kv_write", Op::kKvWrite},
       {"kv_write_shared", Op::kKvWrite},
       {"kv_read", Op::kKvRead},
@@ -693,6 +762,7 @@ int doe_cuda_buffer_write(doe_cuda_ctx* ctx, uint64_t handle, uint64_t offset, c
   ctx->staging_used += (size + 255) / 256 * 256;
   if (rc == DOE_OK) rc = cu(ctx, cudaEventRecord(b->ev_written, ctx->copy), "cudaEventRecord");
   if (rc == DOE_OK) b->write_pending = true;
+  if (rc == DOE_OK) rc = upload_submitted(ctx);
   return rc;
 }
 
@@ -715,6 +785,20 @@ int doe_cuda_buffer_write_async(doe_cuda_ctx* ctx, uint64_t handle, uint64_t off
              "cudaMemcpyAsync(H2D)"));
   DOE_TRY(cu(ctx, cudaEventRecord(b->ev_written, ctx->copy), "cudaEventRecord"));
   b->write_pending = true;
+  return upload_submitted(ctx);
+}
+
+int doe_cuda_set_upload_behavior(doe_cuda_ctx* ctx, int mode, uint32_t submit_every) {
+  if (!ctx) return DOE_INVALID_ARGUMENT;
+  if (mode != DOE_UPLOAD_COPY_DST_COPY_SRC && mode != DOE_UPLOAD_COPY_DST)
+    return fail(ctx, DOE_INVALID_ARGUMENT, "set_upload_behavior: unknown usage mode %d", mode);
+  ctx->upload_mode = mode;
+  ctx->upload_submit_every = submit_every > 0 ? submit_every : 1;
+  if (ctx->pending_uploads >= ctx->upload_submit_every) {
+    ctx->pending_uploads = 0;
+    DOE_TRY(bind_device(ctx));
+    return sync_stream(ctx);
+  }
   return DOE_OK;
 }
 
@@ -888,6 +972,7 @@ int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel, const char* entry_p
       case Op::kDecodeWgsl: rc = run_attention_decode(d); break;
       case Op::kPrefillWgsl: rc = run_attention_prefill_wgsl(d); break;
       case Op::kOnline: rc = run_attention_online(d, 0); break;
+      case Op::kPrefill: rc = run_attention_online(d, 0, true); break;
       case Op::kOnline256: rc = run_attention_online(d, 256); break;
       case Op::kOnline512: rc = run_attention_online(d, 512); break;
       case Op::kKvWrite: rc = run_kv_write(d); break;

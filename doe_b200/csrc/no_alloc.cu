@@ -15,9 +15,16 @@
 //     lives until the process exits on every device that loads the library.
 //     A problem whose partials would not fit (num_heads x splits x
 //     (head_dim + 2) floats > 256 KiB) is rejected with DOE_INVALID_ARGUMENT.
+//     The limit is checked with the workspace count of the split path for
+//     every problem, also for those whose splits would fit one thread-block
+//     cluster and never touch the array, so the sizes accepted do not depend
+//     on which launch form a device can schedule.
 //   * The first call on a device looks up the array's device address
 //     (cudaGetSymbolAddress) with that device current and caches it; make that
-//     first call before any stream capture on the device.
+//     first call before any stream capture on the device.  The cached address
+//     lives as long as the process: after cudaDeviceReset (or a reset of the
+//     device's primary context by an embedder) it is stale, so the library
+//     must not be used on that device again.
 //   * Every call shares the one array and leaves the previous call's partials
 //     in it.  Calls whose kernels overlap on the GPU (different streams with
 //     no ordering between them) race on the array and must be serialised by

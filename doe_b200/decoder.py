@@ -245,6 +245,16 @@ class Decoder:
             t(li, "out", x)
         return x
 
+    def check(self) -> None:
+        """Raise on device-side errors of the steps run so far: a tensor-parallel
+        reduction timeout (TpTimeoutError, the peers then unusable) or any
+        other DOE_DEVICE_ERR_* bit.  Reads the status word: not inside a capture."""
+        if self.peers is not None:
+            self.peers.check_status(self.status)
+        value = int(self.status.item())
+        if value:
+            raise RuntimeError(f"decoder step: device status {value:#x}")
+
     def launches_per_step(self) -> int:
         """Kernels of this library per step."""
         return 7 * self.cfg.layers + (1 if self.peers is not None else 0)

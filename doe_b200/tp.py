@@ -26,8 +26,18 @@ class _DevArray:
                                          "version": 3, "strides": None}
 
 
+class TpTimeoutError(RuntimeError):
+    """A tensor-parallel reduction gave up waiting for a peer (DOE_DEVICE_ERR_TIMEOUT)."""
+
+
 class TpPeers:
-    """This rank's peer buffer and every other rank's, mapped into this process."""
+    """This rank's peer buffer and every other rank's, mapped into this process.
+
+    After a reduction reports DOE_DEVICE_ERR_TIMEOUT, its sums and norms are
+    not valid (a late peer's slot was read before it was complete) and the
+    ranks' epochs no longer agree: check_status() raises TpTimeoutError and
+    marks these peers unusable, so that every later reduce_rmsnorm raises
+    until new peer buffers are made on every rank."""
 
     def __init__(self, rows: int, cols: int, group=None, device=None):
         self.rows, self.cols = rows, cols
@@ -68,9 +78,25 @@ class TpPeers:
             ptr = lib.doe_tp_slot_ptr(self._own, s, rows, cols)
             self.slots.append(torch.as_tensor(_DevArray(ptr, (rows, cols), "<f4"), device=self.device))
 
+    failed = False
+
+    def check_status(self, status) -> None:
+        """Raise TpTimeoutError if the launch status word (a device int32 tensor
+        or its value) holds DOE_DEVICE_ERR_TIMEOUT; the peers are then unusable.
+        Reads the device word, so call it after the step, outside graph capture."""
+        value = int(status.item()) if hasattr(status, "item") else int(status)
+        if value & abi.DOE_DEVICE_ERR_TIMEOUT:
+            self.failed = True
+            raise TpTimeoutError(
+                f"rank {self.rank}: a tensor-parallel reduction timed out waiting for a peer "
+                f"(status {value:#x}); its outputs are invalid and the peer buffers must be "
+                "recreated on every rank")
+
     def reduce_rmsnorm(self, slot: int, h_out: torch.Tensor, gamma=None, eps: float = 0.0, xn_out=None,
                        status=None, stream=None) -> None:
         """h_out = sum over ranks of slot `slot`; with gamma also xn_out = RMSNorm(h_out) in bf16."""
+        if self.failed:
+            raise TpTimeoutError(f"rank {self.rank}: peer buffers unusable after a reduction timeout")
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         l = abi.Launch(s.cuda_stream, None, 0, status.data_ptr() if status is not None else None)
         abi.check("doe_tp_reduce_rmsnorm", abi.lib().doe_tp_reduce_rmsnorm(

@@ -145,9 +145,17 @@ int doe_cuda_buffer_device_ptr(doe_cuda_ctx* ctx, uint64_t handle, void** out);
  * "attention-prefill.wgsl", "attention_head256_f16kv.wgsl",
  * "attention_head512_f16kv.wgsl", "rope.wgsl") or an exec-v1 op name
  * (runtime/zig/src/doe_wgsl/emit_csl_exec_v1.zig:113-180: "attention",
- * "attention_sliding", "attention_prefill", "kv_write", "kv_write_shared",
- * "kv_read", "rope").  Unknown names return DOE_UNSUPPORTED with a message;
- * nothing runs on the host instead.                                        */
+ * "attention_sliding", "attention_prefill", "attention_prefill_kv_axis_sharded",
+ * "kv_write", "kv_write_shared", "kv_read", "rope").  Unknown names return
+ * DOE_UNSUPPORTED with a message; nothing runs on the host instead.
+ * The two prefill op names take the tcgen05 prefill (doe_attention_prefill_f16,
+ * Q rounded to f16 first) when the 15-word uniform describes a whole prompt:
+ * head_dim 128, query_len == seq_len, start_pos == kv_start == 0, dense
+ * layout, kv_len from the uniform, no softcap and no window, with 16-byte
+ * aligned bindings.  Other uniforms run the head256 kernel.  The kv-axis
+ * sharded form's per-shard partials and host stitch (a Cerebras PE layout,
+ * runtime/zig/src/doe_wgsl/emit_csl_semantic_ops.zig:560-600) collapse into
+ * the one kernel, which writes the stitched output rows.                  */
 int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel,
                       const char* entry_point, uint32_t x, uint32_t y,
                       uint32_t z, const doe_binding* bindings,
@@ -158,6 +166,18 @@ int doe_cuda_kernel_supported(const char* kernel);
 int doe_cuda_prewarm_kernel(doe_cuda_ctx* ctx, const char* kernel);
 /* prewarm_upload_path (backend_iface.zig:22): sizes the pinned staging area. */
 int doe_cuda_prewarm_upload(doe_cuda_ctx* ctx, uint64_t max_upload_bytes);
+/* set_upload_behavior (backend_iface.zig:17; the Vulkan backend's
+ * runtime/zig/src/backend/vulkan/backend_execute.zig:514-519, used at :51-55):
+ * after every `submit_every` buffer writes (doe_cuda_buffer_write and
+ * doe_cuda_buffer_write_async) the queue is flushed and waited for, like
+ * flush_queue; 0 counts as 1, UINT32_MAX never flushes (the default, the
+ * reference's lazy batching).  `mode` is the upload buffer usage
+ * (UploadBufferUsageMode, runtime/zig/src/backend/runtime_types.zig:6-9);
+ * device buffers here are always copy sources and destinations, so it is
+ * validated and kept but changes nothing.                                  */
+#define DOE_UPLOAD_COPY_DST_COPY_SRC 0
+#define DOE_UPLOAD_COPY_DST 1
+int doe_cuda_set_upload_behavior(doe_cuda_ctx* ctx, int mode, uint32_t submit_every);
 /* set_queue_sync_mode (backend_iface.zig:19): 0 deferred, 1 per command.   */
 int doe_cuda_set_queue_sync_mode(doe_cuda_ctx* ctx, int per_command);
 /* set_gpu_timestamp_mode (backend_iface.zig:20): 0 off, 1 on.              */
@@ -447,7 +467,11 @@ int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out
  * All ranks make the same sequence of calls.  Two slots suffice when the
  * calls alternate them: a rank overwrites slot s only after a later reduce
  * saw every peer's flag, which peers raise after reading slot s.  Buffers
- * start zeroed; cols a multiple of 4; world <= 8.                          */
+ * start zeroed; cols a multiple of 4; world <= 8.
+ * After a call that set DOE_DEVICE_ERR_TIMEOUT, its h_out / xn_out are not
+ * valid (a late peer's slot may have been read before it was complete) and
+ * the ranks' epochs no longer agree: the peer buffers must be freed and
+ * created again, zeroed, on every rank before the next reduction.          */
 #define DOE_TP_MAX_RANKS 8
 typedef struct doe_tp_peers {
   uint32_t rank;
@@ -479,9 +503,15 @@ int doe_tp_reduce_rmsnorm(const doe_tp_peers* peers, uint32_t slot, const void* 
  * array inside the library, held on every device that loads it until the
  * process exits.  The call allocates nothing: no cudaMalloc / cudaFree.
  *   - Problems whose partials exceed DOE_NOALLOC_SCRATCH_BYTES (num_heads x
- *     splits x (head_dim + 2) floats) return DOE_INVALID_ARGUMENT.
+ *     splits x (head_dim + 2) floats, as doe_attention_decode_f32_workspace_bytes
+ *     counts them) return DOE_INVALID_ARGUMENT.  The limit applies to every
+ *     problem, also to those whose splits fit one thread-block cluster and
+ *     keep their partials in shared memory, so whether a size is accepted
+ *     does not depend on the device.
  *   - The first call on a device looks up the array's device address; make
- *     it before any stream capture on that device.
+ *     it before any stream capture on that device.  The address is kept for
+ *     the life of the process: the library must not be used on a device
+ *     after cudaDeviceReset (or any reset of its primary context).
  *   - All calls share the array: calls whose kernels may overlap on the GPU
  *     race and must be ordered by the caller.
  * `stream` is a cudaStream_t (NULL = legacy default stream).               */

@@ -42,7 +42,7 @@ def test_abi_version_and_kernel_table():
     assert lib.doe_cuda_abi_version() == 1
     for k in ("attention-decode.wgsl", "attention-prefill.wgsl", "attention_head256_f16kv.wgsl",
               "attention_head512_f16kv.wgsl", "attention", "attention_sliding", "attention_prefill",
-              "kv_write", "kv_write_shared", "kv_read", "rope", "rope.wgsl",
+              "attention_prefill_kv_axis_sharded", "kv_write", "kv_write_shared", "kv_read", "rope", "rope.wgsl",
               "attention_paged_decode", "kv_append_paged", "attention_stitch"):
         assert lib.doe_cuda_kernel_supported(k.encode()) == 1, k
     for k in ("matmul", "rmsnorm", "attention_linear", "", "attention-decode"):

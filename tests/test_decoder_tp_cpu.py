@@ -111,3 +111,24 @@ def test_pack_gate_up_blocks():
     w = decoder.pack_gate_up(gate, up)
     assert torch.equal(w[0:64], gate[0:64]) and torch.equal(w[64:128], up[0:64])
     assert torch.equal(w[128:192], gate[64:128]) and torch.equal(w[192:256], up[64:128])
+
+
+def test_tp_timeout_status_poisons_the_peers():
+    """A reduction that reports DOE_DEVICE_ERR_TIMEOUT makes check_status raise
+    and every later reduce_rmsnorm refuse to run (no GPU: the check is host
+    logic on the status word's value)."""
+    import pytest
+
+    from doe_b200 import _abi as abi
+    from doe_b200.tp import TpPeers, TpTimeoutError
+
+    peers = TpPeers.__new__(TpPeers)
+    peers.rank = 1
+    peers.check_status(0)
+    peers.check_status(abi.DOE_DEVICE_ERR_PAGE)  # not a reduction failure
+    assert not peers.failed
+    with pytest.raises(TpTimeoutError):
+        peers.check_status(abi.DOE_DEVICE_ERR_TIMEOUT | abi.DOE_DEVICE_ERR_PAGE)
+    assert peers.failed
+    with pytest.raises(TpTimeoutError):
+        peers.reduce_rmsnorm(0, None)

@@ -255,3 +255,82 @@ def test_queued_steps_on_alternating_buffers_match_synchronous_steps(be):
             assert np.array_equal(outs[i].numpy().view(np.float32), expected[i]), f"step {i}"
     finally:
         b2.close()
+
+
+def _uniform15(**u) -> np.ndarray:
+    names = ("num_heads", "num_kv_heads", "head_dim", "seq_len", "query_len", "scale", "is_causal",
+             "start_pos", "attn_softcap", "sliding_window", "kv_len_source", "kv_start", "page_size",
+             "kv_layout")
+    return np.array([np.float32(u[n]).view(np.uint32) if isinstance(u[n], float) else u[n] for n in names]
+                    + [0], np.uint32)
+
+
+@pytest.fixture(scope="module")
+def prefill_config2_case():
+    """Config 2 shapes with f32 queries (not f16-representable, so the
+    dispatch's f16 rounding of Q is exercised) and the oracle over every row."""
+    w = workloads.prefill_f16()
+    S, H, D = w.q.shape
+    q = np.random.default_rng(12).standard_normal((S, H, D), dtype=np.float32) * np.float32(0.5)
+    u = dict(num_heads=H, num_kv_heads=w.k.shape[1], head_dim=D, seq_len=S, query_len=S,
+             scale=float(np.float32(w.scale)), is_causal=1, start_pos=0, attn_softcap=0.0,
+             sliding_window=0, kv_len_source=0, kv_start=0, page_size=16, kv_layout=0)
+    ref = oracle.attention_online_f16kv(u, q, w.k.view(np.uint16), w.v.view(np.uint16))
+    return w, q, u, ref
+
+
+@pytest.mark.parametrize("name", ["attention_prefill", "attention_prefill_kv_axis_sharded"])
+def test_exec_v1_prefill_runs_tcgen05_prefill(be, name, prefill_config2_case):
+    """The exec-v1 prefill ops (emit_csl_exec_v1.zig:118,125) on config 2's
+    shapes take the tensor-core prefill: the launch list holds prefill_kernel,
+    and every output row is within 2e-3 of the oracle."""
+    w, q, u, ref = prefill_config2_case
+    for h, arr in ((80, _uniform15(**u)), (81, q), (82, w.k), (83, w.v)):
+        be.execute_buffer_write_bytes(h, 0, arr)
+    be.flush_queue()
+    binds = [Bind(0, 80, size=64), Bind(1, 81), Bind(2, 82), Bind(3, 83), Bind(4, 84, size=q.nbytes)]
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        be.execute_kernel_dispatch(name, binds)
+        be.flush_queue()
+    kernels = [e.key for e in prof.key_averages()]
+    assert any("prefill_kernel" in k for k in kernels), kernels
+    assert not any("attn_online_generic" in k for k in kernels), kernels
+    out = np.frombuffer(be.capture_buffer(84, 0, q.nbytes), np.float32).reshape(q.shape)
+    within(out, ref, 2e-3)
+
+
+def test_exec_v1_prefill_other_uniforms_run_head256_kernel(be):
+    """attention_prefill with a softcap, a query chunk after earlier keys and
+    GQA is not a whole-prompt prefill: it runs the head256 kernel and matches
+    the oracle at the f32 bound."""
+    g = np.random.default_rng(14)
+    S, Q0, H, Hkv, D = 96, 64, 4, 2, 128
+    q = g.standard_normal((S - Q0, H, D), dtype=np.float32)
+    k = g.standard_normal((S, Hkv, D), dtype=np.float32).astype(np.float16)
+    v = g.standard_normal((S, Hkv, D), dtype=np.float32).astype(np.float16)
+    u = dict(num_heads=H, num_kv_heads=Hkv, head_dim=D, seq_len=S, query_len=S - Q0, scale=0.088,
+             is_causal=1, start_pos=Q0, attn_softcap=20.0, sliding_window=0, kv_len_source=0,
+             kv_start=0, page_size=16, kv_layout=0)
+    for h, arr in ((90, _uniform15(**u)), (91, q), (92, k), (93, v)):
+        be.execute_buffer_write_bytes(h, 0, arr)
+    binds = [Bind(0, 90, size=64), Bind(1, 91), Bind(2, 92), Bind(3, 93), Bind(4, 94, size=q.nbytes)]
+    be.execute_kernel_dispatch("attention_prefill", binds)
+    out = np.frombuffer(be.capture_buffer(94, 0, q.nbytes), np.float32).reshape(q.shape)
+    within(out, oracle.attention_online_f16kv(u, q, k.view(np.uint16), v.view(np.uint16)), 1e-5)
+
+
+def test_upload_behavior_flushes_every_n_writes(be):
+    """set_upload_behavior (backend_iface.zig:17): writes still land in order
+    with a flush every 2 writes; unknown usage modes are refused."""
+    g = np.random.default_rng(15)
+    be.set_upload_behavior(abi.DOE_UPLOAD_COPY_DST, 2)
+    chunks = [g.integers(0, 256, 4096, dtype=np.uint8) for _ in range(5)]
+    for i, c in enumerate(chunks):
+        be.execute_buffer_write_bytes(95, i * 4096, c)
+    assert be.capture_buffer(95, 0, 5 * 4096) == np.concatenate(chunks).tobytes()
+    be.set_upload_behavior(abi.DOE_UPLOAD_COPY_DST_COPY_SRC, 0xFFFFFFFF)
+    with pytest.raises(abi.DoeError) as e:
+        be.set_upload_behavior(7, 1)
+    assert e.value.rc == abi.DOE_INVALID_ARGUMENT

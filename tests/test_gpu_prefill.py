@@ -94,8 +94,24 @@ def test_prefill_writes_paged_cache_bit_exact(cache_start):
     within(out.cpu().numpy()[rows], _oracle_rows(q, k, v, rows, True, 1 / np.sqrt(128)), TOL)
 
 
-def test_config2_full_size_parity_and_cache():
+@pytest.fixture(scope="module")
+def config2_reference():
+    """Config 2 at full size and the oracle's causal head256 online softmax
+    over every query row of every head (query_len = S, start_pos 0)."""
     w = workloads.prefill_f16()
+    S, H, D = w.q.shape
+    u = dict(num_heads=H, num_kv_heads=w.k.shape[1], head_dim=D, seq_len=S, query_len=S,
+             scale=w.scale, is_causal=1, start_pos=0, attn_softcap=0.0, sliding_window=0,
+             kv_len_source=0, kv_start=0, page_size=16, kv_layout=0)
+    ref = oracle.attention_online_f16kv(u, w.q.astype(np.float32), w.k.view(np.uint16),
+                                        w.v.view(np.uint16))
+    return w, ref
+
+
+def test_config2_full_size_parity_and_cache(config2_reference):
+    """Every one of the 2048 x 32 output rows within 2e-3 of the oracle, and
+    the fused cache write equal to the prompt's K and V bit for bit."""
+    w, ref = config2_reference
     S, H, _ = w.q.shape
     table = np.arange(S // 16, dtype=np.int32)[None, ::-1].copy()  # reversed pages
     cache = PagedKVCache(num_pages=S // 16, page_size=16, num_kv_heads=w.k.shape[1], head_dim=128,
@@ -105,8 +121,36 @@ def test_config2_full_size_parity_and_cache():
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     o = out.cpu().numpy()
-    assert np.isfinite(o).all()
+    within(o, ref, TOL)
+    # spot rows against the per-row form of the oracle (query_len 1 at start_pos r)
     rows = np.array([0, 1, 127, 128, 129, 1000, 1023, 1024, 2046, 2047])
     within(o[rows], _oracle_rows(w.q, w.k, w.v, rows, True, w.scale), TOL)
     kp = cache.k_pool.cpu().numpy().view(np.uint16)
+    vp = cache.v_pool.cpu().numpy().view(np.uint16)
     assert np.array_equal(oracle.paged_gather(kp, table[0], S, page_size=16), w.k.view(np.uint16))
+    assert np.array_equal(oracle.paged_gather(vp, table[0], S, page_size=16), w.v.view(np.uint16))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_config2_kv_head_shards_match_oracle(world, config2_reference):
+    """Config 2 sharded by KV head over `world` GPUs (each rank: Hkv / world
+    KV heads and their query heads, the slicing bench.py runs under torchrun),
+    run rank after rank on this GPU: every rank's output equals the oracle's
+    heads of that rank, and its cache holds its heads' K/V bit for bit."""
+    w, ref = config2_reference
+    S, H, _ = w.q.shape
+    Hkv = w.k.shape[1]
+    kvh, qh = Hkv // world, H // world
+    for rank in range(world):
+        q = w.q[:, rank * qh:(rank + 1) * qh]
+        k = w.k[:, rank * kvh:(rank + 1) * kvh]
+        v = w.v[:, rank * kvh:(rank + 1) * kvh]
+        cache = PagedKVCache(num_pages=S // 16, page_size=16, num_kv_heads=kvh, head_dim=128,
+                             block_table=np.arange(S // 16, dtype=np.int32)[None])
+        status = ops.status_word()
+        out = ops.attention_prefill_f16(_t(q), _t(k), _t(v), w.scale, cache=cache, status=status)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        within(out.cpu().numpy(), ref[:, rank * qh:(rank + 1) * qh], TOL)
+        assert np.array_equal(cache.k_pool.cpu().numpy().view(np.uint16), k.view(np.uint16))
+        assert np.array_equal(cache.v_pool.cpu().numpy().view(np.uint16), v.view(np.uint16))

@@ -68,3 +68,22 @@ def test_config5_decoder_bytes():
     per_token = cfg.batch * cfg.kv_heads * cfg.head_dim * 2 * 2 * cfg.layers
     assert cfg.kv_read_bytes() - per_token == 2_147_483_648
     assert cfg.weight_bytes() + cfg.kv_read_bytes() == 3_892_903_936
+
+
+def test_config4_strong_split_covers_every_sequence_once():
+    """bench.py's config-4 split at N = 2, 4, 8: every one of the 32 sequences
+    on exactly one rank, each shard's pages renumbered densely, token loads
+    within one sequence of each other (LPT)."""
+    import bench
+
+    w = workloads.paged_int8()
+    for world in (2, 4, 8):
+        shards = [bench.strong_split(w, world, r)[0] for r in range(world)]
+        idx = np.concatenate([s.meta["global_index"] for s in shards])
+        assert sorted(idx.tolist()) == list(range(w.num_seqs))
+        for s in shards:
+            used = s.block_table[s.block_table >= 0]
+            assert np.array_equal(np.sort(used), np.arange(s.num_pages))
+            assert np.array_equal(s.ctx, w.ctx[s.meta["global_index"]])
+        loads = [int(s.seq_lens.sum()) for s in shards]
+        assert max(loads) - min(loads) <= int(w.seq_lens.max())
