@@ -1,4 +1,4 @@
-"""Build libdoe_cuda.so in-tree for sm_100a.
+"""Build libdoe_cuda.so and the ONNX Runtime plugin EP in-tree for sm_100a.
 
     python -m doe_b200.build [--verbose-ptxas]
 
@@ -6,6 +6,15 @@ Every translation unit under doe_b200/csrc is compiled by nvcc for
 `-gencode arch=compute_100a,code=sm_100a` and linked (with the CUDA runtime
 linked statically) into doe_b200/libdoe_cuda.so, which ships beside the
 package.  Object files go to doe_b200/_build/.
+
+doe_b200/ort_ep/doe_ort_ep.cpp is compiled by g++ into
+doe_b200/libdoe_ort_ep.so (CreateEpFactories / ReleaseEpFactory), linked
+against libdoe_cuda.so.  It needs ONNX Runtime's C API headers
+(onnxruntime_c_api.h and onnxruntime_ep_c_api.h, API version 23 or later):
+the directory named by ORT_INCLUDE_DIR, else the copy the doerun/doe tree
+vendors under runtime/bridge/onnxruntime-ep/vendor/onnxruntime/include when
+that tree is at DOE_REFERENCE_ROOT (default /root/reference).  Without the
+headers the EP library is skipped, or kept if it was built before.
 """
 from __future__ import annotations
 
@@ -82,6 +91,43 @@ def build(force: bool = False, verbose_ptxas: bool = False) -> Path:
     return LIB
 
 
+EP_SRC = PKG / "ort_ep" / "doe_ort_ep.cpp"
+EP_LIB = PKG / "libdoe_ort_ep.so"
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+
+
+def ort_include_dir() -> Path | None:
+    """ONNX Runtime's C API header directory (see the module docstring)."""
+    cands = []
+    if os.environ.get("ORT_INCLUDE_DIR"):
+        cands.append(Path(os.environ["ORT_INCLUDE_DIR"]))
+    ref = Path(os.environ.get("DOE_REFERENCE_ROOT", "/root/reference"))
+    cands.append(ref / "runtime" / "bridge" / "onnxruntime-ep" / "vendor" / "onnxruntime" / "include")
+    for c in cands:
+        if (c / "onnxruntime_c_api.h").exists() and (c / "onnxruntime_ep_c_api.h").exists():
+            return c
+    return None
+
+
+def build_ort_ep(force: bool = False) -> Path | None:
+    """Compile libdoe_ort_ep.so (needs libdoe_cuda.so and the ORT headers)."""
+    inc = ort_include_dir()
+    if inc is None:
+        return EP_LIB if EP_LIB.exists() else None
+    if (not force and EP_LIB.exists() and EP_LIB.stat().st_mtime >= max(
+            EP_SRC.stat().st_mtime, LIB.stat().st_mtime, (INCLUDE / "doe_cuda.h").stat().st_mtime)):
+        return EP_LIB
+    cxx = os.environ.get("CXX", "g++")
+    cmd = [cxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-fvisibility=hidden",
+           "-I", str(inc), "-I", str(INCLUDE), "-I", str(CUDA_HOME / "include"), str(EP_SRC),
+           "-o", str(EP_LIB), "-L", str(PKG), "-ldoe_cuda", "-L", str(CUDA_HOME / "lib64"), "-lcudart_static",
+           "-ldl", "-lpthread", "-lrt", "-Wl,-rpath,$ORIGIN"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"g++ failed on {EP_SRC.name}:\n{res.stdout}\n{res.stderr}")
+    return EP_LIB
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
@@ -89,6 +135,7 @@ def main() -> None:
     args = ap.parse_args()
     lib = build(force=args.force, verbose_ptxas=args.verbose_ptxas)
     print(lib)
+    print(build_ort_ep(force=args.force) or "libdoe_ort_ep.so skipped: no ONNX Runtime headers")
     if args.verbose_ptxas:
         print((BUILD / "ptxas.log").read_text())
 
