@@ -143,6 +143,7 @@ SIGNATURES = {
     "doe_cuda_prewarm_upload": (_I, [_P, _U64]),
     "doe_cuda_set_queue_sync_mode": (_I, [_P, _I]),
     "doe_cuda_set_upload_behavior": (_I, [_P, _I, C.c_uint32]),
+    "doe_cuda_set_queue_wait_mode": (_I, [_P, _I]),
     "doe_cuda_set_gpu_timestamp_mode": (_I, [_P, _I]),
     "doe_cuda_flush": (_I, [_P, C.POINTER(_U64)]),
     "doe_attention_decode_f32_workspace_bytes": (_U64, [_U32, _U32, _U32]),
@@ -171,6 +172,11 @@ SIGNATURES = {
     "doe_ep_layernorm_f32": (_I, [_P, _P, _F, _P, _U64, _U32, _LP]),
     "doe_ep_concat_f32": (_I, [_P, _P, _P, _U64, _U64, _U64, _U64, _LP]),
     "doe_ep_matmul_f32": (_I, [_P, _P, _P, _P, _U32, _U32, _U32, _U32, _LP]),
+    "doe_rmsnorm_f32": (_I, [_P, _P, _P, _U32, _U32, C.c_float, _U32, _LP]),
+    "doe_gemv_f32": (_I, [_P, _P, _P, _U32, _U32, _LP]),
+    "doe_gelu_tanh_f32": (_I, [_P, _P, C.c_uint64, _LP]),
+    "doe_argmax_f32": (_I, [_P, _U32, _P, _LP]),
+    "doe_gather_rows_f32": (_I, [_P, _P, C.c_uint64, _P, _U32, _U32, _LP]),
     "doe_ep_gemm_relu_gemm_workspace_bytes": (_U64, [_U32, _U32]),
     "doe_ep_gemm_relu_gemm_f32": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _LP]),
     "doe_linear_workspace_bytes": (_U64, [_U32, _U32]),

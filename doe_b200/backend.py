@@ -132,6 +132,10 @@ class CudaBackend:
         self._check("doe_cuda_set_upload_behavior",
                     self._lib.doe_cuda_set_upload_behavior(self._h, int(mode), int(submit_every)))
 
+    def set_queue_wait_mode(self, mode: int) -> None:
+        """QueueWaitMode: 0 process_events, 1 wait_any (flush waits either way)."""
+        self._check("doe_cuda_set_queue_wait_mode", self._lib.doe_cuda_set_queue_wait_mode(self._h, int(mode)))
+
     def set_queue_sync_mode(self, per_command: bool) -> None:
         self._check("doe_cuda_set_queue_sync_mode",
                     self._lib.doe_cuda_set_queue_sync_mode(self._h, int(per_command)))

@@ -67,6 +67,7 @@ struct doe_cuda_ctx {
   // set_upload_behavior: the queue is flushed after every `submit_every`
   // buffer writes (UINT32_MAX: never, the reference's lazy default)
   int upload_mode = 0;
+  int queue_wait_mode = 0;  // set_queue_wait_mode: 0 process_events, 1 wait_any
   uint32_t upload_submit_every = UINT32_MAX;
   uint32_t pending_uploads = 0;
   cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
@@ -232,6 +233,8 @@ struct DispatchCtx {
   const doe_binding* b;
   uint32_t n;
   const char* kernel;
+  const char* entry_point;  // null or "" = "main"
+  uint32_t x, y, z;         // workgroup counts of the command
 };
 
 const doe_binding* find_binding(const DispatchCtx& d, uint32_t binding) {
@@ -620,6 +623,124 @@ int run_stitch(const DispatchCtx& d) {
                                                    (float*)o.ptr, &l));
 }
 
+// ---- the other kernels of the Gemma command streams -------------------------
+// Element counts follow the dispatch: a 256-thread workgroup kernel with no
+// bounds check of its own (gelu.wgsl, residual.wgsl) covers x * 256
+// elements, clamped to its bindings' sizes.
+uint64_t min3(uint64_t a, uint64_t b, uint64_t c) { return a < b ? (a < c ? a : c) : (b < c ? b : c); }
+
+bool entry_is(const DispatchCtx& d, const char* name) {
+  return d.entry_point != nullptr && std::strcmp(d.entry_point, name) == 0;
+}
+
+// rmsnorm.wgsl: {size, eps}; input, weight, output; one row per workgroup.
+int run_rmsnorm(const DispatchCtx& d) {
+  uint32_t u[2];
+  DOE_TRY(read_uniform(d, 0, u, sizeof(u)));
+  float eps;
+  std::memcpy(&eps, &u[1], 4);
+  const bool offset = entry_is(d, "main_weight_offset");
+  if (d.entry_point && d.entry_point[0] && !offset && !entry_is(d, "main"))
+    return fail(d.ctx, DOE_UNSUPPORTED, "%s: entry point '%s' is not implemented", d.kernel, d.entry_point);
+  Bound in, w, out;
+  DOE_TRY(resolve(d, 1, true, &in));
+  DOE_TRY(resolve(d, 2, true, &w));
+  DOE_TRY(resolve(d, 3, true, &out));
+  const uint64_t rows = d.x, size = u[0];
+  DOE_TRY(need(d, in, rows * size * 4, "input"));
+  DOE_TRY(need(d, w, size * 4, "weight"));
+  DOE_TRY(need(d, out, rows * size * 4, "output"));
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_rmsnorm_f32((const float*)in.ptr, (const float*)w.ptr, (float*)out.ptr, d.x, u[0],
+                                          eps, offset ? 1u : 0u, &l));
+}
+
+// matmul-gemv.wgsl: {rows, cols}; matrix, vector, output; row r < x.
+int run_gemv(const DispatchCtx& d) {
+  uint32_t u[2];
+  DOE_TRY(read_uniform(d, 0, u, sizeof(u)));
+  Bound m, v, out;
+  DOE_TRY(resolve(d, 1, true, &m));
+  DOE_TRY(resolve(d, 2, true, &v));
+  DOE_TRY(resolve(d, 3, true, &out));
+  const uint64_t rows = u[0] < d.x ? u[0] : d.x, cols = u[1];
+  DOE_TRY(need(d, m, rows * cols * 4, "matrix"));
+  DOE_TRY(need(d, v, cols * 4, "vector"));
+  DOE_TRY(need(d, out, rows * 4, "output"));
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_gemv_f32((const float*)m.ptr, (const float*)v.ptr, (float*)out.ptr, (uint32_t)rows,
+                                       u[1], &l));
+}
+
+// matmul-tiled.wgsl: a, b, c, {M, K, N} at binding 3; C = A B row-major.
+int run_matmul_tiled(const DispatchCtx& d) {
+  uint32_t u[3];
+  DOE_TRY(read_uniform(d, 3, u, sizeof(u)));
+  Bound a, b, c;
+  DOE_TRY(resolve(d, 0, true, &a));
+  DOE_TRY(resolve(d, 1, true, &b));
+  DOE_TRY(resolve(d, 2, true, &c));
+  const uint64_t M = u[0], K = u[1], N = u[2];
+  DOE_TRY(need(d, a, M * K * 4, "a"));
+  DOE_TRY(need(d, b, K * N * 4, "b"));
+  DOE_TRY(need(d, c, M * N * 4, "c"));
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_ep_matmul_f32((const float*)a.ptr, (const float*)b.ptr, nullptr, (float*)c.ptr, u[0],
+                                            u[1], u[2], 0, &l));
+}
+
+// gelu.wgsl: input, output.
+int run_gelu(const DispatchCtx& d) {
+  Bound in, out;
+  DOE_TRY(resolve(d, 0, true, &in));
+  DOE_TRY(resolve(d, 1, true, &out));
+  const uint64_t n = min3((uint64_t)d.x * 256, in.size / 4, out.size / 4);
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_gelu_tanh_f32((const float*)in.ptr, (float*)out.ptr, n, &l));
+}
+
+// residual.wgsl: a, b, out.
+int run_residual(const DispatchCtx& d) {
+  Bound a, b, out;
+  DOE_TRY(resolve(d, 0, true, &a));
+  DOE_TRY(resolve(d, 1, true, &b));
+  DOE_TRY(resolve(d, 2, true, &out));
+  const uint64_t n = min3((uint64_t)d.x * 256, a.size / 4, min3(b.size / 4, out.size / 4, UINT64_MAX));
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_ep_binary_f32(DOE_EP_ADD, (const float*)a.ptr, (const float*)b.ptr, (float*)out.ptr,
+                                            n, &l));
+}
+
+// sample.wgsl: {vocab_size}; logits, output_token.
+int run_sample(const DispatchCtx& d) {
+  uint32_t u[1];
+  DOE_TRY(read_uniform(d, 0, u, sizeof(u)));
+  Bound lg, tok;
+  DOE_TRY(resolve(d, 1, true, &lg));
+  DOE_TRY(resolve(d, 2, true, &tok));
+  DOE_TRY(need(d, lg, (uint64_t)u[0] * 4, "logits"));
+  DOE_TRY(need(d, tok, 4, "output_token"));
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_argmax_f32((const float*)lg.ptr, u[0], (uint32_t*)tok.ptr, &l));
+}
+
+// gather.wgsl: {seq_len, embed_dim}; token_ids, embed_table, output.
+int run_gather(const DispatchCtx& d) {
+  uint32_t u[2];
+  DOE_TRY(read_uniform(d, 0, u, sizeof(u)));
+  Bound ids, table, out;
+  DOE_TRY(resolve(d, 1, true, &ids));
+  DOE_TRY(resolve(d, 2, true, &table));
+  DOE_TRY(resolve(d, 3, true, &out));
+  const uint64_t S = u[0], D = u[1];
+  DOE_TRY(need(d, ids, S * 4, "token_ids"));
+  DOE_TRY(need(d, out, S * D * 4, "output"));
+  if (D == 0) return DOE_OK;
+  doe_launch l = make_launch(d.ctx);
+  return op_result(d.ctx, doe_gather_rows_f32((const uint32_t*)ids.ptr, (const float*)table.ptr, table.size / 4 / D,
+                                              (float*)out.ptr, u[0], u[1], &l));
+}
+
 enum class Op {
   kNone,
   kDecodeWgsl,
@@ -633,7 +754,14 @@ enum class Op {
   kRope,
   kPagedDecode,
   kPagedAppend,
-  kStitch
+  kStitch,
+  kRmsNorm,
+  kGemv,
+  kMatmulTiled,
+  kGelu,
+  kResidual,
+  kSample,
+  kGather
 };
 
 Op lookup(const char* k) {
@@ -644,7 +772,8 @@ Op lookup(const char* k) {
   };
   // WGSL kernel names of Doe's command streams and the exec-v1 op names of
   // runtime/zig/src/doe_wgsl/emit_csl_exec_v1.zig:113-180 that belong to the
-  // attention / KV path; the last three are this backend's batched forms.
+  // attention / KV path; attention_paged_decode, kv_append_paged and
+  // attention_stitch are this backend's batched forms.
   static const Entry table[] = {
       {"attention-decode.wgsl", Op::kDecodeWgsl},
       {"complex_attention_decode.wgsl", Op::kDecodeWgsl},
@@ -663,6 +792,14 @@ Op lookup(const char* k) {
       {"attention_paged_decode", Op::kPagedDecode},
       {"kv_append_paged", Op::kPagedAppend},
       {"attention_stitch", Op::kStitch},
+      // the other kernels of the Gemma command streams
+      {"rmsnorm.wgsl", Op::kRmsNorm},
+      {"matmul-gemv.wgsl", Op::kGemv},
+      {"matmul-tiled.wgsl", Op::kMatmulTiled},
+      {"gelu.wgsl", Op::kGelu},
+      {"residual.wgsl", Op::kResidual},
+      {"sample.wgsl", Op::kSample},
+      {"gather.wgsl", Op::kGather},
   };
   for (const Entry& e : table)
     if (std::strcmp(e.name, k) == 0) return e.op;
@@ -786,6 +923,14 @@ int doe_cuda_buffer_write_async(doe_cuda_ctx* ctx, uint64_t handle, uint64_t off
   DOE_TRY(cu(ctx, cudaEventRecord(b->ev_written, ctx->copy), "cudaEventRecord"));
   b->write_pending = true;
   return upload_submitted(ctx);
+}
+
+int doe_cuda_set_queue_wait_mode(doe_cuda_ctx* ctx, int mode) {
+  if (!ctx) return DOE_INVALID_ARGUMENT;
+  if (mode != DOE_QUEUE_WAIT_PROCESS_EVENTS && mode != DOE_QUEUE_WAIT_ANY)
+    return fail(ctx, DOE_INVALID_ARGUMENT, "set_queue_wait_mode: unknown mode %d", mode);
+  ctx->queue_wait_mode = mode;
+  return DOE_OK;
 }
 
 int doe_cuda_set_upload_behavior(doe_cuda_ctx* ctx, int mode, uint32_t submit_every) {
@@ -928,16 +1073,17 @@ int doe_cuda_set_gpu_timestamp_mode(doe_cuda_ctx* ctx, int on) {
 int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel, const char* entry_point, uint32_t x,
                       uint32_t y, uint32_t z, const doe_binding* bindings, uint32_t num_bindings,
                       doe_exec_result* result) {
-  (void)x;
-  (void)y;
-  (void)z;  // grid sizes come from the uniforms; the kernels size their own grids
+  // The attention / KV kernels size their grids from the uniforms; x, the
+  // workgroup count, sets the rows of rmsnorm.wgsl and matmul-gemv.wgsl and
+  // the element count of gelu.wgsl and residual.wgsl, as in the WGSL.
   if (!ctx || (!bindings && num_bindings)) return DOE_INVALID_ARGUMENT;
   doe_exec_result res;
   std::memset(&res, 0, sizeof(res));
   const uint64_t t0 = now_ns();
   const Op op = lookup(kernel);
-  if (entry_point && entry_point[0] && std::strcmp(entry_point, "main") != 0 && op != Op::kNone &&
-      std::strstr(kernel, ".wgsl") != nullptr) {
+  const bool other_entry = entry_point && entry_point[0] && std::strcmp(entry_point, "main") != 0;
+  if (other_entry && op != Op::kNone && std::strstr(kernel, ".wgsl") != nullptr &&
+      !(op == Op::kRmsNorm && std::strcmp(entry_point, "main_weight_offset") == 0)) {
     res.status = DOE_UNSUPPORTED;
     if (result) *result = res;
     return fail(ctx, DOE_UNSUPPORTED, "dispatch: entry point '%s' of %s is not implemented",
@@ -950,7 +1096,7 @@ int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel, const char* entry_p
                 kernel ? kernel : "(null)");
   }
   int rc = bind_device(ctx);
-  DispatchCtx d{ctx, bindings, num_bindings, kernel};
+  DispatchCtx d{ctx, bindings, num_bindings, kernel, entry_point, x, y, z};
   // the kernel runs after the writes and captures queued for its buffers
   for (uint32_t i = 0; i < num_bindings && rc == DOE_OK && bindings; ++i) {
     auto bit = ctx->buffers.find(bindings[i].handle);
@@ -981,6 +1127,13 @@ int doe_cuda_dispatch(doe_cuda_ctx* ctx, const char* kernel, const char* entry_p
       case Op::kPagedDecode: rc = run_paged_decode(d); break;
       case Op::kPagedAppend: rc = run_paged_append(d); break;
       case Op::kStitch: rc = run_stitch(d); break;
+      case Op::kRmsNorm: rc = run_rmsnorm(d); break;
+      case Op::kGemv: rc = run_gemv(d); break;
+      case Op::kMatmulTiled: rc = run_matmul_tiled(d); break;
+      case Op::kGelu: rc = run_gelu(d); break;
+      case Op::kResidual: rc = run_residual(d); break;
+      case Op::kSample: rc = run_sample(d); break;
+      case Op::kGather: rc = run_gather(d); break;
       default: rc = DOE_UNSUPPORTED; break;
     }
   }

@@ -146,7 +146,11 @@ int doe_cuda_buffer_device_ptr(doe_cuda_ctx* ctx, uint64_t handle, void** out);
  * "attention_head512_f16kv.wgsl", "rope.wgsl") or an exec-v1 op name
  * (runtime/zig/src/doe_wgsl/emit_csl_exec_v1.zig:113-180: "attention",
  * "attention_sliding", "attention_prefill", "attention_prefill_kv_axis_sharded",
- * "kv_write", "kv_write_shared", "kv_read", "rope").  Unknown names return
+ * "kv_write", "kv_write_shared", "kv_read", "rope") -- and the other kernels
+ * of the Gemma command streams: "rmsnorm.wgsl" (entry points "main" and
+ * "main_weight_offset"), "matmul-gemv.wgsl", "matmul-tiled.wgsl",
+ * "gelu.wgsl", "residual.wgsl", "sample.wgsl", "gather.wgsl", with the
+ * bindings and uniforms of bench/inference-pipeline/kernels/<name>.  Unknown names return
  * DOE_UNSUPPORTED with a message; nothing runs on the host instead.
  * The two prefill op names take the tcgen05 prefill (doe_attention_prefill_f16,
  * Q rounded to f16 first) when the 15-word uniform describes a whole prompt:
@@ -178,6 +182,15 @@ int doe_cuda_prewarm_upload(doe_cuda_ctx* ctx, uint64_t max_upload_bytes);
 #define DOE_UPLOAD_COPY_DST_COPY_SRC 0
 #define DOE_UPLOAD_COPY_DST 1
 int doe_cuda_set_upload_behavior(doe_cuda_ctx* ctx, int mode, uint32_t submit_every);
+/* set_queue_wait_mode (backend_iface.zig:18; QueueWaitMode,
+ * runtime/zig/src/backend/runtime_types.zig:11-14): how flush_queue waits.
+ * As in the Vulkan backend (vulkan/native_runtime.zig:360-369) both modes
+ * wait for every queued copy and kernel; the mode is validated and kept.
+ * Host copies that do not wait are the separate deferred calls
+ * doe_cuda_buffer_write_async / doe_cuda_buffer_read_async.              */
+#define DOE_QUEUE_WAIT_PROCESS_EVENTS 0
+#define DOE_QUEUE_WAIT_ANY 1
+int doe_cuda_set_queue_wait_mode(doe_cuda_ctx* ctx, int mode);
 /* set_queue_sync_mode (backend_iface.zig:19): 0 deferred, 1 per command.   */
 int doe_cuda_set_queue_sync_mode(doe_cuda_ctx* ctx, int per_command);
 /* set_gpu_timestamp_mode (backend_iface.zig:20): 0 off, 1 on.              */
@@ -579,6 +592,40 @@ int doe_ep_gemm_relu_gemm_f32(const float* x, const float* w1, const float* b1,
                               const float* w2, const float* b2, float* y,
                               uint32_t batch, uint32_t in_dim, uint32_t hidden,
                               uint32_t out_dim, const doe_launch* launch);
+
+/* ======================================================================== */
+/* The other kernels of Doe's Gemma inference command streams              */
+/* (examples/inference_gemma3_*_commands.json), so every kernel_dispatch of */
+/* a stream runs on this backend.  Each restates one WGSL kernel of         */
+/* bench/inference-pipeline/kernels/ in f32; reductions may sum in another  */
+/* order (agreement within 1e-5 * max(|ref|, 1)).  residual.wgsl is         */
+/* doe_ep_binary_f32(DOE_EP_ADD) and matmul-tiled.wgsl is                    */
+/* doe_ep_matmul_f32 (C = A B, row-major).                                   */
+/* ======================================================================== */
+
+/* rmsnorm.wgsl main (:14-52) / main_weight_offset (:54-90): for each of
+ * `rows` rows of `size` floats, out = x * (1 / sqrt(sum(x^2) / size + eps))
+ * * g with g = weight[i] (weight_offset 0) or 1 + weight[i] (1).          */
+int doe_rmsnorm_f32(const float* x, const float* weight, float* out, uint32_t rows,
+                    uint32_t size, float eps, uint32_t weight_offset,
+                    const doe_launch* launch);
+/* matmul-gemv.wgsl (:1-74): out[r] = sum_c matrix[r * cols + c] * vector[c]
+ * for r < rows.                                                            */
+int doe_gemv_f32(const float* matrix, const float* vector, float* out, uint32_t rows,
+                 uint32_t cols, const doe_launch* launch);
+/* gelu.wgsl (:1-12): y = 0.5 x (1 + tanh(clamp(0.7978845608 (x + 0.044715
+ * x^3), -15, 15))).                                                        */
+int doe_gelu_tanh_f32(const float* x, float* y, uint64_t n, const doe_launch* launch);
+/* sample.wgsl main (:1-52): token[0] = argmax of logits[0, n).  A logit
+ * counts only if it is greater than -1e30; among equal maxima the one with
+ * the smallest index mod 256, then the smallest index, wins (the kernel's
+ * 256-thread strided scan and left-leaning tree); with none, 0.             */
+int doe_argmax_f32(const float* logits, uint32_t n, uint32_t* token, const doe_launch* launch);
+/* gather.wgsl (:1-24): out[s, d] = table[ids[s] * dim + d] for s < seq_len,
+ * d < dim; an id >= table_rows sets DOE_DEVICE_ERR_PAGE and writes zeros.   */
+int doe_gather_rows_f32(const uint32_t* ids, const float* table, uint64_t table_rows,
+                        float* out, uint32_t seq_len, uint32_t dim,
+                        const doe_launch* launch);
 
 /* ======================================================================== */
 /* Host KV page pool -- hands out physical pages and keeps the per-sequence  */

@@ -11,7 +11,10 @@ canary test constants (``bench/tests/test_attention_canary_identity.py``),
 and reads the attention-slice determinism fixtures
 (``bench/fixtures/determinism/*attention-slice*``), and reads the ORT plugin
 EP's session smoke cases as text
-(``runtime/bridge/onnxruntime-ep/src/doe_ort_ep_session_smoke.cc``).  The outputs are small
+(``runtime/bridge/onnxruntime-ep/src/doe_ort_ep_session_smoke.cc``), copies
+three of Doe's Gemma command streams (``examples/inference_gemma3_*``) and
+hashes synthetic assets made by its generator
+(``bench/lib/synthetic_assets.py``).  The outputs are small
 .npz / .json files; nothing at test time reads the reference tree.
 """
 from __future__ import annotations
@@ -172,14 +175,58 @@ def make_ort_ep_cases(root: Path) -> None:
     (HERE / "ort_ep_smoke_cases.json").write_text(json.dumps(out, indent=1) + "\n")
 
 
+GEMMA_STREAMS = ("inference_gemma3_270m_decode_1tok_commands", "inference_gemma3_1b_decode_1tok_commands",
+                 "inference_gemma3_270m_prefill_32tok_commands")
+
+
+def make_command_streams(root: Path) -> None:
+    """Doe's Gemma command streams (examples/<name>.json, the reference's own
+    replay inputs), re-serialised compactly, and the sha256 of the synthetic
+    asset of every buffer_load of the 270m decode stream plus a few small
+    cases, computed by the reference's generator
+    (bench/lib/synthetic_assets.py:generate_asset_bytes)."""
+    sys.dont_write_bytecode = True
+    sys.path.insert(0, str(root))
+    from bench.lib import synthetic_assets as sa  # noqa: E402
+
+    streams = {}
+    for name in GEMMA_STREAMS:
+        streams[name] = json.loads((root / "examples" / f"{name}.json").read_text())
+    (HERE / "gemma_command_streams.json").write_text(
+        json.dumps({"source": "examples/<name>.json of the doerun/doe tree", "streams": streams},
+                   separators=(",", ":")) + "\n")
+    cases = []
+    for gen, seed, scale, n in (("splitmix64_f32_nonzero_v1", 0, 1.0, 64), ("splitmix64_f32_nonzero_v1", 7, 0.125, 4096),
+                                ("splitmix64_f32_nonzero_v1", 2 ** 63 + 5, 3.5, 1024),
+                                ("splitmix64_f16_nonzero_v1", 11, 0.5, 2048),
+                                ("splitmix64_f32_nonzero_v1", 123, 1e-7, 256)):
+        data = sa.generate_asset_bytes(generator=gen, seed=seed, scale=scale, byte_length=n)
+        cases.append({"generator": gen, "seed": seed, "scale": scale, "byteLength": n,
+                      "sha256": hashlib.sha256(data).hexdigest(), "head_hex": data[:32].hex()})
+    stream_assets = []
+    for c in streams["inference_gemma3_270m_decode_1tok_commands"]:
+        if c["kind"] != "buffer_load":
+            continue
+        data = sa.generate_asset_bytes(generator=c["generator"], seed=c["seed"], scale=c["scale"],
+                                       byte_length=c["byteLength"])
+        stream_assets.append({"handle": c["handle"], "sha256": hashlib.sha256(data).hexdigest()})
+    (HERE / "synthetic_assets.json").write_text(json.dumps(
+        {"source": "bench/lib/synthetic_assets.py:generate_asset_bytes (splitmix64 nonzero generators)",
+         "cases": cases, "inference_gemma3_270m_decode_1tok": stream_assets}, indent=1) + "\n")
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", type=Path, required=True)
-    ap.add_argument("--only", choices=["stitch", "canary", "slice", "decode_sim", "ort_ep"], default=None,
+    ap.add_argument("--only", choices=["stitch", "canary", "slice", "decode_sim", "ort_ep", "streams"], default=None,
                     help="regenerate one fixture only")
     args = ap.parse_args()
     if args.only == "ort_ep":
         make_ort_ep_cases(args.reference)
+        print("golden fixtures written to", HERE)
+        return
+    if args.only == "streams":
+        make_command_streams(args.reference)
         print("golden fixtures written to", HERE)
         return
     stitch_mod, canary_mod = _import_reference(args.reference)
@@ -193,6 +240,7 @@ def main() -> None:
         make_decode_sim(stitch_mod)
     if args.only is None:
         make_ort_ep_cases(args.reference)
+        make_command_streams(args.reference)
     print("golden fixtures written to", HERE)
 
 

@@ -133,3 +133,22 @@ def test_kv_pool_allocation_and_block_table():
     with pytest.raises(abi.DoeError):
         pool.reserve(7, 1)
     pool.close()
+
+
+def test_zig_shim_binds_only_declared_symbols():
+    """zig/backend/cuda/mod.zig (the backend shim, not compiled here: no Zig
+    toolchain) calls only functions include/doe_cuda.h declares and the
+    library exports, and fills all eleven BackendVTable slots
+    (runtime/zig/src/backend/backend_iface.zig:13-31)."""
+    src = (ROOT / "zig" / "backend" / "cuda" / "mod.zig").read_text()
+    used = set(re.findall(r'extern "doe_cuda" fn (\w+)\(', src))
+    assert used and used <= _declared_functions(), used - _declared_functions()
+    lib = abi.lib()
+    for name in used:
+        assert hasattr(lib, name), name
+    slots = ("deinit", "execute_command", "execute_buffer_write_bytes", "set_upload_behavior",
+             "set_queue_wait_mode", "set_queue_sync_mode", "set_gpu_timestamp_mode", "flush_queue",
+             "prewarm_upload_path", "prewarm_kernel_dispatch", "capture_buffer")
+    table = src[src.index("const VTABLE = backend_iface.BackendVTable{"):]
+    for s in slots:
+        assert f".{s} = " in table, s
