@@ -588,58 +588,86 @@ def measure_e2e(w, cache, steps, warmup, world, gw=None):
 
 
 # ---------------------------------------------------------------------------
-def cpu_sample(w, target_s: float = 12.0, max_seqs: int | None = None):
-    """Time the oracle (C port of the reference CPU path, OpenMP on all cores)
-    on the first sequences of the workload; returns GB/s of that sample."""
+_CPU_POOLS: dict = {}
+
+
+def _cpu_pools(w, nseq: int):
+    """Host pools for the first `nseq` sequences of `w`, pages renumbered densely
+    (seeded N(0,1) f16 K/V, or int8 with f16 scales), cached per workload."""
     import oracle
 
-    from doe_b200 import workloads  # noqa: F401
-
+    key = (w.name, w.seed, nseq)
+    if key in _CPU_POOLS:
+        return _CPU_POOLS[key]
     rng = np.random.default_rng(w.seed + 7)
-    rows_total = w.num_pages * w.page_size
-    # pools for the sampled sequences only: remap their pages densely
-    def run(nseq):
-        sel = np.arange(nseq)
-        pages = [w.block_table[b][w.block_table[b] >= 0] for b in sel]
-        npg = sum(len(p) for p in pages)
-        table = np.full((nseq, w.block_table.shape[1]), -1, np.int32)
-        o = 0
-        for i, p in enumerate(pages):
-            table[i, :len(p)] = np.arange(o, o + len(p))
-            o += len(p)
-        shape = (npg * w.page_size, w.num_kv_heads, w.head_dim)
-        if w.kv_dtype == "f16":
-            kp = rng.standard_normal(shape, dtype=np.float32).astype(np.float16).view(np.uint16)
-            vp = rng.standard_normal(shape, dtype=np.float32).astype(np.float16).view(np.uint16)
-            ks = vs = None
-        else:
-            kp = rng.integers(-127, 128, shape, dtype=np.int8)
-            vp = rng.integers(-127, 128, shape, dtype=np.int8)
-            ks = oracle.f2h(np.full((npg, w.num_kv_heads, w.page_size), 0.01, np.float32))
-            vs = ks.copy()
-        lens = w.seq_lens[sel]
-        threads = os.cpu_count() or 1
-        t0 = time.perf_counter()
+    sel = np.arange(nseq)
+    pages = [w.block_table[b][w.block_table[b] >= 0] for b in sel]
+    npg = sum(len(p) for p in pages)
+    table = np.full((nseq, w.block_table.shape[1]), -1, np.int32)
+    o = 0
+    for i, p in enumerate(pages):
+        table[i, :len(p)] = np.arange(o, o + len(p))
+        o += len(p)
+    shape = (npg * w.page_size, w.num_kv_heads, w.head_dim)
+    if w.kv_dtype == "f16":
+        def pool():
+            out = np.empty(shape, np.uint16)
+            flat = out.reshape(shape[0], -1)
+            for r0 in range(0, shape[0], 1 << 16):
+                flat[r0:r0 + (1 << 16)] = rng.standard_normal(
+                    flat[r0:r0 + (1 << 16)].shape, dtype=np.float32).astype(np.float16).view(np.uint16)
+            return out
+        kp, vp, ks, vs = pool(), pool(), None, None
+    else:
+        kp = rng.integers(-127, 128, shape, dtype=np.int8)
+        vp = rng.integers(-127, 128, shape, dtype=np.int8)
+        ks = oracle.f2h(np.full((npg, w.num_kv_heads, w.page_size), 0.01, np.float32))
+        vs = ks.copy()
+    _CPU_POOLS[key] = (table, kp, vp, ks, vs)
+    return _CPU_POOLS[key]
+
+
+def cpu_sample(w, target_s: float = 12.0, max_seqs: int | None = None):
+    """Time the reference's CPU path (the C port of it) on the host's cores:
+    the fused append + paged decode of the workload's sequences, repeated for
+    about `target_s` seconds.  Returns GB/s of KV + Q/O bytes per pass.
+
+    The timed code is oracle/cpu_baseline.c (OpenMP over (sequence, kv head),
+    -O3 with AVX2 / F16C, the parity oracle's float order, bit-identical to
+    it) when the CPU has AVX2 and F16C, else the parity oracle itself."""
+    import oracle
+
+    nseq = w.num_seqs if max_seqs is None else min(max_seqs, w.num_seqs)
+    table, kp, vp, ks, vs = _cpu_pools(w, nseq)
+    sel = np.arange(nseq)
+    lens = w.seq_lens[sel]
+    threads = os.cpu_count() or 1
+    fast = oracle.fast_decode_available()
+    decode = oracle.cpu_paged_decode if fast else oracle.paged_decode
+
+    def one_pass():
         oracle.paged_append(w.new_k[sel][:, None].view(np.uint16), w.new_v[sel][:, None].view(np.uint16),
                             kp, vp, table, w.ctx[sel].astype(np.int32), page_size=w.page_size,
                             k_scale=ks, v_scale=vs, threads=threads)
-        oracle.paged_decode(w.q[sel].view(np.uint16), kp, vp, table, lens, w.scale,
-                            page_size=w.page_size, k_scale=ks, v_scale=vs, threads=threads)
-        dt = time.perf_counter() - t0
-        nbytes = int(lens.sum()) * w.kv_bytes_per_token() + nseq * (w.num_heads * w.head_dim * 6)
-        return dt, nbytes, threads
+        decode(w.q[sel].view(np.uint16), kp, vp, table, lens, w.scale, page_size=w.page_size, k_scale=ks,
+               v_scale=vs, threads=threads)
 
-    dt, nb, threads = run(1)
-    n = w.num_seqs if max_seqs is None else max_seqs
-    want = int(min(n, max(1, target_s / max(dt, 1e-3))))
-    if want > 1:
-        dt, nb, threads = run(want)
-    else:
-        want = 1
-    del rows_total
-    return {"value": nb / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"first {want} of {w.num_seqs} sequences of {w.name} (fused append + decode), "
-                      f"{dt:.1f} s", "tokens_per_s": want / dt, "seconds": dt}
+    t0 = time.perf_counter()
+    one_pass()
+    first = time.perf_counter() - t0
+    reps = int(max(1, min(200, target_s / max(first, 1e-3))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        one_pass()
+    dt = (time.perf_counter() - t0) / reps
+    nbytes = int(lens.sum()) * w.kv_bytes_per_token() + nseq * (w.num_heads * w.head_dim * 6)
+    build = ("oracle/cpu_baseline.c (-O3 -mavx2 -mf16c -fopenmp, -ffp-contract=off, bit-identical to the "
+             "parity oracle)" if fast else "oracle/doe_oracle.c (parity oracle, -O2 -fopenmp)")
+    return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "cpu": oracle.cpu_model(), "build": build,
+            "sample": f"all {nseq} of {w.num_seqs} sequences of {w.name} (fused append + decode), "
+                      f"{reps} passes of {dt:.3f} s",
+            "tokens_per_s": nseq / dt, "seconds": dt}
 
 
 def run_reference(args):
@@ -653,10 +681,10 @@ def run_reference(args):
     w = workloads.paged_f16()
     vals = []
     for _ in range(args.warmup):
-        cpu_sample(w, target_s=2.0, max_seqs=4)
+        cpu_sample(w, target_s=1.0)
     samples = []
     for _ in range(args.steps):
-        s = cpu_sample(w, target_s=4.0, max_seqs=8)
+        s = cpu_sample(w, target_s=3.0)
         vals.append(s["value"])
         samples.append(s)
     v = float(np.mean(vals))
@@ -668,6 +696,7 @@ def run_reference(args):
         "data": "synthetic (seeded)", "config": config_block(w),
         "tokens_per_s": float(np.mean([s["tokens_per_s"] for s in samples])),
         "cpu_baseline": {"value": v, "unit": "GB/s", "cores": samples[0]["cores"], "kind": "port",
+                         "cpu": samples[0]["cpu"], "build": samples[0]["build"],
                          "sample": samples[0]["sample"]},
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's attention runs through Vulkan/Metal (unavailable on this box) and "

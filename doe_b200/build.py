@@ -118,7 +118,7 @@ def build_ort_ep(force: bool = False) -> Path | None:
             EP_SRC.stat().st_mtime, LIB.stat().st_mtime, (INCLUDE / "doe_cuda.h").stat().st_mtime)):
         return EP_LIB
     cxx = os.environ.get("CXX", "g++")
-    cmd = [cxx, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", "-fvisibility=hidden",
+    cmd = [cxx, "-std=c++17", "-O2", "-g", "-fPIC", "-shared", "-Wall", "-Wextra", "-fvisibility=hidden",
            "-I", str(inc), "-I", str(INCLUDE), "-I", str(CUDA_HOME / "include"), str(EP_SRC),
            "-o", str(EP_LIB), "-L", str(PKG), "-ldoe_cuda", "-L", str(CUDA_HOME / "lib64"), "-lcudart_static",
            "-ldl", "-lpthread", "-lrt", "-Wl,-rpath,$ORIGIN"]

@@ -11,24 +11,27 @@
 //
 // One CTA owns two 128-row query tiles (A = 2m, B = 2m+1) of one head and
 // walks the 128-key tiles up to B's diagonal (heaviest pairs launch first).
-// The two tiles share every K/V tile:
-//   warp 17    TMA producer: Q_A, Q_B once, K and V tiles into two 2-slot
+// The two tiles share every K/V tile.  384 threads in three warpgroups:
+//   warps 0-3  softmax of tile A, warps 4-7 softmax of tile B: one thread
+//              per query row (TMEM lane), holding all 128 scores of a key
+//              tile in registers -- setmaxnreg moves registers from the third
+//              warpgroup to these two (216 per thread), so no row is split
+//              across threads and no row state is exchanged.  Each thread
+//              reads its S row from TMEM, takes the row max, writes P as f16
+//              over the S columns it has read (keys 0-63 first, published on
+//              P_HALF_x so the first half of PV starts while keys 64-127 are
+//              exponentiated, then P_FULL_x), and keeps the running max lazily
+//              (O is rescaled in TMEM only when the max rises by more than
+//              2^8); finally O / l -> f32 rows.
+//   warp 8     TMEM owner + MMA issuer (whole warp, one elected lane issues):
+//              S_A = Q_A K^T, S_B = Q_B K^T, then O_A += P_A V and O_B += P_B V,
+//              ping-ponging so the tensor core works on one tile while the
+//              other tile's softmax runs; each PV runs in two halves
+//   warp 9     TMA producer: Q_A, Q_B once, K and V tiles into two 2-slot
 //              rings (K runs a tile ahead of V: each slot is refilled as soon
 //              as its own tile is released); it also TMA-stores the diagonal
 //              K/V tiles into the paged cache
-//   warp 16    TMEM owner + MMA issuer (whole warp, one elected lane issues):
-//              S_A = Q_A K^T, S_B = Q_B K^T, then O_A += P_A V and O_B += P_B V,
-//              ping-ponging so the tensor core works on one tile while the
-//              other tile's softmax runs; each PV runs in two halves, the
-//              first as soon as the softmax has published P's first chunk
-//   warps 0-7  softmax of tile A, warps 8-15 softmax of tile B: row r (TMEM
-//              lane r) is shared by two threads, one per half of the 128 keys
-//              (warps w and w + 4 of a tile); each reads its 64 scores from TMEM
-//              once, the pair agrees on the row max through shared memory, and
-//              each writes its half of P as f16 over S columns the pair has
-//              already read; P feeds the PV MMA straight from TMEM.  The running
-//              max grows lazily (O is rescaled in TMEM only when it rises by
-//              more than 2^8); finally O / l -> f32 rows.
+//   warps 10-11 no work (their registers go to the softmax warpgroups)
 // TMEM: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512); P_x aliases
 // the first 64 columns of S_x.  A commit on S_x(j+1) covers PV_x(j), so when
 // a softmax warp sees S_x(j+1) its P buffer is free and O_x is quiescent.
@@ -36,6 +39,8 @@
 // P from TMEM.  No cluster multicast.  Every mbarrier wait is bounded (~2 s
 // of clock cycles); on timeout the kernel records DOE_DEVICE_ERR_TIMEOUT, the
 // roles stop, all issued MMAs are waited for (bounded) and TMEM is freed.
+// There is no named barrier: a role that stops early only skips mbarrier
+// arrivals, which the others' bounded waits absorb.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -46,15 +51,18 @@ namespace doe {
 namespace pf {
 
 constexpr int BM = 128, BN = 128, HD = 128;
-constexpr int kThreads = 576;  // 16 softmax warps + MMA warp + TMA warp
+constexpr int kThreads = 384;  // 8 softmax warps, MMA warp, TMA warp, 2 idle warps
+constexpr int kMmaWarp = 8, kTmaWarp = 9;
+// setmaxnreg split of the 384 x 168 launch registers: softmax warpgroups
+// 2 x 128 x 216 + the third warpgroup 128 x 56 = 62,464 <= 64,512
+constexpr int kSoftmaxRegs = 216, kOtherRegs = 56;
 constexpr uint32_t kSub = 128 * 128;      // one 128-row x 64-half swizzled sub-tile (16 KB)
 constexpr uint32_t kTile = 2 * kSub;      // 128 x 128 f16 tile (32 KB)
 constexpr uint32_t OFF_Q = 0;                        // Q_A, Q_B
 constexpr uint32_t OFF_K = OFF_Q + 2 * kTile;        // 2 stages
 constexpr uint32_t OFF_V = OFF_K + 2 * kTile;        // 2 stages
 constexpr uint32_t OFF_BAR = OFF_V + 2 * kTile;      // barriers + TMEM slot
-constexpr uint32_t OFF_XCHG = OFF_BAR + 256;         // row max / sum exchange: [parity][tile][half][128]
-constexpr uint32_t kSmemBytes = OFF_XCHG + 2 * 2 * 2 * 128 * 4 + 1024;  // + alignment slack
+constexpr uint32_t kSmemBytes = OFF_BAR + 256 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr long long kWaitCycles = 4000000000LL;      // ~2 s at 1.9 GHz
 constexpr uint32_t kSuspendNs = 20000;                // try_wait sleep hint (the 2 s bound is checked between)
@@ -183,12 +191,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_kv = nA > nB ? nA : nB;
 
   if (threadIdx.x == 0) {
-    // P_HALF_x / P_FULL_x take one arrival from each of tile x's 8 softmax warps
-    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i >= P_HALF_A && i <= P_FULL_B) ? 8u : 1u);
+    // P_HALF_x / P_FULL_x take one arrival from each of tile x's 4 softmax warps
+    for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i >= P_HALF_A && i <= P_FULL_B) ? 4u : 1u);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
-  if (warp == 16) {
+  if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(
                      smem_u32(tmem_slot)),
                  "r"(kTmemCols));
@@ -198,8 +206,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  if (warp == 17) {
+  // registers: the softmax warpgroups take what the third one gives up; each
+  // role's code sits inside the branch that sets its register count
+  if (warp >= 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kOtherRegs));
+  if (warp == kTmaWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       mbar_expect_tx(bar(Q_FULL), (hasB ? 2 : 1) * kTile);
@@ -265,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
       }
     }
-  } else if (warp == 16) {
+  } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer
     // The whole warp runs the (warp-uniform) control flow and one elected lane
     // issues each tcgen05 instruction: the descriptors stay in uniform
@@ -286,14 +297,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       commit_elect(bar(S_FULL_A + x));
     };
-    // O_x += P_x V_j with P_x (f16) in TMEM columns [128x, 128x + 64)
-    // part 0: keys [0, 32) and [64, 96), the first P chunk of each half-row
-    // (published on P_HALF_x); part 1: keys [32, 64) and [96, 128)
+    // O_x += P_x V_j with P_x (f16) in TMEM columns [128x, 128x + 64), keys
+    // 2c and 2c + 1 in column c: part 0 is keys [0, 64) (published on
+    // P_HALF_x), part 1 keys [64, 128)
     auto issue_pv = [&](int x, int j, int part) {
       const uint64_t v = dv + (((j & 1) * kTile) >> 4);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int kk = (i >> 1) * 4 + part * 2 + (i & 1);  // 16-key slice
+        const int kk = part * 4 + i;  // 16-key slice
         umma_ts_elect(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, v + ((kk * 16 * 128) >> 4), idp,
                       (j > 0 || part > 0 || i > 0) ? 1u : 0u);
       }
@@ -344,108 +355,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     // every MMA this warp issued has finished once MMA_DONE flips
     commit_elect(bar(MMA_DONE));
     wait(MMA_DONE, 0);
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kSoftmaxRegs));
     // ------------------------------------------------------------ softmax
-    const int x = warp >> 3;                 // tile A (x = 0) or B (x = 1)
-    const int half = (warp >> 2) & 1;        // keys [64 half, 64 half + 64)
+    const int x = warp >> 2;                 // tile A (x = 0) or B (x = 1)
     const int wl = warp & 3;                 // TMEM lane group
     const int nt = x == 0 ? nA : nB;
     const int row = wl * 32 + lane;
     const int q_idx = (x == 0 ? tA : tB) * BM + row;
     const uint32_t lane_base = tmem + ((uint32_t)(wl * 32) << 16);
-    const uint32_t s_col = x * 128 + half * 64, o_col = 256 + x * 128 + half * 64;
-    const uint32_t p_col = x * 128 + half * 32;  // P keys 2c, 2c+1 live in column c
-    // [parity][tile][half][row]: iteration j uses parity j & 1, so one pair
-    // barrier per iteration suffices (a warp cannot reuse a parity before its
-    // partner has passed the next iteration's barrier)
-    float* xchg = reinterpret_cast<float*>(smem + OFF_XCHG) + x * 256;
-    const int pair_bar = 1 + x * 4 + wl;     // named barrier of the warp pair (w, w + 4)
+    const uint32_t s_col = x * 128, o_col = 256 + x * 128;
     float m_used = -INFINITY, l = 0.0f;
     bool ok = true;
-    // Both warps of a pair run every iteration and every pair barrier: after a
-    // timed-out wait a warp skips its TMEM work and arrivals but keeps step,
-    // so the named barriers (which have no timeout) always match.
-    for (int j = 0; j < nt; ++j) {
+    for (int j = 0; j < nt && ok; ++j) {
       // S_x(j) is ready; its commit also covers PV_x(j-1): P buffer free, O quiescent
-      if (ok) ok = mbar_wait(bar(S_FULL_A + x), j & 1, abort_flag, a.status);
-      ok = __all_sync(0xffffffffu, ok);  // TMEM ops are warp-collective
-      uint32_t r[64];
-      if (ok) {
-        tc_fence_after();
-        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
-        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
-        tmem_ld32(lane_base + s_col, r0);
-        tmem_ld32(lane_base + s_col + 32, r1);
-        tmem_wait_ld();
-      } else {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(S_FULL_A + x), j & 1, abort_flag, a.status));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t r[128];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) r[i] = 0u;
-      }
-      const int k0 = j * BN + half * 64;
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(lane_base + s_col + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+      tmem_wait_ld();
       const bool masked = (a.causal && j == nt - 1) || j * BN + BN > a.seq_len;
-      const int key_lim = min(a.seq_len, a.causal ? q_idx + 1 : a.seq_len) - k0;  // live keys [0, key_lim)
       if (masked) {
+        const int key_lim = min(a.seq_len, a.causal ? q_idx + 1 : a.seq_len) - j * BN;  // live keys [0, key_lim)
 #pragma unroll
-        for (int i = 0; i < 64; ++i)
+        for (int i = 0; i < 128; ++i)
           if (i >= key_lim) r[i] = __float_as_uint(-INFINITY);
       }
-      // row max of the 64 scores: three-input max, four independent chains
+      // row max of the 128 scores: three-input max, four independent chains
       float mx[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) mx[i] = __uint_as_float(r[i]);
 #pragma unroll
-      for (int i = 4; i < 64; i += 2)
+      for (int i = 4; i < 128; i += 2)
         mx[(i >> 1) & 3] = fmax3(mx[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
-      float m_raw = fmax3(fmax3(mx[0], mx[1], mx[2]), mx[3], -INFINITY);
-      // the pair's agreed row max; the barrier also proves both halves have
-      // read their S columns before either overwrites S with P
-      float* xb = xchg + (j & 1) * 512;
-      xb[half * 128 + row] = m_raw;
-      asm volatile("bar.sync %0, 64;\n" ::"r"(pair_bar) : "memory");
-      m_raw = fmaxf(m_raw, xb[(half ^ 1) * 128 + row]);
+      const float m_raw = fmax3(fmax3(mx[0], mx[1], mx[2]), mx[3], -INFINITY);
       const float m_t = m_raw == -INFINITY ? -INFINITY : m_raw * a.scale_log2;
       const bool grow = m_t > m_used + 8.0f;
       const float m_new = grow ? m_t : m_used;
       const float corr = (grow && m_used != -INFINITY) ? ex2(m_used - m_new) : 1.0f;
       const float neg_m = m_new == -INFINITY ? 0.0f : -m_new;
-      if (!ok) continue;  // barriers above were kept in step; nothing else to do
-      // p = 2^(s * scale * log2e - m): one packed FFMA per two scores and one
-      // MUFU.EX2 per score.  Chunk 0 (the half-row's first 32 keys) is stored
-      // first and published on P_HALF_x once chunk 1's exponentials and sums
-      // are done, by which time its store has landed: the tensor core then
-      // runs the first half of PV_x(j) while chunk 1 is stored.
-      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(neg_m, neg_m);
-      float2 s2[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s2[i] = make_float2(0.0f, 0.0f);
-      uint32_t w[2][16];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int i = c * 32 + 2 * e;
-          const float2 xx = ffma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sc2, nm2);
-          const float p0 = ex2(xx.x);
-          const float p1 = ex2(xx.y);
-          r[i] = __float_as_uint(p0);
-          r[i + 1] = __float_as_uint(p1);
-          w[c][e] = pack_half2(p0, p1);
-        }
-        if (c == 0) tmem_st16(lane_base + p_col, w[0]);
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int i = c * 32 + 2 * e;
-          s2[e & 3] = fadd2(s2[e & 3], make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])));
-        }
-      }
-      const float2 s4 = fadd2(fadd2(s2[0], s2[1]), fadd2(s2[2], s2[3]));
-      const float sum = s4.x + s4.y;
       if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        // the running max rose by more than 2^8: rescale this half-row of O
-        // (quiescent: S_x(j)'s commit covered PV_x(j-1), and no MMA of PV_x(j)
-        // starts before this warp's P_HALF arrival below)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {  // 16 columns at a time
+        // the running max rose by more than 2^8: rescale this row of O
+        // (quiescent: S_x(j)'s commit covered PV_x(j-1), and no MMA of
+        // PV_x(j) starts before this warp's P_HALF arrival below)
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {  // 16 columns at a time
           uint32_t o[16];
           tmem_ld16(lane_base + o_col + c * 16, o);
           tmem_wait_ld();
@@ -454,32 +412,51 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(lane_base + o_col + c * 16, o);
         }
       }
-      tmem_wait_st();  // P chunk 0 (and any O rescale) has landed
+      // p = 2^(s * scale * log2e - m): one packed FFMA per two scores and one
+      // MUFU.EX2 per score.  Keys [0, 64) are stored first and published on
+      // P_HALF_x once keys [64, 128) are exponentiated, by which time their
+      // store has landed; the tensor core then runs the first half of PV_x(j)
+      // while the rest of P is stored.
+      const float2 sc2 = make_float2(a.scale_log2, a.scale_log2), nm2 = make_float2(neg_m, neg_m);
+      float2 s2[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s2[i] = make_float2(0.0f, 0.0f);
+      uint32_t w[2][32];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int i = h * 64 + 2 * e;
+          const float2 xx = ffma2(make_float2(__uint_as_float(r[i]), __uint_as_float(r[i + 1])), sc2, nm2);
+          const float p0 = ex2(xx.x);
+          const float p1 = ex2(xx.y);
+          s2[e & 3] = fadd2(s2[e & 3], make_float2(p0, p1));
+          w[h][e] = pack_half2(p0, p1);
+        }
+        if (h == 0) tmem_st32(lane_base + s_col, w[0]);
+      }
+      tmem_wait_st();  // keys [0, 64) of P (and any O rescale) have landed
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(P_HALF_A + x));
-      tmem_st16(lane_base + p_col + 16, w[1]);
-      tmem_wait_st();  // P chunk 1 has landed
+      tmem_st32(lane_base + s_col + 32, w[1]);
+      tmem_wait_st();  // keys [64, 128) of P have landed
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(P_FULL_A + x));
-      l = l * corr + sum;  // this half's share of the row sum
+      const float2 s4 = fadd2(fadd2(s2[0], s2[1]), fadd2(s2[2], s2[3]));
+      l = l * corr + (s4.x + s4.y);
       m_used = m_new;
     }
-    // ---- epilogue: O / l -> out (l = both halves' shares)
-    if (nt > 0) {
-      if (ok) ok = mbar_wait(bar(O_FULL_A + x), 0, abort_flag, a.status);
-      ok = __all_sync(0xffffffffu, ok);
-      float* xb = xchg + (nt & 1) * 512;  // the parity iteration nt would use
-      xb[half * 128 + row] = l;
-      asm volatile("bar.sync %0, 64;\n" ::"r"(pair_bar) : "memory");
-      const float l_row = l + xb[(half ^ 1) * 128 + row];
+    // ---- epilogue: O / l -> out
+    if (nt > 0 && ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(bar(O_FULL_A + x), 0, abort_flag, a.status));
       if (ok) {
         tc_fence_after();
-        const float inv = l_row > 0.0f ? 1.0f / l_row : 0.0f;
-        float* orow = a.out + ((size_t)q_idx * H + h) * HD + half * 64;
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+        float* orow = a.out + ((size_t)q_idx * H + h) * HD;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
           tmem_ld32(lane_base + o_col + c * 32, o);
           tmem_wait_ld();
@@ -498,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 16) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(kTmemCols));
   }

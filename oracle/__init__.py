@@ -223,6 +223,73 @@ def paged_decode(q_bits, k_pool, v_pool, block_table, kv_lens, scale, *, page_si
     return out
 
 
+_FAST_PATH = _HERE / "libcpu_baseline.so"
+_fast = None
+
+
+def cpu_features() -> set[str]:
+    """CPU flags of this host (Linux /proc/cpuinfo); empty when unreadable."""
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("flags"):
+                return set(line.split(":", 1)[1].split())
+    except OSError:
+        pass
+    return set()
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def fast_decode_available() -> bool:
+    return {"avx2", "f16c"} <= cpu_features()
+
+
+def _fast_lib() -> C.CDLL:
+    global _fast
+    if _fast is None:
+        if not _FAST_PATH.exists():
+            build()
+        _fast = C.CDLL(str(_FAST_PATH))
+        _fast.doe_cpu_paged_decode.restype = _I
+        _fast.doe_cpu_paged_decode.argtypes = [_U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P,
+                                               _U32, _P, _P, _F, _U32, _F, _P, _I]
+    return _fast
+
+
+def cpu_paged_decode(q_bits, k_pool, v_pool, block_table, kv_lens, scale, *, page_size: int,
+                     k_scale=None, v_scale=None, threads: int = 0, sliding_window: int = 0,
+                     softcap: float = 0.0) -> np.ndarray:
+    """paged_decode's result from the CPU-organised build (cpu_baseline.c):
+    the same float order, bit-identical, for timing on the host.  Needs AVX2
+    and F16C (fast_decode_available())."""
+    if not fast_decode_available():
+        raise RuntimeError("cpu_paged_decode needs a CPU with AVX2 and F16C")
+    q = _c(q_bits, np.uint16)
+    B, H, D = q.shape
+    int8 = k_pool.dtype == np.int8
+    kp = _c(k_pool, np.int8 if int8 else np.uint16)
+    vp = _c(v_pool, np.int8 if int8 else np.uint16)
+    Hkv = kp.shape[1]
+    bt = _c(block_table, np.int32)
+    kl = _c(kv_lens, np.int32)
+    ks = None if k_scale is None else _c(k_scale, np.uint16)
+    vs = None if v_scale is None else _c(v_scale, np.uint16)
+    out = np.zeros((B, H, D), np.float32)
+    _check("cpu_paged_decode", _fast_lib().doe_cpu_paged_decode(
+        B, H, Hkv, D, page_size, kp.shape[0] // page_size, bt.shape[1], _ptr(q), _ptr(kp), _ptr(vp),
+        _ptr(ks), _ptr(vs), 1 if int8 else 0, _ptr(bt), _ptr(kl), float(scale), int(sliding_window),
+        float(softcap), _ptr(out), threads))
+    return out
+
+
 def paged_append(new_k_bits, new_v_bits, k_pool, v_pool, block_table, positions, *,
                  page_size: int, k_scale=None, v_scale=None, threads: int = 0) -> None:
     """In-place append of new_k/new_v [B, T, Hkv, D] f16 bits into the pools."""

@@ -108,10 +108,12 @@ class FakeOrt:
                 ("fh_compile", I, [P, P, I, C.c_char_p]),
                 ("fh_compute", I, [P, I, I, C.POINTER(P), C.POINTER(I), C.POINTER(I), C.POINTER(I64), P, I, SZ,
                                    C.POINTER(I), C.POINTER(I64), P]),
-                ("fh_device_roundtrip", I, [P, P, P, SZ])):
+                ("fh_device_roundtrip", I, [P, P, P, SZ]), ("fh_install_crash_handler", None, [])):
             f = getattr(L, fn)
             f.restype = res
             f.argtypes = args
+        if os.environ.get("DOE_FAKE_ORT_BACKTRACE"):
+            L.fh_install_crash_handler()  # native frames of a crash on stderr
         self.h = L.fh_load(str(ep_path).encode(), name.encode())
         if not self.h:
             raise RuntimeError(f"loading the EP failed: {self.error()}")

@@ -15,6 +15,9 @@
 #include <cstdint>
 #include <cstring>
 #include <dlfcn.h>
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
 #include <map>
 #include <memory>
 #include <string>
@@ -446,9 +449,30 @@ struct Host {
 
 }  // namespace
 
+namespace {
+// Prints the native frames of a crash (library + offset, for addr2line) to
+// stderr, then lets the signal take its default course.
+void on_fatal_signal(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  const char msg[] = "fake_ort_host: fatal signal; native frames:\n";
+  if (write(2, msg, sizeof(msg) - 1) < 0) {
+  }
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+}  // namespace
+
 extern "C" {
 
 const char* fh_last_error() { return g_last_error.c_str(); }
+
+void fh_install_crash_handler() {
+  signal(SIGSEGV, on_fatal_signal);
+  signal(SIGBUS, on_fatal_signal);
+  signal(SIGABRT, on_fatal_signal);
+}
 
 // ---- graphs ------------------------------------------------------------------
 OrtGraph* fh_graph_new() { return new OrtGraph(); }
