@@ -9,7 +9,9 @@ package.  Object files go to doe_b200/_build/.
 
 doe_b200/ort_ep/doe_ort_ep.cpp is compiled by g++ into
 doe_b200/libdoe_ort_ep.so (CreateEpFactories / ReleaseEpFactory), linked
-against libdoe_cuda.so.  It needs ONNX Runtime's C API headers
+against libdoe_cuda.so and the shared CUDA runtime (the static one carries
+its own copy of the C++ exception runtime, which the EP's error handling must
+not pick up).  It needs ONNX Runtime's C API headers
 (onnxruntime_c_api.h and onnxruntime_ep_c_api.h, API version 23 or later):
 the directory named by ORT_INCLUDE_DIR, else the copy the doerun/doe tree
 vendors under runtime/bridge/onnxruntime-ep/vendor/onnxruntime/include when
@@ -109,6 +111,17 @@ def ort_include_dir() -> Path | None:
     return None
 
 
+def host_cxx() -> str:
+    """The C++ compiler for the host-side libraries: DOE_CXX, else the system
+    g++.  Not $CXX: a toolchain that links libstdc++ statically would give a
+    library its own copy of the C++ runtime (exception handling included)
+    inside a process that already has the shared one."""
+    for cand in (os.environ.get("DOE_CXX"), "/usr/bin/g++", shutil.which("g++")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("no C++ compiler for libdoe_ort_ep.so (set DOE_CXX)")
+
+
 def build_ort_ep(force: bool = False) -> Path | None:
     """Compile libdoe_ort_ep.so (needs libdoe_cuda.so and the ORT headers)."""
     inc = ort_include_dir()
@@ -117,11 +130,10 @@ def build_ort_ep(force: bool = False) -> Path | None:
     if (not force and EP_LIB.exists() and EP_LIB.stat().st_mtime >= max(
             EP_SRC.stat().st_mtime, LIB.stat().st_mtime, (INCLUDE / "doe_cuda.h").stat().st_mtime)):
         return EP_LIB
-    cxx = os.environ.get("CXX", "g++")
-    cmd = [cxx, "-std=c++17", "-O2", "-g", "-fPIC", "-shared", "-Wall", "-Wextra", "-fvisibility=hidden",
+    cmd = [host_cxx(), "-std=c++17", "-O2", "-g", "-fPIC", "-shared", "-Wall", "-Wextra", "-fvisibility=hidden",
            "-I", str(inc), "-I", str(INCLUDE), "-I", str(CUDA_HOME / "include"), str(EP_SRC),
-           "-o", str(EP_LIB), "-L", str(PKG), "-ldoe_cuda", "-L", str(CUDA_HOME / "lib64"), "-lcudart_static",
-           "-ldl", "-lpthread", "-lrt", "-Wl,-rpath,$ORIGIN"]
+           "-o", str(EP_LIB), "-L", str(PKG), "-ldoe_cuda", "-L", str(CUDA_HOME / "lib64"), "-lcudart",
+           f"-Wl,-rpath,$ORIGIN:{CUDA_HOME / 'lib64'}"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"g++ failed on {EP_SRC.name}:\n{res.stdout}\n{res.stderr}")

@@ -28,14 +28,14 @@ def build(force: bool = False) -> Path | None:
     import sys
 
     sys.path.insert(0, str(HERE.parents[1]))
-    from doe_b200.build import ort_include_dir
+    from doe_b200.build import host_cxx, ort_include_dir
 
     inc = ort_include_dir()
     if inc is None:
         return LIB if LIB.exists() else None
     if not force and LIB.exists() and LIB.stat().st_mtime >= SRC.stat().st_mtime:
         return LIB
-    subprocess.run([os.environ.get("CXX", "g++"), "-std=c++17", "-O1", "-fPIC", "-shared", "-Wall", "-I", str(inc),
+    subprocess.run([host_cxx(), "-std=c++17", "-O1", "-fPIC", "-shared", "-Wall", "-I", str(inc),
                     str(SRC), "-o", str(LIB), "-ldl"], check=True)
     return LIB
 
