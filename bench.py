@@ -173,11 +173,36 @@ def max_over_ranks(world, vals: list[float]) -> list[float]:
     return t.tolist()
 
 
-def time_steps(step, steps: int, warmup: int, world: int):
-    """Device time of `steps` calls: total (ms) and per-call event times (ms)."""
+L2_FLUSH_NOTE = ("flushed between steps: a 256 MB write, then a 256 MB read of a second buffer, "
+                 "so no line of the flush is still dirty in L2 when the timed call starts")
+
+
+def l2_flusher():
+    """A callable that leaves L2 holding none of the timed call's data: it
+    writes one buffer larger than L2, then reads a second one, so the flush's
+    own dirty lines are written back before the next timed call rather than
+    during it."""
+    import torch
+
+    a = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    b = torch.zeros(256 << 20, dtype=torch.uint8, device="cuda")
+    n = iter(range(1 << 62))
+
+    def flush():
+        a.fill_(next(n) & 0xff)
+        b.amax()
+    return flush
+
+
+def time_steps(step, steps: int, warmup: int, world: int, flush=None):
+    """Device time of `steps` calls: total (ms) and per-call event times (ms).
+    With `flush` (a callable that overwrites L2), it runs before every call,
+    outside the per-call events, and the total is the sum of those."""
     import torch
 
     for _ in range(warmup):
+        if flush is not None:
+            flush()
         step()
     barrier(world)
     stream = torch.cuda.current_stream()
@@ -188,13 +213,15 @@ def time_steps(step, steps: int, warmup: int, world: int):
     torch.cuda._sleep(2_000_000 * max(1, (steps + 9) // 10))
     ev0.record(stream)
     for a, b in per:
+        if flush is not None:
+            flush()
         a.record(stream)
         step()
         b.record(stream)
     ev1.record(stream)
     torch.cuda.synchronize()
-    total = ev0.elapsed_time(ev1)
     each = [a.elapsed_time(b) for a, b in per]
+    total = sum(each) if flush is not None else ev0.elapsed_time(ev1)
     barrier(world)
     return total, each
 
@@ -286,7 +313,9 @@ def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512, gw=None)
 
     def step():
         ops.paged_append(cache, nk, nv, pos, status=status)
-    total, each = time_steps(step, steps, warmup, world)
+    # the chunk's 67 MB of input and 34 MB of output fit in L2 together: flush
+    # it between calls so that every call reads and writes HBM
+    total, each = time_steps(step, steps, warmup, world, flush=l2_flusher())
     local_ms = total
     total, = max_over_ranks(world, [total])
     assert int(status.item()) == 0
@@ -298,7 +327,8 @@ def measure_chunk_append(w, cache, steps, warmup, world, pk, chunk=512, gw=None)
     job = nbytes(gw.num_seqs) * (world if gw is w else 1)
     return {"ms_per_step": total / steps, "gbs": job * steps / (total / 1e3) / 1e9,
             "bytes_per_step": nbytes(w.num_seqs), "job_bytes_per_step": job,
-            "frac": nbytes(w.num_seqs) * steps / (local_ms / 1e3) / 1e9 / pk["hbm_gbs"]}
+            "frac": nbytes(w.num_seqs) * steps / (local_ms / 1e3) / 1e9 / pk["hbm_gbs"],
+            "l2": L2_FLUSH_NOTE}
 
 
 def measure_f32(steps, warmup, world, pk):
@@ -406,10 +436,10 @@ def measure_prefill(steps, warmup, world, pk, rank=0):
     cache = PagedKVCache(num_pages=S // 16, page_size=16, num_kv_heads=kvh, head_dim=128,
                          block_table=np.arange(S // 16, dtype=np.int32)[None])
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    flush = l2_flusher()
     times = []
     for i in range(warmup + steps):
-        flush.fill_(i & 0xff)  # 48 MB of inputs + outputs would otherwise stay in L2
+        flush()  # 48 MB of inputs + outputs would otherwise stay in L2
         torch.cuda._sleep(200_000)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
@@ -427,7 +457,7 @@ def measure_prefill(steps, warmup, world, pk, rank=0):
             "scaling": "strong" if world > 1 else None,
             "frac_of_dense_peak": tflops / world / pk["bf16_tflops"], "flops": w.flops,
             "peak_tflops": pk["bf16_tflops"], "peak_note": "measured dense bf16 burst (f16 runs at the same rate)",
-            "l2": "flushed (256 MB write) between steps"}
+            "l2": L2_FLUSH_NOTE}
 
 
 def measure_decoder(steps, warmup, world, rank, pk):

@@ -31,6 +31,7 @@ struct PagedAppendArgs {
   const float* freq_cis;  // RoPE table [rope_positions, D/2, {cos, sin}] or null
   int n_tokens, num_kv_heads, head_dim, page_size, num_pages, max_pages;
   int rope_positions;
+  int page_shift;  // log2(page_size) when it is a power of two, else -1
 };
 
 // One warp per (sequence, token, kv head); lane owns head_dim/32 elements
@@ -177,6 +178,102 @@ __global__ void __launch_bounds__(128) paged_append_d128_kernel(const PagedAppen
   }
 }
 
+// head_dim 128 int8 quantise-append without RoPE: four lanes per row, each
+// with 32 consecutive elements (64 bytes in, 32 bytes out), so one warp
+// instruction works on 8 rows and the per-row work (the |x| max exchange,
+// the scale's quotient and reciprocal, the page lookup, the scale store) is
+// shared by 4 lanes instead of 16.  A warp covers 16 rows: one token of 8 kv
+// heads (K then V), or 16 / (2 HKV) tokens of fewer heads; it loads all of
+// them before it quantises any.  The page of each of the warp's tokens is
+// looked up once, by lane j for its j-th token, and passed by shuffle.
+// Same arithmetic, same bytes as paged_append_d128_kernel<true, HKV>.
+template <int HKV>
+__global__ void __launch_bounds__(128) paged_append_int8_d128_kernel(const PagedAppendArgs a) {
+  constexpr int D = 128, ROWS = 2 * HKV, TPW = 16 / ROWS;  // tokens per warp
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, l4 = lane & 3;
+  const int b = blockIdx.y;
+  const int t0 = (blockIdx.x * 4 + warp) * TPW;
+  const __half* in_k = a.new_k + ((size_t)b * a.n_tokens) * HKV * D + 32 * l4;
+  const __half* in_v = a.new_v + ((size_t)b * a.n_tokens) * HKV * D + 32 * l4;
+  uint4 x[2][4];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int fr = 8 * i + (lane >> 2), t = t0 + fr / ROWS, rr = fr % ROWS;
+    if (t < a.n_tokens) {
+      const uint4* src = reinterpret_cast<const uint4*>((rr < HKV ? in_k : in_v) +
+                                                        ((size_t)t * HKV + rr % HKV) * D);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[i][j] = __ldcs(src + j);  // read once: evict first
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x[i][j] = make_uint4(0, 0, 0, 0);
+    }
+  }
+  // lane j < TPW: the page row of token t0 + j (-1 when outside the chunk)
+  long long my_row = -1;
+  int my_in_page = 0, my_page = 0;
+  {
+    const int t = t0 + lane;
+    const int pos0 = a.positions[b];
+    if (lane < TPW && t < a.n_tokens) {
+      const unsigned pos = (unsigned)pos0 + (unsigned)t;  // < 2^32: pos0 >= 0, t < 2^31
+      const unsigned pidx = a.page_shift >= 0 ? pos >> a.page_shift : pos / (unsigned)a.page_size;
+      int page = -1;
+      if (pos0 >= 0 && pidx < (unsigned)a.max_pages) page = a.block_table[(size_t)b * a.max_pages + pidx];
+      if ((unsigned)page < (unsigned)a.num_pages) {
+        my_page = page;
+        my_in_page = (int)(pos - pidx * (unsigned)a.page_size);
+        my_row = (long long)page * a.page_size + my_in_page;
+      } else {
+        report(a.status, DOE_DEVICE_ERR_PAGE);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int fr = 8 * i + (lane >> 2), tt = fr / ROWS, rr = fr % ROWS, h = rr % HKV;
+    const long long row = __shfl_sync(0xffffffffu, my_row, tt);
+    const int page = __shfl_sync(0xffffffffu, my_page, tt);
+    const int in_page = __shfl_sync(0xffffffffu, my_in_page, tt);
+    const __half2* hx = reinterpret_cast<const __half2*>(&x[i][0]);
+    __half2 m2 = __habs2(hx[0]);
+#pragma unroll
+    for (int e = 1; e < 16; ++e) m2 = __hmax2(m2, __habs2(hx[e]));
+    float amax = fmaxf(__low2float(m2), __high2float(m2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const __half sh = __float2half_rn(div127(amax));
+    const float sf = __half2float(sh);
+    uint32_t w[8];
+    if (sf >= 0x1p-14f && sf <= 65504.0f) {  // normal scale: packed, no clamp needed
+      const float rs = __frcp_rn(sf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int q0, q1, q2, q3;
+        quantize_s8x2_normal(__half22float2(hx[2 * e]), sf, rs, q0, q1);
+        quantize_s8x2_normal(__half22float2(hx[2 * e + 1]), sf, rs, q2, q3);
+        w[e] = pack_s8x4(q0, q1, q2, q3);
+      }
+    } else if (sf != 0.0f) {
+      const float rs = __frcp_rn(sf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        w[e] = pack_s8x4(quantize_s8(__low2float(hx[2 * e]), sf, rs), quantize_s8(__high2float(hx[2 * e]), sf, rs),
+                         quantize_s8(__low2float(hx[2 * e + 1]), sf, rs),
+                         quantize_s8(__high2float(hx[2 * e + 1]), sf, rs));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w[e] = 0;
+    }
+    if (row < 0) continue;  // outside the chunk, or a bad page (reported above)
+    uint8_t* pool = rr < HKV ? a.k_pool : a.v_pool;
+    uint4* dst = reinterpret_cast<uint4*>(pool + ((size_t)row * HKV + h) * D + 32 * l4);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    if (l4 == 0) (rr < HKV ? a.k_scale : a.v_scale)[((size_t)page * HKV + h) * a.page_size + in_page] = sh;
+  }
+}
+
 int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_tokens,
                         const void* new_k, const void* new_v, const int32_t* positions,
                         const float* freq_cis, uint32_t rope_positions, const doe_launch* launch) {
@@ -211,8 +308,22 @@ int launch_paged_append(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t n_to
   a.max_pages = (int)kv->max_pages_per_seq;
   a.freq_cis = freq_cis;
   a.rope_positions = (int)rope_positions;
+  a.page_shift = -1;
+  for (int s = 0; s < 31; ++s)
+    if (kv->page_size == (1u << s)) a.page_shift = s;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
   const bool int8 = kv->kv_dtype == DOE_KV_INT8;
+  if (d128 && int8 && freq_cis == nullptr) {
+    const unsigned tok_per_cta = 4 * (8 / kv->num_kv_heads);
+    dim3 g4((n_tokens + tok_per_cta - 1) / tok_per_cta, num_seqs);
+    switch (kv->num_kv_heads) {
+      case 8: paged_append_int8_d128_kernel<8><<<g4, 128, 0, st>>>(a); break;
+      case 4: paged_append_int8_d128_kernel<4><<<g4, 128, 0, st>>>(a); break;
+      case 2: paged_append_int8_d128_kernel<2><<<g4, 128, 0, st>>>(a); break;
+      default: paged_append_int8_d128_kernel<1><<<g4, 128, 0, st>>>(a); break;
+    }
+    return cuda_status(cudaGetLastError(), "paged_append_int8_d128_kernel");
+  }
   if (d128) {
     dim3 g2((n_tokens + 3) / 4, num_seqs);
 #define DOE_PA2(H) \

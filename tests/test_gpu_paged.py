@@ -98,9 +98,11 @@ def test_paged_decode_without_append_reads_cache_only():
     assert np.array_equal(c.k_pool.cpu().numpy().view(np.uint16), kp)  # nothing written
 
 
-@pytest.mark.parametrize("kv_dtype", ["f16", "int8"])
-def test_chunk_append_bit_exact(kv_dtype):
-    w = workloads.small_paged(21, [0, 37, 100], kv_dtype=kv_dtype, extra_tokens=64)
+@pytest.mark.parametrize("kv_dtype,Hkv,page_size", [("f16", 8, 16), ("int8", 8, 16), ("int8", 4, 48),
+                                                    ("int8", 2, 32), ("int8", 1, 16), ("int8", 8, 80)])
+def test_chunk_append_bit_exact(kv_dtype, Hkv, page_size):
+    w = workloads.small_paged(21, [0, 37, 100], num_heads=4 * Hkv, num_kv_heads=Hkv, page_size=page_size,
+                              kv_dtype=kv_dtype, extra_tokens=64)
     c = _cache(w)
     kp, vp, ks, vs = _host(c)
     g = np.random.default_rng(3)
@@ -108,6 +110,9 @@ def test_chunk_append_bit_exact(kv_dtype):
     nk = g.standard_normal((w.num_seqs, T, w.num_kv_heads, w.head_dim), dtype=np.float32).astype(np.float16)
     nv = g.standard_normal((w.num_seqs, T, w.num_kv_heads, w.head_dim), dtype=np.float32).astype(np.float16)
     nk[0, 3] = 0  # an all-zero row quantises to scale 0
+    nv[1, 4, 0] *= np.float16(1e-6)  # subnormal scale: the clamped path
+    nv[2, 5, -1, 7] = np.float16(60000.0)  # a large row maximum
+    nk[1, 6, 0, :] = np.float16(2.0 ** -24)  # every element the smallest subnormal
     pos = w.ctx.astype(np.int32)
     oracle.paged_append(nk.view(np.uint16), nv.view(np.uint16), kp, vp, w.block_table, pos,
                         page_size=w.page_size, k_scale=ks, v_scale=vs)
@@ -116,6 +121,40 @@ def test_chunk_append_bit_exact(kv_dtype):
     ops.paged_append(c, t(nk), t(nv), t(pos), status=status)
     gk, gv, gks, gvs = _host(c)
     assert int(status.item()) == 0
+    assert np.array_equal(gk, kp) and np.array_equal(gv, vp)
+    if ks is not None:
+        assert np.array_equal(gks, ks) and np.array_equal(gvs, vs)
+
+
+@pytest.mark.parametrize("kv_dtype", ["f16", "int8"])
+def test_chunk_append_bad_page_reports_and_skips_those_tokens(kv_dtype):
+    """A table entry outside the pool: the tokens that land on it are not
+    written and DOE_DEVICE_ERR_PAGE is set; every other token is."""
+    w = workloads.small_paged(23, [5, 40], kv_dtype=kv_dtype, extra_tokens=48)
+    c = _cache(w)
+    kp, vp, ks, vs = _host(c)
+    bt = w.block_table.copy()
+    bad_seq, bad_idx = 1, (40 + 20) // w.page_size  # a page in the middle of seq 1's chunk
+    bt[bad_seq, bad_idx] = w.num_pages + 3
+    c.set_block_table(bt)
+    g = np.random.default_rng(5)
+    T = 40
+    nk = g.standard_normal((w.num_seqs, T, w.num_kv_heads, w.head_dim), dtype=np.float32).astype(np.float16)
+    nv = g.standard_normal((w.num_seqs, T, w.num_kv_heads, w.head_dim), dtype=np.float32).astype(np.float16)
+    pos = w.ctx.astype(np.int32)
+    keep = np.ones((w.num_seqs, T), bool)
+    for t in range(T):
+        keep[bad_seq, t] = (int(pos[bad_seq]) + t) // w.page_size != bad_idx
+    for b in range(w.num_seqs):  # the oracle appends the kept tokens one at a time
+        for t in np.nonzero(keep[b])[0]:
+            oracle.paged_append(nk[b:b + 1, t:t + 1].view(np.uint16), nv[b:b + 1, t:t + 1].view(np.uint16),
+                                kp, vp, w.block_table[b:b + 1], np.array([pos[b] + t], np.int32),
+                                page_size=w.page_size, k_scale=ks, v_scale=vs)
+    t_ = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    status = ops.status_word()
+    ops.paged_append(c, t_(nk), t_(nv), t_(pos), status=status)
+    gk, gv, gks, gvs = _host(c)
+    assert int(status.item()) & DOE_DEVICE_ERR_PAGE
     assert np.array_equal(gk, kp) and np.array_equal(gv, vp)
     if ks is not None:
         assert np.array_equal(gks, ks) and np.array_equal(gvs, vs)
