@@ -460,7 +460,41 @@ def measure_prefill(steps, warmup, world, pk, rank=0):
             "l2": L2_FLUSH_NOTE}
 
 
-def measure_decoder(steps, warmup, world, rank, pk):
+def kernel_shares(replay, world, rank, reps=5):
+    """Device time per kernel name over `reps` replays, from the CUDA activity
+    records of torch.profiler on rank 0 (the other ranks replay alongside).
+    Shares only: times taken under a tracer are not bench values."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    barrier(world)
+    if rank == 0:
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            for _ in range(reps):
+                replay()
+            torch.cuda.synchronize()
+    else:
+        for _ in range(reps):
+            replay()
+        torch.cuda.synchronize()
+    barrier(world)
+    if rank != 0:
+        return None
+    tot = {}
+    for e in prof.key_averages():
+        t = getattr(e, "device_time_total", None)
+        if t is None:
+            t = getattr(e, "cuda_time_total", 0.0)
+        if t > 0:
+            tot[e.key] = tot.get(e.key, 0.0) + t
+    allt = sum(tot.values()) or 1.0
+    top = sorted(tot.items(), key=lambda kv: -kv[1])[:8]
+    return {"per_step_us": {k[:60]: round(v / reps, 2) for k, v in top},
+            "share": {k[:60]: round(v / allt, 4) for k, v in top},
+            "how": f"torch.profiler CUDA activity on rank 0 over {reps} graph replays (shares only)"}
+
+
+def measure_decoder(steps, warmup, world, rank, pk, shares=False):
     """Config 5: the 4-layer bf16 decoder step (batch 32, ctx 4096), tensor
     parallel by KV head over the `world` ranks, captured in a CUDA graph."""
     import torch
@@ -484,6 +518,7 @@ def measure_decoder(steps, warmup, world, rank, pk):
         total = max_over_ranks(world, [total])[0]
         status = int(dec.status.item())
         finite = bool(torch.isfinite(x).all().item())
+        ks = kernel_shares(dec.replay, world, rank) if shares else None
     finally:
         dec.release()
     ms = total / steps
@@ -497,7 +532,8 @@ def measure_decoder(steps, warmup, world, rank, pk):
             "bytes_per_step": job_bytes, "gbs": job_bytes / (ms / 1e3) / 1e9,
             "per_gpu_frac": rank_bytes / (ms / 1e3) / 1e9 / pk["hbm_gbs"],
             "gpu_launches_per_step": launches, "graph": "one CUDA graph per step",
-            "status": status, "output_finite": finite}
+            "status": status, "output_finite": finite,
+            **({"kernel_shares": ks} if ks is not None else {})}
 
 
 LINEAR_SHAPES = {  # config 5's products at tp1: (n_out, k, SwiGLU)
@@ -763,6 +799,9 @@ def main():
                     help="with --only linear: time this product alone")
     ap.add_argument("--split-pages", type=int, default=0,
                     help="pages per split of the paged decode (0 = the library's choice)")
+    ap.add_argument("--kernel-shares", action="store_true",
+                    help="with --only decoder: per-kernel device-time shares of the step on rank 0 "
+                         "(torch.profiler CUDA activity)")
     ap.add_argument("--seqs", type=int, default=0,
                     help="override the number of sequences (smaller cases for ncu captures)")
     args = ap.parse_args()
@@ -783,7 +822,7 @@ def main():
         elif args.only == "linear":
             r = measure_linear(args.steps, args.warmup, world, pk, args.linear_shape)
         elif args.only == "decoder":
-            r = measure_decoder(args.steps, args.warmup, world, rank, pk)
+            r = measure_decoder(args.steps, args.warmup, world, rank, pk, shares=args.kernel_shares)
         elif args.only == "prefill":
             r = measure_prefill(args.steps, args.warmup, world, pk, rank)
         elif args.only == "f32":
