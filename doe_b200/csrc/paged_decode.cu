@@ -24,7 +24,7 @@
 // flipped, in the low half of 1024's f16 bits); the 1152 offsets are removed
 // once per row instead of per element: S -= 1152 * sum(q), O -= 1152 *
 // sum(f16 P).  The K scale multiplies S and the V scale folds into P.  Scores
-// run in the log2 domain (exp2f).
+// run in the log2 domain (the SFU's ex2 per key; exp2f for the merges).
 #include "tma.cuh"
 
 namespace doe {
@@ -164,6 +164,13 @@ __device__ __forceinline__ uint32_t lds32(uint32_t addr) {
   return v;
 }
 
+// 2^x on the SFU (ex2.approx.ftz: relative error ~2^-22, -inf -> +0), for the
+// per-key exponentials of the online softmax
+__device__ __forceinline__ float ex2a(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 // CAP: the score softcap is compiled in only where a launch asks for it
 template <bool INT8, int GROUP, bool CAP>
 __global__ void __launch_bounds__(kWarps * 32)
@@ -407,13 +414,14 @@ __global__ void __launch_bounds__(kWarps * 32)
 
     // ---- online softmax (log2 domain), rows r ------------------------------
     float x[2][2];
-    bool valid[2][2];
+    // only the window's first tile and the sequence's last hold dead keys;
+    // int8 tiles skip the per-key checks elsewhere (the f16 kernel, bound by
+    // HBM rather than issue, keeps them)
+    const bool edge = !INT8 || pos0 < min_key || pos0 + 16 > seq_len;
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int key = pos0 + nb * 8 + 2 * c + e;
-        valid[nb][e] = key < seq_len && key >= min_key;
         float sv = s[nb][e];
         if (INT8) {
           __half2 k2 = *reinterpret_cast<__half2*>(&ksc[nb]);
@@ -421,8 +429,17 @@ __global__ void __launch_bounds__(kWarps * 32)
         }
         // softcap (…wgsl:197-199): cap * tanh((q.k * scale) / cap), then log2 domain
         const float xs = CAP ? a.softcap * tanhf(sv * a.scale / a.softcap) * kLog2e : sv * a.scale_log2;
-        x[nb][e] = valid[nb][e] ? xs : -INFINITY;
+        x[nb][e] = xs;
       }
+    if (edge) {
+#pragma unroll
+      for (int nb = 0; nb < 2; ++nb)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int key = pos0 + nb * 8 + 2 * c + e;
+          if (!(key < seq_len && key >= min_key)) x[nb][e] = -INFINITY;
+        }
+    }
     float tmax = fmaxf(fmaxf(x[0][0], x[0][1]), fmaxf(x[1][0], x[1][1]));
     tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
     tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
@@ -431,12 +448,12 @@ __global__ void __launch_bounds__(kWarps * 32)
     // most tiles skip the rescale; the tile holds a valid key, so tmax is finite
     const bool grow = tmax > m_run + 8.0f;
     const float m_new = grow ? tmax : m_run;
-    const float corr = grow ? exp2f(m_run - m_new) : 1.0f;
+    const float corr = grow ? ex2a(m_run - m_new) : 1.0f;
     float p[2][2];
 #pragma unroll
     for (int nb = 0; nb < 2; ++nb)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) p[nb][e] = exp2f(x[nb][e] - m_new);
+      for (int e = 0; e < 2; ++e) p[nb][e] = ex2a(x[nb][e] - m_new);
     l_run = l_run * corr + ((p[0][0] + p[0][1]) + (p[1][0] + p[1][1]));
     m_run = m_new;
 
@@ -450,7 +467,7 @@ __global__ void __launch_bounds__(kWarps * 32)
           __half2 v2 = *reinterpret_cast<__half2*>(&vsc[nb]);
           sc = e ? __high2float(v2) : __low2float(v2);
         }
-        pv[nb][e] = (valid[nb][e] && r < GROUP) ? p[nb][e] * sc : 0.0f;
+        pv[nb][e] = r < GROUP ? p[nb][e] * sc : 0.0f;  // dead keys have p = +0
       }
     const uint32_t pb0 = pack_half2(pv[0][0], pv[0][1]);
     const uint32_t pb1 = pack_half2(pv[1][0], pv[1][1]);
