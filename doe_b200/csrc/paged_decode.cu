@@ -53,7 +53,14 @@ struct PagedDecodeArgs {
   int split_tiles, max_splits;
   int out_bf16;
   float scale_log2;
+  int page_shift;           // log2(page_size) when it is a power of two, else -1
 };
+
+// pos / page_size: a shift for power-of-two pages (every common size), so the
+// per-tile copy issue carries no integer division
+__device__ __forceinline__ int page_of(const PagedDecodeArgs& a, int pos) {
+  return a.page_shift >= 0 ? pos >> a.page_shift : pos / a.page_size;
+}
 
 constexpr int kD = 128;
 constexpr int kWarps = 4;
@@ -231,7 +238,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   int pg = -1;
   if (lane < nt) {
     const int pos = (tile_origin + tile_begin + warp + kWarps * lane) << 4;
-    pg = table[pos / a.page_size];
+    pg = table[page_of(a, pos)];
   }
 
   // ---- Q fragments (rows = heads g*GROUP + r, r < GROUP) -----------------
@@ -318,7 +325,7 @@ __global__ void __launch_bounds__(kWarps * 32)
       return;
     }
     const int pos0 = (tile_origin + tile_begin + warp + kWarps * k) << 4;
-    const int pidx = pos0 / a.page_size;
+    const int pidx = page_of(a, pos0);
     const int in0 = pos0 - pidx * a.page_size;
     const int row0 = page * a.page_size + in0;
     const uint32_t dst = slot(k);
@@ -419,18 +426,23 @@ __global__ void __launch_bounds__(kWarps * 32)
     // HBM rather than issue, keeps them)
     const bool edge = !INT8 || pos0 < min_key || pos0 + 16 > seq_len;
 #pragma unroll
-    for (int nb = 0; nb < 2; ++nb)
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float sv = s[nb][e];
-        if (INT8) {
-          __half2 k2 = *reinterpret_cast<__half2*>(&ksc[nb]);
-          sv = (sv - q1152) * (e ? __high2float(k2) : __low2float(k2));
-        }
+    for (int nb = 0; nb < 2; ++nb) {
+      // the two keys of a score pair in packed FP32: (s - 1152 sum q) * k_scale,
+      // then the log2-domain scale, each product and sum rounded as in scalar form
+      float2 sv = make_float2(s[nb][0], s[nb][1]);
+      if (INT8)
+        sv = fmul2(fadd2(sv, make_float2(-q1152, -q1152)),
+                   __half22float2(*reinterpret_cast<const __half2*>(&ksc[nb])));
+      if (CAP) {
         // softcap (…wgsl:197-199): cap * tanh((q.k * scale) / cap), then log2 domain
-        const float xs = CAP ? a.softcap * tanhf(sv * a.scale / a.softcap) * kLog2e : sv * a.scale_log2;
-        x[nb][e] = xs;
+        x[nb][0] = a.softcap * tanhf(sv.x * a.scale / a.softcap) * kLog2e;
+        x[nb][1] = a.softcap * tanhf(sv.y * a.scale / a.softcap) * kLog2e;
+      } else {
+        const float2 xs = fmul2(sv, make_float2(a.scale_log2, a.scale_log2));
+        x[nb][0] = xs.x;
+        x[nb][1] = xs.y;
       }
+    }
     if (edge) {
 #pragma unroll
       for (int nb = 0; nb < 2; ++nb)
@@ -781,6 +793,9 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.num_kv_heads = (int)Hkv;
   a.num_pages = (int)kv->num_pages;
   a.page_size = (int)kv->page_size;
+  a.page_shift = -1;
+  for (int sh = 0; sh < 31; ++sh)
+    if (kv->page_size == (1u << sh)) a.page_shift = sh;
   a.max_pages = (int)kv->max_pages_per_seq;
   a.split_tiles = (int)split_tiles;
   a.max_splits = (int)max_splits;
