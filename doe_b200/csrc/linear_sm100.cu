@@ -71,7 +71,7 @@ enum Bar { FULL0 = 0, EMPTY0 = FULL0 + kStages, ACC_FULL0 = EMPTY0 + kStages, AC
            MMA_DONE = ACC_EMPTY0 + 2, RECV_FULL = MMA_DONE + 1, NUM_BARS };
 constexpr uint32_t OFF_BAR = kStages * kStageBytes;
 constexpr uint32_t OFF_MISC = OFF_BAR + 8 * NUM_BARS;  // TMEM slot, abort flag, last-arrival flag
-constexpr uint32_t OFF_XCHG = OFF_BAR + 512;            // SwiGLU up values [NB][64] f32
+constexpr uint32_t OFF_XCHG = OFF_BAR + 512;            // SwiGLU mate values [NB / 2][128] f32
 constexpr uint32_t kTileBytes = BM * NB * 4;            // one f32 accumulator tile (16 KB)
 // cluster mode: the other CTAs' accumulator tiles, row r's 32 values in one
 // 128-byte line with 16-byte chunk c at c ^ (r & 7)
@@ -296,6 +296,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       const bool whole = it == tile * a.kb && end == (tile + 1) * a.kb;
       it = end;
       const int acc = seg & 1;
+      // a residual this CTA will certainly add (a whole tile, or the tile of a
+      // cluster's rank 0) is loaded while the MMAs still run, so its latency
+      // leaves the tail of the launch
+      const bool pre_res = a.residual != nullptr && a.epilogue != DOE_LINEAR_SWIGLU &&
+                           (whole || (a.cluster > 1 && crank == 0));
+      float rres[NB];
+      if (pre_res) {
+        const size_t col = (size_t)tile * BM + row;
+#pragma unroll
+        for (int j = 0; j < NB; ++j) rres[j] = j < a.batch ? a.residual[(size_t)j * a.n_out + col] : 0.0f;
+      }
       const bool ok = epi_all(wait_bar(bar(ACC_FULL0 + acc), (uint32_t)(seg >> 1) & 1, abort_flag, a.status));
       if (!ok) break;
       tc_fence_after();
@@ -377,20 +388,26 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
 
       if (a.epilogue == DOE_LINEAR_SWIGLU) {
-        // rows 0-63 of the tile are gate rows, 64-127 the matching up rows
-        if (row >= 64) {
+        // rows 0-63 of the tile are gate rows, 64-127 the matching up rows;
+        // the threads of rows r and r + 64 split the batch: the gate-row
+        // thread finishes columns [0, 16), the up-row thread [16, 32), each
+        // taking its mate's value for those columns through shared memory,
+        // so all four epilogue warps share the SwiGLU (one warp per
+        // scheduler, with the exponentials on the SFU)
+        const bool gate = row < 64;
+        const int j0 = gate ? 0 : NB / 2;
 #pragma unroll
-          for (int j = 0; j < NB; ++j) xchg[j * 64 + row - 64] = v[j];
-        }
+        for (int jj = 0; jj < NB / 2; ++jj) xchg[jj * 128 + row] = gate ? v[NB / 2 + jj] : v[jj];
         epi_sync();
-        if (row < 64) {
-          const size_t width = (size_t)a.n_out / 2, col = (size_t)tile * 64 + row;
+        const size_t width = (size_t)a.n_out / 2, col = (size_t)tile * 64 + (row & 63);
+        const int mate = row ^ 64;
 #pragma unroll
-          for (int j = 0; j < NB; ++j) {
-            if (j < a.batch) {
-              const float g = v[j], u = xchg[j * 64 + row];
-              store_elem(a.out[0], a.dtype, j * width + col, g / (1.0f + expf(-g)) * u);
-            }
+        for (int jj = 0; jj < NB / 2; ++jj) {
+          const int j = j0 + jj;
+          if (j < a.batch) {
+            const float other = xchg[jj * 128 + mate], mine = gate ? v[jj] : v[NB / 2 + jj];
+            const float g = gate ? mine : other, u = gate ? other : mine;
+            store_elem(a.out[0], a.dtype, j * width + col, __fdividef(g, 1.0f + __expf(-g)) * u);
           }
         }
         // the next writes to xchg come after the next segment's epi_all
@@ -405,12 +422,13 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           // all residual loads before any store: each (row, column) is read and
           // written by this thread alone, so an in-place residual (out[0] ==
           // residual) stays correct while the loads overlap
-          float r[NB];
+          if (!pre_res) {
 #pragma unroll
-          for (int j = 0; j < NB; ++j) r[j] = j < a.batch ? a.residual[(size_t)j * a.n_out + col] : 0.0f;
+            for (int j = 0; j < NB; ++j) rres[j] = j < a.batch ? a.residual[(size_t)j * a.n_out + col] : 0.0f;
+          }
 #pragma unroll
           for (int j = 0; j < NB; ++j)
-            if (j < a.batch) static_cast<float*>(dst)[j * width + (col - base)] = v[j] + r[j];
+            if (j < a.batch) static_cast<float*>(dst)[j * width + (col - base)] = v[j] + rres[j];
         } else {
 #pragma unroll
           for (int j = 0; j < NB; ++j)
