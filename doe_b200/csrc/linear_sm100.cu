@@ -12,9 +12,13 @@
 // product are divided evenly over a persistent grid of at most one CTA per
 // SM, so the grid is balanced for any (n_out, k); a CTA's range can start and
 // end inside a tile.  A CTA that covers a whole tile runs the epilogue from
-// TMEM; otherwise it writes its f32 partial tile to the workspace and the
-// last contributor to arrive sums all the tile's partials in contributor
-// order (the result does not depend on arrival order) and runs the epilogue.
+// TMEM.  A split tile is finished by the CTA holding its first k block, for
+// which it is the last segment: the later contributors (for which it is the
+// first) write their f32 partial tiles to the workspace and count in, and the
+// finisher waits for the count, adds the partials to its own accumulator in
+// contributor order (the result does not depend on timing) and runs the
+// epilogue.  That wait needs every CTA of the grid resident at once, which a
+// grid of at most one CTA per SM gives; it is bounded like every other wait.
 // Work split (cluster): when there are at most half as many tiles as SMs, a
 // tile's k range is split over a cluster of up to 4 CTAs instead (the largest
 // size whose clusters are all resident at once).  Ranks 1-3 send their f32
@@ -70,7 +74,7 @@ constexpr int kMaxCluster = 4;            // CTAs of one tile in cluster mode
 enum Bar { FULL0 = 0, EMPTY0 = FULL0 + kStages, ACC_FULL0 = EMPTY0 + kStages, ACC_EMPTY0 = ACC_FULL0 + 2,
            MMA_DONE = ACC_EMPTY0 + 2, RECV_FULL = MMA_DONE + 1, NUM_BARS };
 constexpr uint32_t OFF_BAR = kStages * kStageBytes;
-constexpr uint32_t OFF_MISC = OFF_BAR + 8 * NUM_BARS;  // TMEM slot, abort flag, last-arrival flag
+constexpr uint32_t OFF_MISC = OFF_BAR + 8 * NUM_BARS;  // TMEM slot, abort flag
 constexpr uint32_t OFF_XCHG = OFF_BAR + 512;            // SwiGLU mate values [NB / 2][128] f32
 constexpr uint32_t kTileBytes = BM * NB * 4;            // one f32 accumulator tile (16 KB)
 // cluster mode: the other CTAs' accumulator tiles, row r's 32 values in one
@@ -115,6 +119,12 @@ __device__ __forceinline__ bool epi_all(bool ok) {
       : "r"((uint32_t)ok)
       : "memory");
   return r != 0;
+}
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ long long it_begin(long long c, const Args& a) { return c * a.iters / a.ctas; }
@@ -173,7 +183,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 8);
-  volatile int* last_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 16);
   float* xchg = reinterpret_cast<float*>(smem + OFF_XCHG);
   auto bar = [&](int i) { return smem_addr(&bars[i]); };
 
@@ -288,7 +297,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int q = warp & 3;
     const int row = q * 32 + lane;  // weight row within the tile = TMEM lane
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
-    const long long first_tile = it0 / a.kb;
     int seg = 0;
     for (long long it = it0; it < it1; ++seg) {
       const long long tile = it / a.kb;
@@ -347,32 +355,46 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           }
         }
       } else if (!whole) {
-        const int slot = tile == first_tile ? 0 : 1;
-        float* p = a.part + ((size_t)blockIdx.x * 2 + slot) * NB * BM + row;
-#pragma unroll
-        for (int j = 0; j < NB; ++j) __stcg(p + j * BM, v[j]);
-        __threadfence();
-        epi_sync();
+        // Stream-K fix-up.  The tile's k blocks run on CTAs c0..c1 in order.
+        // For c0, which holds k block 0, the tile is its last segment; for
+        // every later contributor it is the first, so they finish their share
+        // early.  They store their f32 partial tile and count in; c0 waits
+        // (bounded) for the count, adds the partials to its own accumulator
+        // in contributor order (the sum c0 + c0+1 + ... of before) and runs
+        // the epilogue, with no round trip of its own partial through memory.
         const int c0 = cta_of(tile * a.kb, a), c1 = cta_of((tile + 1) * a.kb - 1, a);
+        if ((int)blockIdx.x != c0) {
+          float* p = a.part + ((size_t)blockIdx.x * 2) * NB * BM + row;  // slot 0: this CTA's first tile
+#pragma unroll
+          for (int j = 0; j < NB; ++j) __stcg(p + j * BM, v[j]);
+          __threadfence();
+          epi_sync();
+          if (threadIdx.x == 64) atomicAdd(&a.counters[tile], 1u);
+          continue;
+        }
         if (threadIdx.x == 64) {
-          const unsigned old = atomicAdd(&a.counters[tile], 1u);
-          const int last = old == (unsigned)(c1 - c0);
-          if (last) a.counters[tile] = 0u;  // ready for the next launch
-          *last_flag = last;
+          const unsigned want = (unsigned)(c1 - c0);
+          const long long t0 = clock64();
+          while (ld_acquire_u32(&a.counters[tile]) < want) {
+            if (clock64() - t0 > kWaitCycles) {
+              *abort_flag = 1;
+              report(a.status, DOE_DEVICE_ERR_TIMEOUT);
+              break;
+            }
+            __nanosleep(64);
+          }
+          a.counters[tile] = 0u;  // ready for the next launch
         }
         epi_sync();
-        if (!*last_flag) continue;
+        if (*abort_flag) break;
         __threadfence();
-#pragma unroll
-        for (int j = 0; j < NB; ++j) v[j] = 0.0f;
-        // contributors in order, four partial tiles in flight at a time
-        for (int c = c0; c <= c1; c += 4) {
+        // the later contributors in order, four partial tiles in flight at a time
+        for (int c = c0 + 1; c <= c1; c += 4) {
           float t[4][NB];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             if (c + u <= c1) {
-              const int sl = tile == it_begin(c + u, a) / a.kb ? 0 : 1;
-              const float* pc = a.part + ((size_t)(c + u) * 2 + sl) * NB * BM + row;
+              const float* pc = a.part + ((size_t)(c + u) * 2) * NB * BM + row;
 #pragma unroll
               for (int j = 0; j < NB; ++j) t[u][j] = __ldcg(pc + j * BM);
             }
