@@ -121,6 +121,19 @@ __device__ __forceinline__ bool epi_all(bool ok) {
   return r != 0;
 }
 
+// Cluster mode: the rank that finishes row block q (rows 32q .. 32q + 31) of
+// the tile.  The blocks are dealt round the cluster so every rank sums and
+// stores a share; SwiGLU pairs row r with r + 64, so rank 0 keeps them all.
+__device__ __forceinline__ int block_owner(int q, const Args& a) {
+  return a.epilogue == DOE_LINEAR_SWIGLU ? 0 : q % a.cluster;
+}
+// Bytes the other ranks send to `rank`: each owned row, once from each of them.
+__device__ __forceinline__ uint32_t recv_bytes(int rank, const Args& a) {
+  uint32_t n = 0;
+  for (int q = 0; q < 4; ++q) n += block_owner(q, a) == rank ? 32u : 0u;
+  return n * (uint32_t)(a.cluster - 1) * (NB * 4);
+}
+
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
@@ -195,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     for (int i = 0; i < NUM_BARS; ++i) mbar_init(bar(i), (i >= ACC_EMPTY0 && i < ACC_EMPTY0 + 2) ? 4u : 1u);
     *abort_flag = 0;
     // cluster mode: the tile's other CTAs send their accumulators here
-    if (a.cluster > 1 && crank == 0) mbar_expect_tx(bar(RECV_FULL), (uint32_t)(a.cluster - 1) * kTileBytes);
+    if (a.cluster > 1 && recv_bytes((int)crank, a) > 0) mbar_expect_tx(bar(RECV_FULL), recv_bytes((int)crank, a));
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   if (warp == 1) {
@@ -308,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       // cluster's rank 0) is loaded while the MMAs still run, so its latency
       // leaves the tail of the launch
       const bool pre_res = a.residual != nullptr && a.epilogue != DOE_LINEAR_SWIGLU &&
-                           (whole || (a.cluster > 1 && crank == 0));
+                           (whole || (a.cluster > 1 && block_owner(q, a) == (int)crank));
       float rres[NB];
       if (pre_res) {
         const size_t col = (size_t)tile * BM + row;
@@ -329,22 +342,25 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       for (int j = 0; j < NB; ++j) v[j] = __uint_as_float(r[j]);
 
       if (a.cluster > 1) {
-        // the tile's k ranges were split over a cluster: ranks 1.. send their
-        // accumulator rows into rank 0's shared memory; rank 0 adds them in
-        // rank order and finishes the tile
+        // the tile's k ranges were split over a cluster: each row block is
+        // finished by its owner rank; the other ranks send it their rows into
+        // the owner's shared memory (slot = sender rank, skipping the owner)
+        // and the owner adds them to its own in that fixed order
         const uint32_t line = (uint32_t)row * 128u;
-        if (crank != 0) {
-          const uint32_t dst = mapa_rank(sbase + OFF_RECV + (crank - 1) * kTileBytes + line, 0);
-          const uint32_t rbar = mapa_rank(bar(RECV_FULL), 0);
+        const int own = block_owner(q, a);
+        if (own != (int)crank) {
+          const int slot = (int)crank < own ? (int)crank : (int)crank - 1;
+          const uint32_t dst = mapa_rank(sbase + OFF_RECV + slot * kTileBytes + line, (uint32_t)own);
+          const uint32_t rbar = mapa_rank(bar(RECV_FULL), (uint32_t)own);
 #pragma unroll
           for (int c = 0; c < NB / 4; ++c)
             st_async_v4(dst + (((uint32_t)c ^ (row & 7)) << 4), v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3],
                         rbar);
           continue;
         }
-        if (!epi_all(wait_bar(bar(RECV_FULL), 0, abort_flag, a.status))) break;
-        for (int src = 1; src < a.cluster; ++src) {
-          const uint8_t* rl = smem + OFF_RECV + (src - 1) * kTileBytes + line;
+        if (!__all_sync(0xffffffffu, wait_bar(bar(RECV_FULL), 0, abort_flag, a.status))) break;
+        for (int slot = 0; slot < a.cluster - 1; ++slot) {
+          const uint8_t* rl = smem + OFF_RECV + slot * kTileBytes + line;
 #pragma unroll
           for (int c = 0; c < NB / 4; ++c) {
             const float4 t = *reinterpret_cast<const float4*>(rl + ((c ^ (row & 7)) << 4));
@@ -462,7 +478,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 
   // cluster rank 0 keeps its shared memory until every remote store has
   // landed, also when it stopped early (bounded)
-  if (a.cluster > 1 && crank == 0 && warp >= 2) mbar_wait_bounded(bar(RECV_FULL), 0);
+  if (a.cluster > 1 && warp >= 2 && recv_bytes((int)crank, a) > 0) mbar_wait_bounded(bar(RECV_FULL), 0);
   tc_fence_before();
   __syncthreads();
   // no CTA of a cluster leaves before rank 0 holds every accumulator

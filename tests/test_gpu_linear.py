@@ -35,8 +35,11 @@ def _close(got, ref, dtype):
                           f"{float((got - ref).abs().max()):.3g}"
 
 
+# cluster split-K over 4 (768, 4096, 128 x 14336, 1920), 3 (6144: 48 tiles) and
+# 2 ranks (8192: 64 tiles); stream-K fix-up below (5 x 256, 1 x 128) and in the
+# decoder tests' 28672-row products
 @pytest.mark.parametrize("batch,n_out,k", [(32, 768, 4096), (32, 4096, 512), (5, 256, 128), (1, 128, 64),
-                                           (32, 128, 14336), (17, 1920, 1792)])
+                                           (32, 128, 14336), (17, 1920, 1792), (32, 6144, 1024), (32, 8192, 512)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_linear_store(batch, n_out, k, dtype):
     g = np.random.default_rng(batch * 7 + n_out + k)
