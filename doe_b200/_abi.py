@@ -89,6 +89,7 @@ class DecodeOptions(C.Structure):
 
 DECODE_OUT_BF16 = 0x1
 DECODE_COUNTERS_ZEROED = 0x2
+DECODE_INPUTS_STABLE = 0x4
 LINEAR_STORE, LINEAR_SWIGLU = 0, 1
 DTYPE_BF16, DTYPE_F16, DTYPE_F32 = 0, 1, 2
 EP_IDENTITY, EP_RELU, EP_SIGMOID, EP_TANH, EP_GELU = 0, 1, 2, 3, 4

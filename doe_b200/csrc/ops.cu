@@ -238,7 +238,7 @@ int paged_decode_common(const char* who, const doe_paged_kv* kv, uint32_t num_se
   if (num_seqs == 0) return DOE_OK;
   if (num_seqs > 65535) return invalid("%s: at most 65535 sequences per launch", who);
   if (opts != nullptr) {
-    if ((opts->flags & ~(DOE_DECODE_OUT_BF16 | DOE_DECODE_COUNTERS_ZEROED)) != 0)
+    if ((opts->flags & ~(DOE_DECODE_OUT_BF16 | DOE_DECODE_COUNTERS_ZEROED | DOE_DECODE_INPUTS_STABLE)) != 0)
       return invalid("%s: unknown bits in options.flags", who);
     if (opts->freq_cis != nullptr) {
       int rr = check_rope_table(who, opts->freq_cis, opts->rope_positions);

@@ -54,6 +54,7 @@ struct PagedDecodeArgs {
   int out_bf16;
   float scale_log2;
   int page_shift;           // log2(page_size) when it is a power of two, else -1
+  int inputs_stable;        // DOE_DECODE_INPUTS_STABLE: first copies before griddepcontrol.wait
 };
 
 // pos / page_size: a shift for power-of-two pages (every common size), so the
@@ -64,6 +65,7 @@ __device__ __forceinline__ int page_of(const PagedDecodeArgs& a, int pos) {
 
 constexpr int kD = 128;
 constexpr int kWarps = 4;
+constexpr int kPageRegs = 4;  // page ids held per lane: 128 tiles per warp, 512 per split
 
 __device__ __forceinline__ uint4 ldcg4(const uint8_t* p) {
   uint4 v;
@@ -188,8 +190,9 @@ __global__ void __launch_bounds__(kWarps * 32)
   extern __shared__ __align__(1024) uint8_t dsmem_raw[];
   // the swizzled boxes need 1024-byte alignment
   uint8_t* dsmem = dsmem_raw + ((1024 - (smem_addr(dsmem_raw) & 1023)) & 1023);
-  pdl_wait();  // launched with launch_pdl: q, new K/V and the pools come from earlier kernels
-  pdl_trigger();
+  // launched with launch_pdl: q, new K/V and (unless inputs_stable) the
+  // lengths, table and pools come from earlier kernels
+  if (!a.inputs_stable) pdl_wait();
   const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
@@ -223,22 +226,79 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
   __syncwarp();
 
-  if (a.new_k != nullptr && split == nsplits - 1 && seq_len > 0) {
+  // ---- this warp's tiles: tile_begin + warp + 4k, k < nt; page ids up front
+  const int span = tile_end - tile_begin - warp;
+  const int nt = span > 0 ? (span + kWarps - 1) / kWarps : 0;
+  // page ids of the warp's tiles: lane l holds tile l + 32 i in pg[i]
+  auto load_page = [&](int i) {
+    if (lane + 32 * i >= nt) return -1;
+    return table[page_of(a, (tile_origin + tile_begin + warp + kWarps * (lane + 32 * i)) << 4)];
+  };
+  static_assert(kPageRegs == 4, "pg0..pg3");
+  const int pg0 = load_page(0), pg1 = load_page(1), pg2 = load_page(2), pg3 = load_page(3);
+  auto page_of_tile = [pg0, pg1, pg2, pg3](int k) {  // k warp-uniform
+    const int i = k >> 5;
+    return __shfl_sync(0xffffffffu, i == 0 ? pg0 : (i == 1 ? pg1 : (i == 2 ? pg2 : pg3)), k & 31);
+  };
+
+  const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
+  const uint32_t wbase = smem_addr(dsmem) + warp * R::kWarpBytes;
+  auto slot = [&](int k) { return wbase + (k % P) * R::kTile; };
+  auto scales = [&](int k) { return wbase + P * R::kTile + (k % P) * R::kScale; };
+
+  // Fills slot k % P with tile k (whole warp calls, one lane issues).  A tile
+  // whose page id is out of range gets a plain arrival instead, so the slot's
+  // barrier phase still advances; the consumer reports the bad page.
+  auto issue = [&](int k) {
+    const int page = page_of_tile(k);
+    if (lane != 0) return;
+    const uint32_t bar = smem_addr(&ring_bar[warp][k % P]);
+    if ((unsigned)page >= (unsigned)a.num_pages) {
+      mbar_arrive(bar);
+      return;
+    }
+    const int pos0 = (tile_origin + tile_begin + warp + kWarps * k) << 4;
+    const int pidx = page_of(a, pos0);
+    const int in0 = pos0 - pidx * a.page_size;
+    const int row0 = page * a.page_size + in0;
+    const uint32_t dst = slot(k);
+    // this warp read the slot's previous tile through the generic proxy
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    mbar_expect_tx(bar, R::kTx);
+    if (!INT8) {
+      tma_load_3d(dst, &tm_k, bar, 0, g, row0);
+      tma_load_3d(dst + 2048, &tm_k, bar, 64, g, row0);
+      tma_load_3d(dst + 4096, &tm_v, bar, 0, g, row0);
+      tma_load_3d(dst + 6144, &tm_v, bar, 64, g, row0);
+    } else {
+      tma_load_3d(dst, &tm_k, bar, 0, g, row0);
+      tma_load_3d(dst + 2048, &tm_v, bar, 0, g, row0);
+      const size_t sidx = ((size_t)page * Hkv + g) * a.page_size + in0;
+      bulk_load(scales(k), a.k_scale + sidx, 32, bar);
+      bulk_load(scales(k) + 32, a.v_scale + sidx, 32, bar);
+    }
+  };
+
+  // The first copies of the ring go out before the query work, and before
+  // griddepcontrol.wait when the caller vouches that seq_lens, the block table
+  // and the pool rows are final (DOE_DECODE_INPUTS_STABLE); a tile holding the
+  // row this launch appends waits for the append.
+  const bool appends = a.new_k != nullptr && split == nsplits - 1 && seq_len > 0;
+  const int new_tile = ((seq_len - 1) >> 4) - tile_origin - tile_begin;  // split-relative
+  int issued = 0;
+  for (; issued < P - 1 && issued < nt; ++issued)
+    if (appends && new_tile == warp + kWarps * issued) break;
+    else issue(issued);
+  if (a.inputs_stable) pdl_wait();
+  pdl_trigger();
+
+  if (appends) {
     if (warp == 0) {
       append_row<INT8>(a, b, g, seq_len - 1, table, lane);
       // the row is read back below by TMA (the async proxy)
       asm volatile("fence.proxy.async.global;\n" ::: "memory");
     }
     __syncthreads();
-  }
-
-  // ---- this warp's tiles: tile_begin + warp + 4k, k < nt; page ids up front
-  const int span = tile_end - tile_begin - warp;
-  const int nt = span > 0 ? (span + kWarps - 1) / kWarps : 0;
-  int pg = -1;
-  if (lane < nt) {
-    const int pos = (tile_origin + tile_begin + warp + kWarps * lane) << 4;
-    pg = table[page_of(a, pos)];
   }
 
   // ---- Q fragments (rows = heads g*GROUP + r, r < GROUP) -----------------
@@ -308,51 +368,13 @@ __global__ void __launch_bounds__(kWarps * 32)
   }
   float p1152 = 0.0f;  // int8: running sum of this row's f16 P (times 1152 at the end)
 
-  const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
-  const uint32_t wbase = smem_addr(dsmem) + warp * R::kWarpBytes;
-  auto slot = [&](int k) { return wbase + (k % P) * R::kTile; };
-  auto scales = [&](int k) { return wbase + P * R::kTile + (k % P) * R::kScale; };
-
-  // Fills slot k % P with tile k (whole warp calls, one lane issues).  A tile
-  // whose page id is out of range gets a plain arrival instead, so the slot's
-  // barrier phase still advances; the consumer reports the bad page.
-  auto issue = [&](int k) {
-    const int page = __shfl_sync(0xffffffffu, pg, k & 31);
-    if (lane != 0) return;
-    const uint32_t bar = smem_addr(&ring_bar[warp][k % P]);
-    if ((unsigned)page >= (unsigned)a.num_pages) {
-      mbar_arrive(bar);
-      return;
-    }
-    const int pos0 = (tile_origin + tile_begin + warp + kWarps * k) << 4;
-    const int pidx = page_of(a, pos0);
-    const int in0 = pos0 - pidx * a.page_size;
-    const int row0 = page * a.page_size + in0;
-    const uint32_t dst = slot(k);
-    // this warp read the slot's previous tile through the generic proxy
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-    mbar_expect_tx(bar, R::kTx);
-    if (!INT8) {
-      tma_load_3d(dst, &tm_k, bar, 0, g, row0);
-      tma_load_3d(dst + 2048, &tm_k, bar, 64, g, row0);
-      tma_load_3d(dst + 4096, &tm_v, bar, 0, g, row0);
-      tma_load_3d(dst + 6144, &tm_v, bar, 64, g, row0);
-    } else {
-      tma_load_3d(dst, &tm_k, bar, 0, g, row0);
-      tma_load_3d(dst + 2048, &tm_v, bar, 0, g, row0);
-      const size_t sidx = ((size_t)page * Hkv + g) * a.page_size + in0;
-      bulk_load(scales(k), a.k_scale + sidx, 32, bar);
-      bulk_load(scales(k) + 32, a.v_scale + sidx, 32, bar);
-    }
-  };
 
   float m_run = -INFINITY, l_run = 0.0f;
   float acc[8][4];
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) acc[mb][0] = acc[mb][1] = acc[mb][2] = acc[mb][3] = 0.0f;
 
-#pragma unroll
-  for (int s0 = 0; s0 < P - 1; ++s0)
+  for (int s0 = issued; s0 < P - 1; ++s0)
     if (s0 < nt) issue(s0);
   bool ring_ok = true;
   for (int k = 0; k < nt; ++k) {
@@ -363,7 +385,7 @@ __global__ void __launch_bounds__(kWarps * 32)
       if (lane == 0) report(a.status, DOE_DEVICE_ERR_TIMEOUT);
       break;
     }
-    const int page = __shfl_sync(0xffffffffu, pg, k & 31);
+    const int page = page_of_tile(k);
     if ((unsigned)page >= (unsigned)a.num_pages) {
       if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
       continue;
@@ -742,24 +764,31 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
     // f16, 128 for int8 measured best on config 3 / 4, whose work fills
     // several waves of 3 CTAs per SM on 148 SMs at that length).  Less work
     // than that (a decode batch of uniform contexts, or one tensor-parallel
-    // rank's few KV heads) runs best with as few splits as still keep about
-    // two CTAs per SM busy, each at most 128 tiles and all of one length.
+    // rank's few KV heads) runs best in ONE wave: a CTA that starts when an
+    // earlier one ends spends microseconds on its lengths, page ids and first
+    // copies while the SM's share of HBM idles.  So: as few splits as keep
+    // about two CTAs per SM busy, but no more than fit one wave of 3 CTAs per
+    // SM (config 5: 256 (sequence, kv head) rows, one split each, 0.778 ->
+    // 0.753 ms per step against three splits in 1.7 waves), each split at most
+    // kWarps * 32 * kPageRegs tiles and all of one length.
     const uint64_t seq_rows = (uint64_t)num_seqs * Hkv;
     const uint64_t want = ((uint64_t)max_tiles * seq_rows + 1775) / 1776;
     const uint32_t cap = kv->kv_dtype == DOE_KV_INT8 ? 128u : 64u;
     if (want >= cap) {
       split_tiles = cap;
     } else {
-      uint64_t s = (max_tiles + 127) / 128;
+      const uint64_t most = (uint64_t)kWarps * 32 * kPageRegs;
       const uint64_t fill = (280 + seq_rows - 1) / seq_rows;
-      if (s < fill) s = fill;
+      const uint64_t wave = 444 / seq_rows;
+      uint64_t s = fill < wave ? fill : wave;
+      if (s < (max_tiles + most - 1) / most) s = (max_tiles + most - 1) / most;
       if (s < 1) s = 1;
       const uint64_t t = (max_tiles + s - 1) / s;
       split_tiles = (uint32_t)(t < 4 ? 4 : t);
     }
   }
   if (split_tiles == 0) split_tiles = 1;
-  if (split_tiles > 4 * 32) split_tiles = 4 * 32;  // 4 warps x 32 prefetched page ids
+  if (split_tiles > kWarps * 32 * kPageRegs) split_tiles = kWarps * 32 * kPageRegs;  // prefetched page ids
   const uint32_t max_splits = max_tiles == 0 ? 1 : ceil_div(max_tiles, split_tiles);
   const uint64_t rows = (uint64_t)num_seqs * Hkv * max_splits * group;
   const uint64_t part_bytes = rows * (kD + 2) * sizeof(float);
@@ -806,6 +835,7 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
   a.softcap = opts ? opts->attn_softcap : 0.0f;
   a.scale = scale;
   a.out_bf16 = (opts && (opts->flags & DOE_DECODE_OUT_BF16)) ? 1 : 0;
+  a.inputs_stable = (opts && (opts->flags & DOE_DECODE_INPUTS_STABLE)) ? 1 : 0;
   cudaStream_t st = static_cast<cudaStream_t>(launch->stream);
   // arrival counters of the split stitch start at zero on every launch; the
   // last split of each (sequence, kv head) puts its counter back to zero, so a

@@ -212,10 +212,12 @@ class Decoder:
             t(li, "xn", self.xn)
             ops.linear(self.xn, L["wqkv"], [self.q, self.k, self.v], status=self.status, ws=self.lin_ws)
             t(li, "q", self.q), t(li, "k", self.k), t(li, "v", self.v)
+            # seq_lens, the table and this layer's pool rows are written by no
+            # kernel of the step but this call's own append (inputs_stable)
             ops.paged_decode(cache, self.q.view(B, self.qh, D), self.seq_lens, self.scale,
                              new_k=self.k.view(B, self.kvh, D), new_v=self.v.view(B, self.kvh, D),
                              out=self.attn.view(B, self.qh, D), status=self.status, freq_cis=self.freq_cis,
-                             out_dtype=torch.bfloat16, ws=self.dec_ws)
+                             out_dtype=torch.bfloat16, ws=self.dec_ws, inputs_stable=True)
             t(li, "attn", self.attn)
             if fused:
                 # partial o_proj into slot 0 of this rank's peer buffer, then the

@@ -101,7 +101,7 @@ def stitch(partials, out=None, stream=None):
 
 def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new_v=None, out=None,
                  split_pages: int = 0, status=None, stream=None, freq_cis=None, sliding_window: int = 0,
-                 softcap: float = 0.0, out_dtype=torch.float32, ws=None):
+                 softcap: float = 0.0, out_dtype=torch.float32, ws=None, inputs_stable: bool = False):
     """Batched GQA decode: q [B,H,D] f16, seq_lens [B] int32 -> out [B,H,D] f32.
 
     With new_k/new_v ([B,Hkv,D] f16) the new token is first written at
@@ -113,7 +113,10 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
     out_dtype torch.bfloat16 writes a bf16 output (DOE_DECODE_OUT_BF16).
     `ws`: a workspace kept for paged decodes alone, zeroed when created
     (decode_workspace); its split counters then need no clearing per call
-    (DOE_DECODE_COUNTERS_ZEROED)."""
+    (DOE_DECODE_COUNTERS_ZEROED).  inputs_stable: seq_lens, the block table and
+    the pool rows (other than the appended ones) are final before the call is
+    enqueued, so the first copies may start before the preceding kernel ends
+    (DOE_DECODE_INPUTS_STABLE)."""
     _need(q, torch.float16, "q")
     _need(seq_lens, torch.int32, "seq_lens")
     if out_dtype not in (torch.float32, torch.bfloat16):
@@ -124,6 +127,8 @@ def paged_decode(cache: PagedKVCache, q, seq_lens, scale: float, new_k=None, new
     flags = abi.DECODE_OUT_BF16 if out_dtype == torch.bfloat16 else 0
     if ws is not None:
         flags |= abi.DECODE_COUNTERS_ZEROED
+    if inputs_stable:
+        flags |= abi.DECODE_INPUTS_STABLE
     kv = cache.struct()
     lib = abi.lib()
     need = lib.doe_paged_decode_workspace_bytes(C.byref(kv), B, H, split_pages)

@@ -357,9 +357,19 @@ int doe_paged_decode_rope(const doe_paged_kv* kv, uint32_t num_seqs,
  *                              on zeroed memory; every decode that sets no
  *                              DOE_DEVICE_ERR_TIMEOUT leaves them zero), so
  *                              the per-call clear is skipped;
+ *                              DOE_DECODE_INPUTS_STABLE: seq_lens, the block
+ *                              table and every pool row other than the rows
+ *                              this call appends hold their final values
+ *                              before the call is enqueued (no kernel that
+ *                              may still run writes them), so the kernel
+ *                              reads them and starts its first copies before
+ *                              waiting for the preceding kernel (programmatic
+ *                              dependent launch); q, new_k, new_v and the
+ *                              RoPE table may still come from that kernel;
  *                              other bits must be 0.                       */
 #define DOE_DECODE_OUT_BF16 0x1u
 #define DOE_DECODE_COUNTERS_ZEROED 0x2u
+#define DOE_DECODE_INPUTS_STABLE 0x4u
 typedef struct doe_decode_options {
   const float* freq_cis;
   uint32_t rope_positions;

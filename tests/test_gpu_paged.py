@@ -85,6 +85,29 @@ def test_paged_decode_split_and_page_sizes(split_pages, page_size):
     within(_gpu_step(w, c, split_pages=split_pages), ref, F16_TOL)
 
 
+@pytest.mark.parametrize("split_pages", [1, 3, 0, 400])
+def test_paged_decode_inputs_stable_and_long_splits(split_pages):
+    """DOE_DECODE_INPUTS_STABLE issues each warp's first copy before the
+    append and the query work, except the copy of the tile that receives the
+    new row (split_pages 1: that tile is the only one of the last split;
+    3: the first tile of warp 2 there).  split_pages 400 gives splits of 400
+    tiles, so a warp walks up to 100 tiles and reads page ids from every
+    register of its prefetch (tiles 0-31, 32-63, 64-95, 96-127)."""
+    w = workloads.small_paged(17, [0, 15, 16, 33, 300, 2049, 6000, 6399])
+    c = _cache(w)
+    kp, vp, ks, vs = _host(c)
+    ref = _oracle_step(w, kp, vp, ks, vs)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    status = ops.status_word()
+    out = ops.paged_decode(c, t(w.q), t(w.seq_lens), w.scale, new_k=t(w.new_k), new_v=t(w.new_v),
+                           split_pages=split_pages, status=status, inputs_stable=True)
+    torch.cuda.synchronize()
+    gk, gv, _, _ = _host(c)
+    assert np.array_equal(gk, kp) and np.array_equal(gv, vp), "append wrote different cache bytes"
+    assert int(status.item()) == 0
+    within(out.cpu().numpy(), ref, F16_TOL)
+
+
 def test_paged_decode_without_append_reads_cache_only():
     w = workloads.small_paged(13, [40, 3, 129])
     c = _cache(w)
