@@ -84,64 +84,78 @@ __device__ __forceinline__ int clamp_len(int len, int cap) {
   return len < 0 ? 0 : (len > cap ? cap : len);
 }
 
-// Writes the new token's K/V row of kv head g at position pos (one warp).
+// The new token's K/V row of kv head g at position pos, written by one warp
+// in two steps: load() fetches the f16 rows (and the RoPE factors) right after
+// the launch's wait, store() rotates, quantises and writes them into the pool
+// later, when the loads have landed, so neither stalls the warp's walk.
 template <bool INT8>
-__device__ void append_row(const PagedDecodeArgs& a, int b, int g, int pos,
-                           const int32_t* table, int lane) {
-  const int pidx = pos / a.page_size;
-  const int page = table[pidx];
-  if ((unsigned)page >= (unsigned)a.num_pages) {
-    if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
-    return;
-  }
-  const int in_page = pos - pidx * a.page_size;
-  const size_t row = (size_t)page * a.page_size + in_page;
-  const int Hkv = a.num_kv_heads;
-  const __half* srcs[2] = {a.new_k + ((size_t)b * Hkv + g) * kD,
-                           a.new_v + ((size_t)b * Hkv + g) * kD};
-  const uint8_t* pools[2] = {a.k_pool, a.v_pool};
-  const __half* scales[2] = {a.k_scale, a.v_scale};
-  // RoPE on the K row: dim d < 64 (lanes 0-15) pairs with d + 64 (lane ^ 16)
+struct AppendRow {
+  uint2 raw[2];       // lane's 4 elements of the K and the V row
   float rc[4], rsn[4];
-  if (a.freq_cis != nullptr)
-    rope_table<2>(a.freq_cis, a.rope_positions, kD / 2, pos, 4 * (lane & 15), a.status, lane == 0, rc, rsn);
-#pragma unroll
-  for (int kv = 0; kv < 2; ++kv) {
-    // lane owns elements [4*lane, 4*lane+4)
-    uint2 raw = *reinterpret_cast<const uint2*>(srcs[kv] + 4 * lane);
-    if (kv == 0 && a.freq_cis != nullptr) {
-      const uint2 partner = make_uint2(__shfl_xor_sync(0xffffffffu, raw.x, 16),
-                                       __shfl_xor_sync(0xffffffffu, raw.y, 16));
-      rope_rotate<2>(reinterpret_cast<const uint32_t*>(&raw), reinterpret_cast<const uint32_t*>(&partner),
-                     lane < 16, rc, rsn, reinterpret_cast<uint32_t*>(&raw));
-    }
-    if (!INT8) {
-      uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * (kD * 2) + 8 * lane;
-      *reinterpret_cast<uint2*>(dst) = raw;
-    } else {
-      __half2 h01 = *reinterpret_cast<__half2*>(&raw.x);
-      __half2 h23 = *reinterpret_cast<__half2*>(&raw.y);
-      float x[4] = {__low2float(h01), __high2float(h01), __low2float(h23), __high2float(h23)};
-      float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
-      amax = warp_max(amax);
-      __half sh = __float2half_rn(div127(amax));
-      float sf = __half2float(sh);
-      int qv[4] = {0, 0, 0, 0};
-      if (sf != 0.0f) {
-        const float rs = __frcp_rn(sf);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) qv[e] = quantize_s8(x[e], sf, rs);
-      }
-      const uint32_t packed = pack_s8x4(qv[0], qv[1], qv[2], qv[3]);
-      uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * kD + 4 * lane;
-      *reinterpret_cast<uint32_t*>(dst) = packed;
-      if (lane == 0) {
-        __half* sdst = const_cast<__half*>(scales[kv]);
-        sdst[((size_t)page * Hkv + g) * a.page_size + in_page] = sh;
-      }
-    }
+  int page, in_page;
+
+  __device__ __forceinline__ void load(const PagedDecodeArgs& a, int b, int g, int pos, const int32_t* table,
+                                       int lane) {
+    const int pidx = pos / a.page_size;
+    page = table[pidx];
+    in_page = pos - pidx * a.page_size;
+    const size_t src = ((size_t)b * a.num_kv_heads + g) * kD + 4 * lane;  // lane owns [4 lane, 4 lane + 4)
+    raw[0] = *reinterpret_cast<const uint2*>(a.new_k + src);
+    raw[1] = *reinterpret_cast<const uint2*>(a.new_v + src);
+    // RoPE on the K row: dim d < 64 (lanes 0-15) pairs with d + 64 (lane ^ 16)
+    if (a.freq_cis != nullptr)
+      rope_table<2>(a.freq_cis, a.rope_positions, kD / 2, pos, 4 * (lane & 15), a.status, lane == 0, rc, rsn);
   }
-}
+
+  // Ends with the fence that lets this warp's later TMA copies (the async
+  // proxy) read the row.
+  __device__ __forceinline__ void store(const PagedDecodeArgs& a, int g, int lane) {
+    if ((unsigned)page >= (unsigned)a.num_pages) {
+      if (lane == 0) report(a.status, DOE_DEVICE_ERR_PAGE);
+      return;
+    }
+    const size_t row = (size_t)page * a.page_size + in_page;
+    const int Hkv = a.num_kv_heads;
+    const uint8_t* pools[2] = {a.k_pool, a.v_pool};
+    const __half* scales[2] = {a.k_scale, a.v_scale};
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      uint2 v = raw[kv];
+      if (kv == 0 && a.freq_cis != nullptr) {
+        const uint2 partner = make_uint2(__shfl_xor_sync(0xffffffffu, v.x, 16), __shfl_xor_sync(0xffffffffu, v.y, 16));
+        rope_rotate<2>(reinterpret_cast<const uint32_t*>(&raw[0]), reinterpret_cast<const uint32_t*>(&partner),
+                       lane < 16, rc, rsn, reinterpret_cast<uint32_t*>(&v));
+      }
+      if (!INT8) {
+        uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * (kD * 2) + 8 * lane;
+        *reinterpret_cast<uint2*>(dst) = v;
+      } else {
+        __half2 h01 = *reinterpret_cast<__half2*>(&v.x);
+        __half2 h23 = *reinterpret_cast<__half2*>(&v.y);
+        float x[4] = {__low2float(h01), __high2float(h01), __low2float(h23), __high2float(h23)};
+        float amax = fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3])));
+        amax = warp_max(amax);
+        __half sh = __float2half_rn(div127(amax));
+        float sf = __half2float(sh);
+        int qv[4] = {0, 0, 0, 0};
+        if (sf != 0.0f) {
+          const float rs = __frcp_rn(sf);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) qv[e] = quantize_s8(x[e], sf, rs);
+        }
+        const uint32_t packed = pack_s8x4(qv[0], qv[1], qv[2], qv[3]);
+        uint8_t* dst = const_cast<uint8_t*>(pools[kv]) + (row * Hkv + g) * kD + 4 * lane;
+        *reinterpret_cast<uint32_t*>(dst) = packed;
+        if (lane == 0) {
+          __half* sdst = const_cast<__half*>(scales[kv]);
+          sdst[((size_t)page * Hkv + g) * a.page_size + in_page] = sh;
+        }
+      }
+    }
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");
+    __syncwarp();
+  }
+};
 
 // Per-warp ring of TMA-filled tiles.  A slot holds one 16-token tile, each
 // 16-row x 128-byte box on a 1024-byte boundary (chunk x of row R at x ^ R%8):
@@ -292,14 +306,12 @@ __global__ void __launch_bounds__(kWarps * 32)
   if (a.inputs_stable) pdl_wait();
   pdl_trigger();
 
-  if (appends) {
-    if (warp == 0) {
-      append_row<INT8>(a, b, g, seq_len - 1, table, lane);
-      // the row is read back below by TMA (the async proxy)
-      asm volatile("fence.proxy.async.global;\n" ::: "memory");
-    }
-    __syncthreads();
-  }
+  // the warp whose walk holds the new row's tile appends the row itself, so
+  // no other warp waits for it: loads now, the pool write after the query's
+  // loads, before any copy of that tile
+  const bool append_pending = appends && new_tile % kWarps == warp;
+  AppendRow<INT8> app;
+  if (append_pending) app.load(a, b, g, seq_len - 1, table, lane);
 
   // ---- Q fragments (rows = heads g*GROUP + r, r < GROUP) -----------------
   // f16 pools:  k-block j = 2i + jj holds dims 32i + 8c + 4jj + {0,1 | 2,3}
@@ -374,6 +386,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 #pragma unroll
   for (int mb = 0; mb < 8; ++mb) acc[mb][0] = acc[mb][1] = acc[mb][2] = acc[mb][3] = 0.0f;
 
+  // after the query's loads: the row's loads, issued with them, have landed
+  if (append_pending) app.store(a, g, lane);
   for (int s0 = issued; s0 < P - 1; ++s0)
     if (s0 < nt) issue(s0);
   bool ring_ok = true;
