@@ -113,6 +113,13 @@ class LinearOut(C.Structure):
                 ("epilogue", C.c_uint32), ("residual", C.c_void_p)]
 
 
+class LinearNorm(C.Structure):
+    """doe_linear_norm: the RMSNorm split over two doe_linear_bf16_norm products."""
+
+    _fields_ = [("gamma", C.c_void_p), ("normed_out", C.c_void_p), ("ssq_out", C.c_void_p),
+                ("ssq_in", C.c_void_p), ("eps", C.c_float)]
+
+
 _P = C.c_void_p
 _U32 = C.c_uint32
 _U64 = C.c_uint64
@@ -182,6 +189,7 @@ SIGNATURES = {
     "doe_ep_gemm_relu_gemm_f32": (_I, [_P, _P, _P, _P, _P, _P, _U32, _U32, _U32, _U32, _LP]),
     "doe_linear_workspace_bytes": (_U64, [_U32, _U32]),
     "doe_linear_bf16": (_I, [_P, _P, _U32, _U32, _U32, C.POINTER(LinearOut), _LP]),
+    "doe_linear_bf16_norm": (_I, [_P, _P, _U32, _U32, _U32, C.POINTER(LinearOut), C.POINTER(LinearNorm), _LP]),
     "doe_tp_buffer_bytes": (_U64, [_U32, _U32]),
     "doe_tp_slot_ptr": (_P, [_P, _U32, _U32, _U32]),
     "doe_peer_buffer_create": (_I, [_U64, C.POINTER(_P), _P]),

@@ -102,7 +102,7 @@ int launch_prefill_f16(const void* q, const void* k, const void* v, float* out, 
                        const doe_launch* launch);
 uint64_t linear_workspace(uint32_t n_out, uint32_t k);
 int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
-                  const doe_linear_out* out, const doe_launch* launch);
+                  const doe_linear_out* out, const doe_linear_norm* norm, const doe_launch* launch);
 int launch_rmsnorm(const float* x, const void* gamma, float eps, void* out, uint32_t rows, uint32_t cols,
                    const doe_launch* launch);
 int num_sms();  // of the current device, cached per device

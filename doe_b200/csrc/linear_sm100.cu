@@ -75,7 +75,9 @@ enum Bar { FULL0 = 0, EMPTY0 = FULL0 + kStages, ACC_FULL0 = EMPTY0 + kStages, AC
            MMA_DONE = ACC_EMPTY0 + 2, RECV_FULL = MMA_DONE + 1, NUM_BARS };
 constexpr uint32_t OFF_BAR = kStages * kStageBytes;
 constexpr uint32_t OFF_MISC = OFF_BAR + 8 * NUM_BARS;  // TMEM slot, abort flag
+constexpr uint32_t OFF_RSCALE = OFF_MISC + 64;          // consumer's row scales [NB] f32
 constexpr uint32_t OFF_XCHG = OFF_BAR + 512;            // SwiGLU mate values [NB / 2][128] f32
+static_assert(OFF_RSCALE + NB * 4 <= OFF_XCHG, "misc area");
 constexpr uint32_t kTileBytes = BM * NB * 4;            // one f32 accumulator tile (16 KB)
 // cluster mode: the other CTAs' accumulator tiles, row r's 32 values in one
 // 128-byte line with 16-byte chunk c at c ^ (r & 7)
@@ -92,6 +94,14 @@ struct Args {
   int batch, n_out, kb, tiles, ctas, epilogue, dtype;
   long long iters;         // tiles * kb
   int cluster;             // > 1: cluster mode, this many CTAs per tile; else stream-K
+  // RMSNorm split over two products (doe_linear_norm): the producer of the
+  // residual stream also writes bf16(y * gamma) and per-32-column sums of
+  // squares; the consumer scales its rows by 1 / sqrt(sum / k + eps)
+  const __nv_bfloat16* gamma_out;  // [n_out] or null
+  __nv_bfloat16* normed_out;       // [batch, n_out]
+  float* ssq_out;                  // [n_out / 32][NB]
+  const float* ssq_in;             // [k / 32][NB] or null
+  float eps;
 };
 
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, volatile int* abort_flag,
@@ -176,6 +186,22 @@ __device__ __forceinline__ void cluster_sync_all() {
 // The CTA whose iteration range holds iteration i.
 __device__ __forceinline__ int cta_of(long long i, const Args& a) {
   return (int)(((i + 1) * a.ctas - 1) / a.iters);
+}
+
+// eight f32 values as eight bf16 (or f16), rounded to nearest even
+__device__ __forceinline__ uint4 pack8(const float* y, bool bf16) {
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    if (bf16) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * e], y[2 * e + 1]);
+      w[e] = *reinterpret_cast<const uint32_t*>(&h);
+    } else {
+      const __half2 h = __floats2half2_rn(y[2 * e], y[2 * e + 1]);
+      w[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 __device__ __forceinline__ void store_elem(void* base, int dtype, size_t idx, float y) {
@@ -310,6 +336,22 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     const int q = warp & 3;
     const int row = q * 32 + lane;  // weight row within the tile = TMEM lane
     const uint32_t t_lane = tmem + ((uint32_t)(q * 32) << 16);
+    const float* rscale = reinterpret_cast<const float*>(smem + OFF_RSCALE);
+    if (a.ssq_in != nullptr) {
+      // consumer of a split RMSNorm: batch row b's sum of squares over the
+      // k / 32 column blocks, thread (b, part) adding blocks part, part + 4,
+      // ... in order, then the four parts pairwise; computed while the MMAs run
+      const int b = row >> 2, part = row & 3;
+      const int nblk = a.kb * (BK / 32);
+      float sum = 0.0f;
+#pragma unroll 8
+      for (int i = part; i < nblk; i += 4) sum += a.ssq_in[(size_t)i * NB + b];
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if (part == 0)
+        reinterpret_cast<float*>(smem + OFF_RSCALE)[b] = 1.0f / sqrtf(sum / (float)(a.kb * BK) + a.eps);
+      epi_sync();
+    }
     int seg = 0;
     for (long long it = it0; it < it1; ++seg) {
       const long long tile = it / a.kb;
@@ -322,6 +364,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       // leaves the tail of the launch
       const bool pre_res = a.residual != nullptr && a.epilogue != DOE_LINEAR_SWIGLU &&
                            (whole || (a.cluster > 1 && block_owner(q, a) == (int)crank));
+      // the norm producer's gamma for the warp's 32 columns (64 bytes), copied
+      // into the warp's 64 bytes of the exchange area (unused without SwiGLU)
+      // while the MMAs run
+      const uint32_t gsm = sbase + OFF_XCHG + (uint32_t)q * 64;
+      if (a.normed_out != nullptr && lane < 4)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\ncp.async.commit_group;\n" ::"r"(gsm + lane * 16),
+                     "l"(a.gamma_out + (size_t)tile * BM + q * 32 + lane * 8)
+                     : "memory");
       float rres[NB];
       if (pre_res) {
         const size_t col = (size_t)tile * BM + row;
@@ -425,6 +475,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
       }
 
+      if (a.ssq_in != nullptr) {
+#pragma unroll
+        for (int j = 0; j < NB; ++j) v[j] *= rscale[j];
+      }
+
       if (a.epilogue == DOE_LINEAR_SWIGLU) {
         // rows 0-63 of the tile are gate rows, 64-127 the matching up rows;
         // the threads of rows r and r + 64 split the batch: the gate-row
@@ -455,27 +510,82 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         const int base = sg == 0 ? 0 : (sg == 1 ? a.seg_end[0] : a.seg_end[1]);
         const size_t width = (size_t)((sg == 0 ? a.seg_end[0] : (sg == 1 ? a.seg_end[1] : a.seg_end[2])) - base);
         void* dst = sg == 0 ? a.out[0] : (sg == 1 ? a.out[1] : a.out[2]);
-        const int col = col0 + row;
         if (a.residual) {
-          // all residual loads before any store: each (row, column) is read and
-          // written by this thread alone, so an in-place residual (out[0] ==
-          // residual) stays correct while the loads overlap
+          // each residual element is loaded by the thread of its column before
+          // the transpose below, and stored after it: an in-place residual
+          // (out[0] == residual) stays correct
           if (!pre_res) {
+            const int col = col0 + row;
 #pragma unroll
             for (int j = 0; j < NB; ++j) rres[j] = j < a.batch ? a.residual[(size_t)j * a.n_out + col] : 0.0f;
           }
 #pragma unroll
-          for (int j = 0; j < NB; ++j)
-            if (j < a.batch) static_cast<float*>(dst)[j * width + (col - base)] = v[j] + rres[j];
-        } else {
+          for (int j = 0; j < NB; ++j) v[j] += rres[j];
+        }
+        // Transpose the warp's 32 columns x 32 batch rows through its own 32
+        // lines of the receive area (unused outside cluster mode; in cluster
+        // mode this warp's lines of slot 0, already added up), so that lane j
+        // holds batch row j's 32 consecutive columns and writes them with
+        // 16-byte stores: a few dozen instructions on the launch's tail
+        // instead of 32 scalar stores per thread.  Column c of row j sits in
+        // 16-byte chunk (c / 4) ^ (j % 8) of line j (no bank conflicts).
+        float* tl = reinterpret_cast<float*>(smem + OFF_RECV + (uint32_t)q * 32 * 128);
+        __syncwarp();
 #pragma unroll
-          for (int j = 0; j < NB; ++j)
-            if (j < a.batch) store_elem(dst, a.dtype, j * width + (col - base), v[j]);
+        for (int j = 0; j < NB; ++j) tl[j * 32 + ((((lane >> 2) ^ (j & 7)) << 2) | (lane & 3))] = v[j];
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 t = *reinterpret_cast<const float4*>(tl + lane * 32 + ((c ^ (lane & 7)) << 2));
+          v[4 * c] = t.x;
+          v[4 * c + 1] = t.y;
+          v[4 * c + 2] = t.z;
+          v[4 * c + 3] = t.w;
+        }
+        if (a.normed_out != nullptr) asm volatile("cp.async.wait_all;\n" ::: "memory");
+        __syncwarp();  // the lines are free again for the next segment; gamma has landed
+        const int cw = col0 + q * 32;  // the warp's first column
+        if (lane < a.batch) {
+          if (a.dtype == DOE_DTYPE_F32) {
+            float4* o = reinterpret_cast<float4*>(static_cast<float*>(dst) + lane * width + (cw - base));
+#pragma unroll
+            for (int c = 0; c < 8; ++c) o[c] = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+          } else {
+            uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(dst) + lane * width + (cw - base));
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[c] = pack8(v + 8 * c, a.dtype == DOE_DTYPE_BF16);
+          }
+          if (a.normed_out != nullptr) {
+            // producer of a split RMSNorm (f32, one segment): bf16(y * gamma)
+            // and row `lane`'s sum of y^2 over the warp's 32 columns, in order
+            uint4* o = reinterpret_cast<uint4*>(a.normed_out + (size_t)lane * a.n_out + cw);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint4 g4 = *reinterpret_cast<const uint4*>(smem + OFF_XCHG + q * 64 + c * 16);
+              const uint32_t gw[4] = {g4.x, g4.y, g4.z, g4.w};
+              float y[8];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 g2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&gw[e]));
+                y[2 * e] = v[8 * c + 2 * e] * g2.x;
+                y[2 * e + 1] = v[8 * c + 2 * e + 1] * g2.y;
+              }
+              o[c] = pack8(y, true);
+            }
+            float ss = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+            a.ssq_out[(size_t)(cw >> 5) * NB + lane] = ss;
+          }
+        } else if (a.normed_out != nullptr) {
+          a.ssq_out[(size_t)(cw >> 5) * NB + lane] = 0.0f;  // rows past batch
         }
       }
     }
   }
 
+  // no copy of gamma may land after the CTA exits
+  if (warp >= 2 && a.normed_out != nullptr) asm volatile("cp.async.wait_all;\n" ::: "memory");
   // cluster rank 0 keeps its shared memory until every remote store has
   // landed, also when it stopped early (bounded)
   if (a.cluster > 1 && warp >= 2 && recv_bytes((int)crank, a) > 0) mbar_wait_bounded(bar(RECV_FULL), 0);
@@ -623,7 +733,7 @@ uint64_t linear_workspace(uint32_t n_out, uint32_t k) {
 }
 
 int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
-                  const doe_linear_out* o, const doe_launch* launch) {
+                  const doe_linear_out* o, const doe_linear_norm* norm, const doe_launch* launch) {
   const uint32_t tiles = n_out / lin::BM, kb = k / lin::BK;
   if (tiles > kMaxTiles) {
     set_op_error("doe_linear_bf16: n_out %u exceeds %llu rows", n_out, (unsigned long long)(kMaxTiles * lin::BM));
@@ -691,6 +801,11 @@ int launch_linear(const void* x, const void* w, uint32_t batch, uint32_t n_out, 
   a.dtype = (int)o->dtype;
   a.iters = iters;
   a.cluster = cluster;
+  a.gamma_out = norm ? static_cast<const __nv_bfloat16*>(norm->gamma) : nullptr;
+  a.normed_out = norm && norm->gamma ? static_cast<__nv_bfloat16*>(norm->normed_out) : nullptr;
+  a.ssq_out = norm && norm->gamma ? norm->ssq_out : nullptr;
+  a.ssq_in = norm ? norm->ssq_in : nullptr;
+  a.eps = norm ? norm->eps : 0.0f;
   CUtensorMap mw, mx;
   int rc = encode_rows_map(&mw, w, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, k, 1, n_out, 64, lin::BM,
                            "doe_linear_bf16");

@@ -538,9 +538,9 @@ int doe_tp_reduce_rmsnorm(const doe_tp_peers* peers, uint32_t slot, const void* 
   return launch_tp_reduce_rmsnorm(peers, slot, gamma, eps, h_out, xn_out, rows, cols, launch_or_default(launch));
 }
 
-int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
-                    const doe_linear_out* out, const doe_launch* launch) {
-  const char* who = "doe_linear_bf16";
+static int linear_checked(const char* who, const void* x, const void* w, uint32_t batch, uint32_t n_out,
+                          uint32_t k, const doe_linear_out* out, const doe_linear_norm* norm,
+                          const doe_launch* launch) {
   if (!x || !w || !out) return invalid("%s: x, w and out are required", who);
   if (batch == 0) return DOE_OK;
   if (batch > 32) {
@@ -551,6 +551,8 @@ int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out
   if (k == 0 || k % 64 != 0) return invalid("%s: k %u must be a positive multiple of 64", who, k);
   if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16)
     return invalid("%s: x and w must be 16-byte aligned", who);
+  for (int i = 0; i < 3; ++i)
+    if (reinterpret_cast<uintptr_t>(out->out[i]) % 16) return invalid("%s: outputs must be 16-byte aligned", who);
   if (out->dtype > DOE_DTYPE_F32) return invalid("%s: unknown dtype %u", who, out->dtype);
   if (out->epilogue == DOE_LINEAR_SWIGLU) {
     if (!out->out[0] || out->residual) return invalid("%s: SwiGLU writes out[0] only, without residual", who);
@@ -572,7 +574,29 @@ int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out
   } else {
     return invalid("%s: unknown epilogue %u", who, out->epilogue);
   }
-  return launch_linear(x, w, batch, n_out, k, out, launch_or_default(launch));
+  if (norm && norm->gamma) {
+    if (out->epilogue != DOE_LINEAR_STORE || out->dtype != DOE_DTYPE_F32 || out->width[1] != 0)
+      return invalid("%s: the norm's producer side needs a STORE product with f32 output and one segment", who);
+    if (!norm->normed_out || !norm->ssq_out) return invalid("%s: gamma needs normed_out and ssq_out", who);
+    if (reinterpret_cast<uintptr_t>(norm->gamma) % 16 || reinterpret_cast<uintptr_t>(norm->normed_out) % 16 ||
+        reinterpret_cast<uintptr_t>(norm->ssq_out) % 4)
+      return invalid("%s: gamma and normed_out must be 16-byte aligned, ssq_out 4-byte aligned", who);
+  }
+  if (norm && norm->ssq_in) {
+    if (reinterpret_cast<uintptr_t>(norm->ssq_in) % 4) return invalid("%s: ssq_in must be 4-byte aligned", who);
+    if (!(norm->eps >= 0.0f)) return invalid("%s: eps must be >= 0", who);
+  }
+  return launch_linear(x, w, batch, n_out, k, out, norm, launch_or_default(launch));
+}
+
+int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
+                    const doe_linear_out* out, const doe_launch* launch) {
+  return linear_checked("doe_linear_bf16", x, w, batch, n_out, k, out, nullptr, launch);
+}
+
+int doe_linear_bf16_norm(const void* x, const void* w, uint32_t batch, uint32_t n_out, uint32_t k,
+                         const doe_linear_out* out, const doe_linear_norm* norm, const doe_launch* launch) {
+  return linear_checked("doe_linear_bf16_norm", x, w, batch, n_out, k, out, norm, launch);
 }
 
 }  // extern "C"

@@ -139,14 +139,25 @@ class Decoder:
 
     def __init__(self, cfg: DecoderConfig, *, seed: int = 4, rank: int = 0, world: int = 1, group=None,
                  device=None, layers: list[dict] | None = None, caches: list[PagedKVCache] | None = None,
-                 reduce: str = "fused"):
+                 reduce: str = "fused", split_norm: bool | None = None):
         """reduce (world > 1): "fused" sums the partial products over peer
         buffers inside the following RMSNorm (doe_tp_reduce_rmsnorm); "nccl"
-        all-reduces them with NCCL and normalises separately."""
+        all-reduces them with NCCL and normalises separately.
+        split_norm (world 1 only; the default there): every RMSNorm after the
+        first is split over the products around it (doe_linear_bf16_norm):
+        o_proj / down_proj also write bf16(h * gamma) and per-32-column sums
+        of squares of h, and the next product scales its rows by
+        1 / sqrt(mean(h^2) + eps), so the step has no RMSNorm launch but the
+        first."""
         cfg.check(world)
         if reduce not in ("fused", "nccl"):
             raise ValueError("reduce must be 'fused' or 'nccl'")
         self.cfg, self.rank, self.world, self.group = cfg, rank, world, group
+        if split_norm is None:
+            split_norm = world == 1
+        if split_norm and world != 1:
+            raise ValueError("split_norm needs world 1: the norm follows the tensor-parallel reduction")
+        self.split_norm = split_norm
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.device = dev
         B, D = cfg.batch, cfg.head_dim
@@ -180,6 +191,7 @@ class Decoder:
         self.attn = torch.empty((B, self.qh * D), dtype=torch.bfloat16, device=dev)
         self.h = torch.empty((B, cfg.hidden), dtype=torch.float32, device=dev)
         self.act = torch.empty((B, self.f), dtype=torch.bfloat16, device=dev)
+        self.ssq = ops.ssq_buffer(cfg.hidden, dev)  # split_norm: the sums of squares of x or h
         n_max = max(cfg.hidden, (self.qh + 2 * self.kvh) * D, 2 * self.f)
         self.lin_ws = torch.zeros(int(ops.abi.lib().doe_linear_workspace_bytes(n_max, 64)), dtype=torch.uint8,
                                   device=dev)
@@ -203,14 +215,17 @@ class Decoder:
         cfg, B, D = self.cfg, self.cfg.batch, self.cfg.head_dim
         first = self.rank == 0
         fused = self.peers is not None
+        split = self.split_norm
         t = trace if trace is not None else (lambda *_: None)
         for li, (L, cache) in enumerate(zip(self.layers, self.caches)):
             t(li, "x", x)
-            if li == 0 or not fused:
+            if li == 0 or not (fused or split):
                 ops.rmsnorm(x, L["g1"], cfg.eps, out=self.xn, status=self.status)
-            # (fused: the previous layer's reduction already wrote x and its norm)
+            # (fused: the previous layer's reduction already wrote x and its norm;
+            # split: the previous down_proj wrote bf16(x * g1) and x's sums of squares)
             t(li, "xn", self.xn)
-            ops.linear(self.xn, L["wqkv"], [self.q, self.k, self.v], status=self.status, ws=self.lin_ws)
+            ops.linear(self.xn, L["wqkv"], [self.q, self.k, self.v], status=self.status, ws=self.lin_ws,
+                       norm_in=(self.ssq, cfg.eps) if split and li > 0 else None)
             t(li, "q", self.q), t(li, "k", self.k), t(li, "v", self.v)
             # seq_lens, the table and this layer's pool rows are written by no
             # kernel of the step but this call's own append (inputs_stable)
@@ -227,12 +242,14 @@ class Decoder:
                 self.peers.reduce_rmsnorm(0, self.h, L["g2"], cfg.eps, self.xn, status=self.status)
             else:
                 ops.linear(self.attn, L["wo"], [self.h], residual=x if first else None, status=self.status,
-                           ws=self.lin_ws)
+                           ws=self.lin_ws, norm_out=(L["g2"], self.xn, self.ssq) if split else None)
                 self._all_reduce(self.h)
-                ops.rmsnorm(self.h, L["g2"], cfg.eps, out=self.xn, status=self.status)
+                if not split:
+                    ops.rmsnorm(self.h, L["g2"], cfg.eps, out=self.xn, status=self.status)
             t(li, "h", self.h)
             t(li, "hn", self.xn)
-            ops.linear(self.xn, L["wgu"], [self.act], swiglu=True, status=self.status, ws=self.lin_ws)
+            ops.linear(self.xn, L["wgu"], [self.act], swiglu=True, status=self.status, ws=self.lin_ws,
+                       norm_in=(self.ssq, cfg.eps) if split else None)
             t(li, "act", self.act)
             if fused:
                 nxt = self.layers[li + 1] if li + 1 < len(self.layers) else None
@@ -241,8 +258,9 @@ class Decoder:
                 self.peers.reduce_rmsnorm(1, x, nxt["g1"] if nxt else None, cfg.eps,
                                           self.xn if nxt else None, status=self.status)
             else:
+                nxt = self.layers[li + 1] if li + 1 < len(self.layers) else None
                 ops.linear(self.act, L["wd"], [x], residual=self.h if first else None, status=self.status,
-                           ws=self.lin_ws)
+                           ws=self.lin_ws, norm_out=(nxt["g1"], self.xn, self.ssq) if split and nxt else None)
                 self._all_reduce(x)
             t(li, "out", x)
         return x
@@ -259,6 +277,8 @@ class Decoder:
 
     def launches_per_step(self) -> int:
         """Kernels of this library per step."""
+        if self.split_norm:
+            return 5 * self.cfg.layers + 1
         return 7 * self.cfg.layers + (1 if self.peers is not None else 0)
 
     def capture(self, x: torch.Tensor) -> None:

@@ -292,13 +292,25 @@ def rmsnorm(x, gamma, eps: float, out=None, status=None, stream=None):
     return out
 
 
-def linear(x, w, outs, *, swiglu: bool = False, residual=None, status=None, stream=None, ws=None):
+def ssq_buffer(cols: int, device=None) -> torch.Tensor:
+    """The [cols / 32, 32] f32 sums of squares a norm-producing linear writes."""
+    return torch.zeros((cols // 32, 32), dtype=torch.float32, device=device)
+
+
+def linear(x, w, outs, *, swiglu: bool = False, residual=None, status=None, stream=None, ws=None,
+           norm_out=None, norm_in=None):
     """doe_linear_bf16: x [batch, k] bf16 times w [n_out, k] bf16 transposed.
 
     `outs` is a list of 1-3 contiguous tensors of one dtype (bf16, f16 or f32),
     each [batch, width]; with swiglu=True a single [batch, n_out/2] output of
     silu(gate) * up (w packed in 128-row blocks: 64 gate rows, 64 up rows).
-    `residual` ([batch, n_out] f32, f32 output) is added to the product."""
+    `residual` ([batch, n_out] f32, f32 output) is added to the product.
+
+    The RMSNorm between two products (doe_linear_bf16_norm): norm_out =
+    (gamma [n_out] bf16, normed [batch, n_out] bf16, ssq (ssq_buffer(n_out)))
+    makes this product (f32, one segment) also write bf16(y * gamma) and its
+    per-32-column sums of squares; norm_in = (ssq, eps), with x such a normed
+    output, scales each row of this product by 1 / sqrt(mean(h^2) + eps)."""
     _need(x, torch.bfloat16, "x")
     _need(w, torch.bfloat16, "w")
     batch, k = x.shape
@@ -321,6 +333,25 @@ def linear(x, w, outs, *, swiglu: bool = False, residual=None, status=None, stre
     ws = linear_workspace(n_out, k, x.device) if ws is None else ws
     s = stream if stream is not None else torch.cuda.current_stream(x.device)
     l = abi.Launch(s.cuda_stream, ws.data_ptr(), ws.numel(), status.data_ptr() if status is not None else None)
-    abi.check("doe_linear_bf16", abi.lib().doe_linear_bf16(
-        x.data_ptr(), w.data_ptr(), batch, n_out, k, C.byref(lo), C.byref(l)))
+    if norm_out is None and norm_in is None:
+        abi.check("doe_linear_bf16", abi.lib().doe_linear_bf16(
+            x.data_ptr(), w.data_ptr(), batch, n_out, k, C.byref(lo), C.byref(l)))
+        return outs
+    ln = abi.LinearNorm()
+    if norm_out is not None:
+        gamma, normed, ssq = norm_out
+        _need(gamma, torch.bfloat16, "norm_out gamma")
+        _need(normed, torch.bfloat16, "norm_out normed")
+        _need(ssq, torch.float32, "norm_out ssq")
+        if gamma.numel() != n_out or normed.shape != (batch, n_out) or ssq.numel() != n_out:
+            raise ValueError("norm_out: gamma [n_out], normed [batch, n_out], ssq [n_out / 32, 32]")
+        ln.gamma, ln.normed_out, ln.ssq_out = gamma.data_ptr(), normed.data_ptr(), ssq.data_ptr()
+    if norm_in is not None:
+        ssq, eps = norm_in
+        _need(ssq, torch.float32, "norm_in ssq")
+        if ssq.numel() != k:
+            raise ValueError("norm_in: ssq [k / 32, 32]")
+        ln.ssq_in, ln.eps = ssq.data_ptr(), float(eps)
+    abi.check("doe_linear_bf16_norm", abi.lib().doe_linear_bf16_norm(
+        x.data_ptr(), w.data_ptr(), batch, n_out, k, C.byref(lo), C.byref(ln), C.byref(l)))
     return outs

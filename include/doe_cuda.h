@@ -434,7 +434,8 @@ int doe_rmsnorm_bf16(const float* x, const void* gamma, float eps, void* out,
  * with f32 accumulation on the tensor cores; the weights stream from HBM
  * once.  x [batch, k] bf16 with batch <= 32; w [n_out, k] bf16 (output
  * features as rows: an ONNX MatMul initializer [k, n] is transposed once at
- * load); n_out a multiple of 128, k a multiple of 64; 16-byte aligned.
+ * load); n_out a multiple of 128, k a multiple of 64; x, w and the outputs
+ * 16-byte aligned.
  * Epilogues (doe_linear_out.epilogue):
  *   DOE_LINEAR_STORE   y split into up to 3 consecutive column segments of
  *                      widths width[i] (multiples of 128, summing to n_out),
@@ -469,6 +470,33 @@ typedef struct doe_linear_out {
 uint64_t doe_linear_workspace_bytes(uint32_t n_out, uint32_t k);
 int doe_linear_bf16(const void* x, const void* w, uint32_t batch, uint32_t n_out,
                     uint32_t k, const doe_linear_out* out, const doe_launch* launch);
+
+/* doe_linear_bf16 with an RMSNorm split over the two products around it, in
+ * place of the SimplifiedLayerNormalization between them (doe_rmsnorm_bf16)
+ * when no tensor-parallel reduction sits in between.  It has no counterpart
+ * of its own in the reference, whose graph runs the norm as its own node.
+ *   producer (gamma set): a DOE_LINEAR_STORE product with dtype f32 and one
+ *     segment (the o_proj / down_proj writing the residual stream h) also
+ *     writes normed_out [batch, n_out] bf16 = bf16(h * gamma) and ssq_out
+ *     [n_out / 32][32] f32, the sum of h^2 over each 32 columns for each
+ *     batch row (0 for rows past batch);
+ *   consumer (ssq_in set): a product whose x is such a normed_out and ssq_in
+ *     its ssq_out (k = the producer's n_out) multiplies row b of its result
+ *     by 1 / sqrt(sum_i ssq_in[i][b] / k + eps) before its epilogue, so y =
+ *     W (rmsnorm(h) * gamma) with the norm's scale applied after the product
+ *     instead of before the bf16 rounding of x.  The blocks are summed in a
+ *     fixed order: results do not depend on timing.
+ * Either side may be absent; norm null is doe_linear_bf16.                 */
+typedef struct doe_linear_norm {
+  const void* gamma;      /* producer: bf16 [n_out], or null; 16-byte aligned */
+  void* normed_out;       /* producer: bf16 [batch, n_out]; 16-byte aligned */
+  float* ssq_out;         /* producer: f32 [n_out / 32][32]                 */
+  const float* ssq_in;    /* consumer: f32 [k / 32][32], or null            */
+  float eps;              /* consumer: >= 0                                 */
+} doe_linear_norm;
+int doe_linear_bf16_norm(const void* x, const void* w, uint32_t batch, uint32_t n_out,
+                         uint32_t k, const doe_linear_out* out, const doe_linear_norm* norm,
+                         const doe_launch* launch);
 
 /* Tensor-parallel reduction fused into the RMSNorm that consumes it (the
  * AllReduce after o_proj / down_proj, one process per GPU of one node).

@@ -45,9 +45,10 @@ def _oracle_step(dec, x0, layers, caches):
     x = x0.copy()
     table = dec.freq_cis.cpu().numpy()
     seq_lens = dec.seq_lens.cpu().numpy()
-    for L, c in zip(layers, caches):
+    for li, (L, c) in enumerate(zip(layers, caches)):
         x = odec.layer_partials(x, L, c, qh=dec.qh, kvh=dec.kvh, head_dim=cfg.head_dim, eps=cfg.eps,
-                                scale=dec.scale, freq_cis=table, seq_lens=seq_lens, add_residual=True)
+                                scale=dec.scale, freq_cis=table, seq_lens=seq_lens, add_residual=True,
+                                split_first=dec.split_norm and li > 0, split_second=dec.split_norm)
     return x
 
 
@@ -55,10 +56,11 @@ def _x0(cfg, seed=12):
     return np.random.default_rng(seed).standard_normal((cfg.batch, cfg.hidden), dtype=np.float32)
 
 
+@pytest.mark.parametrize("split", [True, False])
 @pytest.mark.parametrize("cfg", [SMALL, decoder.DecoderConfig(hidden=1024, heads=8, kv_heads=1, ffn=2048,
                                                               layers=1, batch=32, ctx=333)])
-def test_decoder_step_matches_oracle(cfg):
-    dec = decoder.Decoder(cfg, seed=4)
+def test_decoder_step_matches_oracle(cfg, split):
+    dec = decoder.Decoder(cfg, seed=4, split_norm=split)
     layers, caches = _host_state(dec)
     x0 = _x0(cfg)
     x = torch.from_numpy(x0).cuda()
@@ -90,11 +92,15 @@ def _f32_close(got, ref, what, tol=1e-4):
     assert float(err.max()) <= tol, f"{what}: max rel err {float(err.max()):.3g}"
 
 
+@pytest.mark.parametrize("split", [True, False])
 @pytest.mark.parametrize("cfg", [SMALL, decoder.DecoderConfig(layers=2, ctx=64)])
-def test_decoder_stages_match_oracle(cfg):
+def test_decoder_stages_match_oracle(cfg, split):
+    """split: every RMSNorm after the first is split over the products around
+    it, so the traced "xn" / "hn" are bf16(x * gamma) (bit-exact) and q / k /
+    v and gate / up carry the row scale 1 / sqrt(mean(x^2) + eps)."""
     import oracle
 
-    dec = decoder.Decoder(cfg, seed=6)
+    dec = decoder.Decoder(cfg, seed=6, split_norm=split)
     layers, caches = _host_state(dec)
     seen: dict = {}
 
@@ -111,8 +117,12 @@ def test_decoder_stages_match_oracle(cfg):
     pos = seq_lens.astype(np.int64) - 1
     for li, (L, c) in enumerate(zip(layers, caches)):
         g = lambda n: seen[(li, n)]  # noqa: E731
-        _ulp_close(g("xn"), odec.rmsnorm(g("x"), L["g1"], cfg.eps), BF16_ULP, f"layer {li} rmsnorm")
-        qkv = odec.matmul(g("xn"), L["wqkv"])
+        if split and li > 0:
+            assert np.array_equal(g("xn"), odec.norm_numerator(g("x"), L["g1"])), f"layer {li} bf16(x * g1)"
+            qkv = odec.matmul(g("xn"), L["wqkv"]) * odec.rms_scale(g("x"), cfg.eps)
+        else:
+            _ulp_close(g("xn"), odec.rmsnorm(g("x"), L["g1"], cfg.eps), BF16_ULP, f"layer {li} rmsnorm")
+            qkv = odec.matmul(g("xn"), L["wqkv"])
         for name, lo, hi in (("q", 0, qh * D), ("k", qh * D, (qh + kvh) * D), ("v", (qh + kvh) * D, None)):
             _ulp_close(g(name), qkv[:, lo:hi].astype(np.float16), F16_ULP, f"layer {li} {name}", extra=ACC)
         q16 = g("q").astype(np.float16).reshape(B, qh, D)
@@ -131,9 +141,14 @@ def test_decoder_stages_match_oracle(cfg):
         _ulp_close(g("attn"), odec.bf16_round(att.reshape(B, -1).astype(np.float32)), BF16_ULP,
                    f"layer {li} attention", extra=2e-3)
         _f32_close(g("h"), odec.matmul(g("attn"), L["wo"]).astype(np.float64) + g("x"), f"layer {li} o_proj")
-        _ulp_close(g("hn"), odec.rmsnorm(g("h"), L["g2"], cfg.eps), BF16_ULP, f"layer {li} rmsnorm 2")
         wg, wu = odec.unpack_gate_up(L["wgu"])
-        gg, uu = odec.matmul(g("hn"), wg), odec.matmul(g("hn"), wu)
+        if split:
+            assert np.array_equal(g("hn"), odec.norm_numerator(g("h"), L["g2"])), f"layer {li} bf16(h * g2)"
+            r = odec.rms_scale(g("h"), cfg.eps)
+            gg, uu = odec.matmul(g("hn"), wg) * r, odec.matmul(g("hn"), wu) * r
+        else:
+            _ulp_close(g("hn"), odec.rmsnorm(g("h"), L["g2"], cfg.eps), BF16_ULP, f"layer {li} rmsnorm 2")
+            gg, uu = odec.matmul(g("hn"), wg), odec.matmul(g("hn"), wu)
         _ulp_close(g("act"), (gg / (np.float32(1.0) + np.exp(-gg)) * uu).astype(np.float32), BF16_ULP,
                    f"layer {li} swiglu", extra=ACC)
         _f32_close(g("out"), odec.matmul(g("act"), L["wd"]).astype(np.float64) + g("h"), f"layer {li} down_proj")

@@ -137,3 +137,75 @@ def test_rmsnorm(rows, cols):
     xd = x.double()
     ref = xd / torch.sqrt((xd * xd).mean(dim=1, keepdim=True) + 1e-5) * gamma.double()
     _close(out, ref, torch.bfloat16)
+
+
+# the split RMSNorm (doe_linear_bf16_norm), producer side in each work split:
+# cluster split-K (4096 x 4096: 32 tiles), stream-K fix-up (12288 x 1024: 96
+# tiles over 148 CTAs) and whole tiles (18944 x 128: one tile per CTA)
+@pytest.mark.parametrize("batch,n_out,k", [(32, 4096, 4096), (32, 12288, 1024), (7, 18944, 128), (3, 256, 512)])
+def test_linear_norm_producer(batch, n_out, k):
+    g = np.random.default_rng(n_out + k + batch)
+    x, w = _bf16(g, (batch, k), 1.0), _bf16(g, (n_out, k), 0.02)
+    res = torch.from_numpy(g.standard_normal((batch, n_out), dtype=np.float32))
+    gamma = _bf16(g, (n_out,), 1.0)
+    h = torch.full((batch, n_out), float("nan"), dtype=torch.float32, device="cuda")
+    normed = torch.full((batch, n_out), float("nan"), dtype=torch.bfloat16, device="cuda")
+    ssq = torch.full((n_out // 32, 32), float("nan"), dtype=torch.float32, device="cuda")
+    status = ops.status_word()
+    ops.linear(x.cuda(), w.cuda(), [h], residual=res.cuda(), norm_out=(gamma.cuda(), normed, ssq), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    _close(h, res.double() + _ref(x, w), torch.float32)
+    hc = h.cpu()
+    # bf16(h * gamma) of the h the kernel wrote, bit for bit
+    assert torch.equal(normed.cpu(), (hc * gamma.float()).to(torch.bfloat16))
+    # per 32-column block and batch row: sum of h^2 (f32 adds in the kernel's order)
+    ref_ssq = (hc.double() ** 2).view(batch, n_out // 32, 32).sum(dim=2).T
+    got = ssq.cpu().double()
+    assert torch.allclose(got[:, :batch], ref_ssq, rtol=1e-5, atol=1e-6)
+    assert bool((got[:, batch:] == 0).all()), "rows past batch must hold 0"
+
+
+@pytest.mark.parametrize("swiglu", [False, True])
+@pytest.mark.parametrize("batch,n_out,k", [(32, 6144, 4096), (32, 28672, 4096), (5, 1024, 512)])
+def test_linear_norm_consumer(batch, n_out, k, swiglu):
+    """y = rms_scale(h) * (bf16(h * gamma) @ w^T), the row scale from the
+    producer's sums of squares (computed here on the host, in block order)."""
+    g = np.random.default_rng(n_out + k + int(swiglu))
+    h = torch.from_numpy(g.standard_normal((batch, k), dtype=np.float32) * 3)
+    gamma = _bf16(g, (k,), 1.0)
+    xn = (h * gamma.float()).to(torch.bfloat16)
+    ssq = torch.zeros((k // 32, 32), dtype=torch.float32)
+    ssq[:, :batch] = (h.double() ** 2).view(batch, k // 32, 32).sum(dim=2).T.float()
+    eps = 1e-5
+    r = 1.0 / torch.sqrt((h.double() ** 2).mean(dim=1, keepdim=True) + eps)
+    w = _bf16(g, (n_out, k), 0.02)
+    status = ops.status_word()
+    if not swiglu:
+        out = torch.full((batch, n_out), float("nan"), dtype=torch.bfloat16, device="cuda")
+        ops.linear(xn.cuda(), w.cuda(), [out], norm_in=(ssq.cuda(), eps), status=status)
+        torch.cuda.synchronize()
+        _close(out, _ref(xn, w) * r, torch.bfloat16)
+    else:
+        out = torch.full((batch, n_out // 2), float("nan"), dtype=torch.bfloat16, device="cuda")
+        ops.linear(xn.cuda(), w.cuda(), [out], swiglu=True, norm_in=(ssq.cuda(), eps), status=status)
+        torch.cuda.synchronize()
+        blocks = w.view(-1, 128, k)
+        gate, up = blocks[:, :64].reshape(-1, k), blocks[:, 64:].reshape(-1, k)
+        gr, ur = _ref(xn, gate) * r, _ref(xn, up) * r
+        _close(out, gr / (1.0 + torch.exp(-gr)) * ur, torch.bfloat16)
+    assert int(status.item()) == 0
+
+
+def test_linear_norm_rejects_producer_without_f32_single_segment():
+    x = torch.zeros((4, 64), dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros((256, 64), dtype=torch.bfloat16, device="cuda")
+    gamma = torch.ones(256, dtype=torch.bfloat16, device="cuda")
+    normed = torch.zeros((4, 256), dtype=torch.bfloat16, device="cuda")
+    ssq = ops.ssq_buffer(256, "cuda")
+    with pytest.raises(ops.abi.DoeError):
+        ops.linear(x, w, [torch.zeros((4, 256), dtype=torch.bfloat16, device="cuda")],
+                   norm_out=(gamma, normed, ssq))
+    with pytest.raises(ops.abi.DoeError):
+        ops.linear(x, w, [torch.zeros((4, 128), dtype=torch.float32, device="cuda"),
+                          torch.zeros((4, 128), dtype=torch.float32, device="cuda")], norm_out=(gamma, normed, ssq))
