@@ -204,15 +204,6 @@ __device__ __forceinline__ uint4 pack8(const float* y, bool bf16) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__device__ __forceinline__ void store_elem(void* base, int dtype, size_t idx, float y) {
-  if (dtype == DOE_DTYPE_BF16)
-    static_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(y);
-  else if (dtype == DOE_DTYPE_F16)
-    static_cast<__half*>(base)[idx] = __float2half_rn(y);
-  else
-    static_cast<float*>(base)[idx] = y;
-}
-
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     linear_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                   const Args a) {
@@ -492,17 +483,42 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll
         for (int jj = 0; jj < NB / 2; ++jj) xchg[jj * 128 + row] = gate ? v[NB / 2 + jj] : v[jj];
         epi_sync();
-        const size_t width = (size_t)a.n_out / 2, col = (size_t)tile * 64 + (row & 63);
+        const size_t width = (size_t)a.n_out / 2;
         const int mate = row ^ 64;
+        // the (feature, batch row) results go through shared memory (the
+        // receive area, free once every epilogue warp has passed the barrier
+        // above; rows padded to 68 floats) so that warp q stores features
+        // [16 q, 16 q + 16) of batch row `lane` with 16-byte stores
+        float* ty = reinterpret_cast<float*>(smem + OFF_RECV);
 #pragma unroll
         for (int jj = 0; jj < NB / 2; ++jj) {
-          const int j = j0 + jj;
-          if (j < a.batch) {
-            const float other = xchg[jj * 128 + mate], mine = gate ? v[jj] : v[NB / 2 + jj];
-            const float g = gate ? mine : other, u = gate ? other : mine;
-            store_elem(a.out[0], a.dtype, j * width + col, __fdividef(g, 1.0f + __expf(-g)) * u);
+          const float other = xchg[jj * 128 + mate], mine = gate ? v[jj] : v[NB / 2 + jj];
+          const float g = gate ? mine : other, u = gate ? other : mine;
+          ty[(j0 + jj) * 68 + (row & 63)] = __fdividef(g, 1.0f + __expf(-g)) * u;
+        }
+        epi_sync();
+        if (lane < a.batch) {
+          float y[16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float4 t = *reinterpret_cast<const float4*>(ty + lane * 68 + q * 16 + 4 * c);
+            y[4 * c] = t.x;
+            y[4 * c + 1] = t.y;
+            y[4 * c + 2] = t.z;
+            y[4 * c + 3] = t.w;
+          }
+          const size_t off = lane * width + (size_t)tile * 64 + q * 16;
+          if (a.dtype == DOE_DTYPE_F32) {
+            float4* o = reinterpret_cast<float4*>(static_cast<float*>(a.out[0]) + off);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) o[c] = make_float4(y[4 * c], y[4 * c + 1], y[4 * c + 2], y[4 * c + 3]);
+          } else {
+            uint4* o = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out[0]) + off);
+            o[0] = pack8(y, a.dtype == DOE_DTYPE_BF16);
+            o[1] = pack8(y + 8, a.dtype == DOE_DTYPE_BF16);
           }
         }
+        // the next writes to ty come after the next segment's first barrier
         // the next writes to xchg come after the next segment's epi_all
       } else {
         const int col0 = (int)tile * BM;
