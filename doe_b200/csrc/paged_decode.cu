@@ -65,7 +65,7 @@ __device__ __forceinline__ int page_of(const PagedDecodeArgs& a, int pos) {
 
 constexpr int kD = 128;
 constexpr int kWarps = 4;
-constexpr int kPageRegs = 4;  // page ids held per lane: 128 tiles per warp, 512 per split
+constexpr int kPageRegs = 4;  // page ids per lane at the prologue: 128 tiles per warp, 512 per split
 
 __device__ __forceinline__ uint4 ldcg4(const uint8_t* p) {
   uint4 v;
@@ -231,6 +231,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   __shared__ float sm_m[kWarps][8];
   __shared__ float sm_l[kWarps][8];
   __shared__ int sm_last;
+  __shared__ int sm_pg[kWarps][32 * kPageRegs];
   __shared__ __align__(8) uint64_t ring_bar[kWarps][P];
 
   if (lane == 0) {
@@ -243,17 +244,14 @@ __global__ void __launch_bounds__(kWarps * 32)
   // ---- this warp's tiles: tile_begin + warp + 4k, k < nt; page ids up front
   const int span = tile_end - tile_begin - warp;
   const int nt = span > 0 ? (span + kWarps - 1) / kWarps : 0;
-  // page ids of the warp's tiles: lane l holds tile l + 32 i in pg[i]
-  auto load_page = [&](int i) {
-    if (lane + 32 * i >= nt) return -1;
-    return table[page_of(a, (tile_origin + tile_begin + warp + kWarps * (lane + 32 * i)) << 4)];
-  };
-  static_assert(kPageRegs == 4, "pg0..pg3");
-  const int pg0 = load_page(0), pg1 = load_page(1), pg2 = load_page(2), pg3 = load_page(3);
-  auto page_of_tile = [pg0, pg1, pg2, pg3](int k) {  // k warp-uniform
-    const int i = k >> 5;
-    return __shfl_sync(0xffffffffu, i == 0 ? pg0 : (i == 1 ? pg1 : (i == 2 ? pg2 : pg3)), k & 31);
-  };
+  // page ids of the warp's tiles, one shared-memory word per tile (one load
+  // per lookup, as cheap as a shuffle, for any number of tiles up to the cap)
+#pragma unroll
+  for (int i = 0; i < kPageRegs; ++i)
+    if (lane + 32 * i < nt)
+      sm_pg[warp][lane + 32 * i] = table[page_of(a, (tile_origin + tile_begin + warp + kWarps * (lane + 32 * i)) << 4)];
+  __syncwarp();
+  auto page_of_tile = [&](int k) { return sm_pg[warp][k]; };  // k < nt
 
   const int vt[4] = {2 * c, 2 * c + 1, 2 * c + 8, 2 * c + 9};
   const uint32_t wbase = smem_addr(dsmem) + warp * R::kWarpBytes;
