@@ -26,6 +26,11 @@
 // shared memory; rank 0 sums them in rank order and runs the epilogue.
 // Epilogues: store into up to three column segments (bf16, f16 or f32),
 // SwiGLU over interleaved 64-row gate / up blocks, or f32 plus a residual.
+// Results leave through shared memory, transposed so that each lane writes
+// one batch row's columns with 16-byte stores.  A split RMSNorm
+// (doe_linear_norm): the f32 producer also writes bf16(y * gamma) and each
+// row's sum of squares per 32 columns; a consumer scales its rows by
+// 1 / sqrt(mean + eps) from those sums before its epilogue.
 // Launched with programmatic dependent launch: the first ring of weight
 // boxes is issued before griddepcontrol.wait, since no kernel of a step
 // writes the weights.
