@@ -776,24 +776,27 @@ int launch_paged_decode(const doe_paged_kv* kv, uint32_t num_seqs, uint32_t num_
     // f16, 128 for int8 measured best on config 3 / 4, whose work fills
     // several waves of 3 CTAs per SM on 148 SMs at that length).  Less work
     // than that (a decode batch of uniform contexts, or one tensor-parallel
-    // rank's few KV heads) runs best in ONE wave: a CTA that starts when an
-    // earlier one ends spends microseconds on its lengths, page ids and first
-    // copies while the SM's share of HBM idles.  So: as few splits as keep
-    // about two CTAs per SM busy, but no more than fit one wave of 3 CTAs per
-    // SM (config 5: 256 (sequence, kv head) rows, one split each, 0.778 ->
-    // 0.753 ms per step against three splits in 1.7 waves), each split at most
-    // kWarps * 32 * kPageRegs tiles and all of one length.
+    // rank's few KV heads) gets as few splits as still keep about two CTAs
+    // per SM busy, each at most 128 tiles and all of one length.  Where the
+    // (sequence, kv head) rows alone put at least one CTA on every SM and fit
+    // one wave of 3 per SM, and a row fits one split, each row is one split:
+    // a second wave would start its CTAs while the first one's SMs idle on
+    // their prologues (config 5: 256 rows, 0.778 -> 0.753 ms per step against
+    // three splits in 1.7 waves).  Ragged lengths keep the short splits,
+    // which balance as CTAs finish (config 4 split over 4 ranks: 16 splits of
+    // 128 tiles, not 5 of 410).
     const uint64_t seq_rows = (uint64_t)num_seqs * Hkv;
     const uint64_t want = ((uint64_t)max_tiles * seq_rows + 1775) / 1776;
     const uint32_t cap = kv->kv_dtype == DOE_KV_INT8 ? 128u : 64u;
+    const uint64_t sms = (uint64_t)num_sms();
     if (want >= cap) {
       split_tiles = cap;
+    } else if (seq_rows >= sms && seq_rows <= 3 * sms && max_tiles <= (uint64_t)kWarps * 32 * kPageRegs) {
+      split_tiles = max_tiles < 4 ? 4u : max_tiles;
     } else {
-      const uint64_t most = (uint64_t)kWarps * 32 * kPageRegs;
+      uint64_t s = (max_tiles + 127) / 128;
       const uint64_t fill = (280 + seq_rows - 1) / seq_rows;
-      const uint64_t wave = 444 / seq_rows;
-      uint64_t s = fill < wave ? fill : wave;
-      if (s < (max_tiles + most - 1) / most) s = (max_tiles + most - 1) / most;
+      if (s < fill) s = fill;
       if (s < 1) s = 1;
       const uint64_t t = (max_tiles + s - 1) / s;
       split_tiles = (uint32_t)(t < 4 ? 4 : t);
