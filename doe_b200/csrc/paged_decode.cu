@@ -25,6 +25,10 @@
 // once per row instead of per element: S -= 1152 * sum(q), O -= 1152 *
 // sum(f16 P).  The K scale multiplies S and the V scale folds into P.  Scores
 // run in the log2 domain (the SFU's ex2 per key; exp2f for the merges).
+// Prologue: each warp's page ids go to shared memory and its first copy is
+// issued before the query work (before griddepcontrol.wait when the caller
+// sets DOE_DECODE_INPUTS_STABLE); the warp whose walk holds the new row's
+// tile appends the row, so no other warp waits for it.
 #include "tma.cuh"
 
 namespace doe {
